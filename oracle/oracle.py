@@ -61,6 +61,7 @@ def _declare(L):
         "orc_quantize_q8_0_gguf": (None, [P, I64, P]),
         "orc_q8_0_deinterleave": (None, [P, I64, P, P]),
         "orc_dequant_rows": (None, [C.c_int, P, P, I64, I64, I64, P]),
+        "orc_requant_q8_0": (None, [C.c_int, P, I64, I64, P, P]),
         "orc_quantize_q8k": (None, [P, I64, P, P, P]),
         "orc_quantize_q8_0": (None, [P, I64, P, P]),
         "orc_q4k_dot": (C.c_float, [P, P, C.c_float, P]),
@@ -82,6 +83,7 @@ def _declare(L):
         "orc_session_create": (P, [P, C.c_int]),
         "orc_session_destroy": (None, [P]),
         "orc_session_reset": (None, [P]),
+        "orc_session_set_kv_fp16": (None, [P, C.c_int]),
         "orc_session_position": (C.c_int, [P]),
         "orc_session_decode": (C.c_int, [P, C.c_int, P]),
         "orc_session_decode_layers": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P]),
@@ -158,6 +160,14 @@ def dequant_rows(type_: int, data: np.ndarray, rows: int, k: int, scales=None, r
     out = np.empty((rows, k), np.float32)
     lib().orc_dequant_rows(type_, _p(data), _p(scales), row0, rows, k, _p(out))
     return out
+
+
+def requant_q8_0(type_: int, data: np.ndarray, rows: int, k: int):
+    """attn_output residency: decode then per-32 Q8_0 with fp32 scales."""
+    q = np.empty(rows * k, np.int8)
+    s = np.empty(rows * k // 32, np.float32)
+    lib().orc_requant_q8_0(type_, _p(data), rows, k, _p(q), _p(s))
+    return q, s
 
 
 # ----------------------------------------------------------- quantizers
@@ -377,6 +387,10 @@ class OracleSession:
 
     def reset(self):
         lib().orc_session_reset(self._s)
+
+    def set_kv_fp16(self, on: bool = True):
+        """Round cached K/V to fp16 as the GPU cache does (test switch)."""
+        lib().orc_session_set_kv_fp16(self._s, int(on))
 
     @property
     def position(self) -> int:

@@ -285,6 +285,25 @@ void orc_dequant_rows(int type, const void *data, const float *q8s,
     }
 }
 
+/* Loading/GgufLlamaLoader.cs:977-995 + :1298-1336 (LoadOutputHeads ->
+ * SplitOutput -> Q8Weight.QuantizeRows, Runtime/Q8Weight.cs:115-158): a
+ * non-Q8_0 attn_output is decoded to fp32 and re-quantized to Q8_0 with fp32
+ * scales.  Head slices of a row are whole 32-blocks, so quantizing each full
+ * row in 32-blocks gives the same bytes as the per-head gather. */
+void orc_quantize_q8_0(const float *x, int64_t k, int8_t *q, float *scales);
+void orc_requant_q8_0(int type, const void *data, int64_t rows, int64_t k, int8_t *q, float *scales) {
+#pragma omp parallel
+    {
+        float *row = (float *)malloc((size_t)k * sizeof(float));
+#pragma omp for schedule(static)
+        for (int64_t r = 0; r < rows; r++) {
+            orc_dequant_rows(type, data, NULL, r, 1, k, row);
+            orc_quantize_q8_0(row, k, q + r * k, scales + r * (k / 32));
+        }
+        free(row);
+    }
+}
+
 /* ------------------------------------------------------------------ */
 /* Activation quantizers                                               */
 /* ------------------------------------------------------------------ */
@@ -706,6 +725,7 @@ void orc_fill_normal(float *dst, int64_t n, uint64_t seed, float mean, float std
 struct orc_session {
     const orc_model *m;
     int max_ctx, pos;
+    int kv_fp16;                  /* test switch: round cached K/V to fp16 like the GPU cache */
     float *kcache, *vcache;       /* F32 [layer][kvh][max_ctx][hd] (KeyValueCache.cs:593-602) */
     float *rope_cos, *rope_sin;   /* [max_ctx][hd/2] */
     float *hidden, *after, *ln, *attn_out, *ffo, *fin;
@@ -756,6 +776,7 @@ void orc_session_destroy(orc_session *s) {
     free(s);
 }
 void orc_session_reset(orc_session *s) { s->pos = 0; }
+void orc_session_set_kv_fp16(orc_session *s, int on) { s->kv_fp16 = on; }
 int orc_session_position(const orc_session *s) { return s->pos; }
 
 static int is_kq(int t) { return t == ORC_Q4_K || t == ORC_Q6_K; }
@@ -839,6 +860,11 @@ static void attention_block(orc_session *s, const orc_layer *L, int layer, int p
                      tv ? hq : NULL, hs, hb, s->q8, s->q8s, s->q8b);
         orc_rope_apply(kb, hd, cp, sp, m->rope_split_half);
         int64_t off = (((int64_t)layer * KVH + g) * s->max_ctx + pos) * hd;
+        if (s->kv_fp16)
+            for (int i = 0; i < hd; i++) {
+                kb[i] = (float)(_Float16)kb[i];
+                vb[i] = (float)(_Float16)vb[i];
+            }
         memcpy(s->kcache + off, kb, (size_t)hd * sizeof(float));
         memcpy(s->vcache + off, vb, (size_t)hd * sizeof(float));
     }

@@ -49,6 +49,7 @@ void orc_encode_q6k_block(const float *src256, uint8_t *block210);
 void orc_quantize_q6k(const float *w, int64_t rows, int64_t k, uint8_t *out);
 void orc_quantize_q8_0_gguf(const float *w, int64_t n, uint8_t *out);
 void orc_q8_0_deinterleave(const uint8_t *gguf, int64_t n, int8_t *quants, float *scales);
+void orc_requant_q8_0(int type, const void *data, int64_t rows, int64_t k, int8_t *q, float *scales);
 void orc_dequant_rows(int type, const void *data, const float *q8_scales,
                       int64_t row0, int64_t nrows, int64_t k, float *dst);
 
@@ -118,6 +119,9 @@ typedef struct orc_session orc_session;
 orc_session *orc_session_create(const orc_model *m, int max_ctx);
 void orc_session_destroy(orc_session *s);
 void orc_session_reset(orc_session *s);
+/* Test switch: store K/V rounded to fp16 (the GPU's cache format); the
+ * reference's cache is F32 (Runtime/KeyValueCache.cs:593-602). */
+void orc_session_set_kv_fp16(orc_session *s, int on);
 int  orc_session_position(const orc_session *s);
 /* One token through the stack; writes logits[vocab] when logits != NULL. */
 int  orc_session_decode(orc_session *s, int token, float *logits);

@@ -1,0 +1,156 @@
+// ovf_common.cuh — shared device helpers for the sm_100a kernels:
+// status plumbing, mbarrier + bulk-copy (TMA 1-D) wrappers with bounded
+// waits, and IEEE-exact float helpers (no FMA contraction) for the parts of
+// the path that must reproduce the reference's fp32 arithmetic bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+#include "../../include/ovf.h"
+
+namespace ovf {
+
+// ------------------------------------------------------------ host status
+void set_error(const char *fmt, ...);
+ovf_status cuda_status(cudaError_t e, const char *what);
+
+#define OVF_CHECK_ARG(cond, ...)          \
+    do {                                  \
+        if (!(cond)) {                    \
+            ::ovf::set_error(__VA_ARGS__); \
+            return OVF_EINVAL;            \
+        }                                 \
+    } while (0)
+
+#define OVF_CUDA_TRY(expr)                                              \
+    do {                                                                \
+        cudaError_t _e = (expr);                                        \
+        if (_e != cudaSuccess) return ::ovf::cuda_status(_e, #expr);    \
+    } while (0)
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Device-side error word (per device, per library instance).  Kernels set it
+// when a bounded wait gives up; the host reads it with ovf_device_error.
+enum : int { DEVERR_NONE = 0, DEVERR_MBAR_TIMEOUT = 1, DEVERR_COUNTER = 2 };
+// Defined once: the library is a single translation unit (csrc/ovf_lib.cu).
+__device__ int g_dev_error = 0;
+
+__device__ __forceinline__ void raise_dev_error(int code) { atomicCAS(&g_dev_error, 0, code); }
+
+// --------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> shared (the TMA engine, no tensor map): dst and src
+// 16-byte aligned, bytes a non-zero multiple of 16.  Completion is signalled
+// on the mbarrier as transaction bytes.  Evict-first L2 policy: weights are
+// streamed once per token and must not push activations out of L2.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after ~2^26 polls (each try_wait itself suspends
+// for a while), raises the device error word and returns false.  A correct
+// program never gets near the limit.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 26); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    raise_dev_error(DEVERR_MBAR_TIMEOUT);
+    return false;
+}
+
+// Programmatic dependent launch: wait until the preceding grid's memory is
+// visible / allow the next grid to start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------------ numerics
+// Explicitly rounded single ops so nvcc cannot contract a*b+c into an FMA:
+// the reference's fp32 tails are separate multiplies and adds.
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
+
+__device__ __forceinline__ float h2f_bits(uint16_t u) { return __half2float(__ushort_as_half(u)); }
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// Q8_K / Q8_0 element quantizer: clamp(round_half_even(x * inv), -127, 127).
+__device__ __forceinline__ int quant_elem(float x, float inv) {
+    float r = rintf(fmul(x, inv));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return static_cast<int>(r);
+}
+
+// Launch helper: launches with the programmatic-stream-serialization
+// attribute so consecutive kernels overlap their prologues (PDL).
+template <typename Kern, typename... Args>
+cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    static const bool no_pdl = [] {
+        const char *v = getenv("OVF_NO_PDL");
+        return v && v[0] == '1';
+    }();
+    attr[0].val.programmaticStreamSerializationAllowed = (pdl && !no_pdl) ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int sm_count(int device);
+
+}  // namespace ovf

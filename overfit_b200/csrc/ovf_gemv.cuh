@@ -1,0 +1,87 @@
+// ovf_gemv.cuh — the quantized decode GEMV (launch parameters and host API).
+//
+// One kernel streams Q4_K (144 B), Q6_K (210 B) and Q8_0 (int8 + fp32 scale)
+// weight rows from HBM with 1-D bulk copies (the TMA engine) into per-warp
+// shared-memory stages, contracts them with a Q8_K / Q8_0 activation held in
+// shared memory using dp4a, and sums each row's super-block terms in
+// ascending order so the result is bit-identical to the reference's
+// sequential fp32 accumulation.  Fused prologues (RMSNorm + activation
+// quantization) and epilogues (bias, residual add, SiLU*up, logits+argmax)
+// remove the separate elementwise launches of a decode step.
+#pragma once
+
+#include "ovf_common.cuh"
+
+namespace ovf {
+
+enum ActMode : int {
+    ACT_PREQ_Q8K = 0,  // Q8_K activation given in global memory (ProjectPreQuantized)
+    ACT_F32 = 1,       // fp32 x, quantized inside every CTA (ProjectParallel)
+    ACT_F32_RMSNORM = 2,  // fp32 x -> RMSNorm(gamma, eps) -> quantized
+};
+
+enum EpiMode : int {
+    EPI_STORE = 0,          // out[row] = bias + sum
+    EPI_RESIDUAL = 1,       // out[row] = resid[row] + (bias + sum)
+    EPI_SILU_PAIR = 2,      // seg0 = gate, seg1 = up: out[row] = silu(gate)*up
+    EPI_LOGITS_ARGMAX = 3,  // out[row] = sum; greedy argmax tracked in DevStep
+};
+
+// Device-resident per-session step state (greedy loop without host syncs).
+struct DevStep {
+    unsigned long long argmax_key;  // (orderable logit << 32) | ~index
+    int done_ctas;                  // last-CTA ticket of the logits kernel
+    int token;                      // token fed to the next step
+    int cur_pos;                    // position being decoded
+    int next_pos;                   // position of the next token
+    int n_generated;
+    int pad[3];
+};
+
+struct GemvSeg {
+    const uint8_t *w;    // K-quant blocks, or Q8_0 int8 quants
+    const float *ws;     // Q8_0 fp32 scales [rows x K/32]
+    const float *bias;   // optional
+    float *out;
+    int type;
+    int rows;
+    int tiles;           // warp-tiles in this segment
+};
+
+struct GemvParams {
+    GemvSeg seg[3];
+    int nseg;
+    int K;
+    int rows_per_tile;   // rows of one warp-tile (per matrix in pair mode)
+    int stages;
+    int q8_group;        // Q8_0 blocks per summation group (== K/32 when ungrouped)
+    int act_mode;
+    int epi;
+    int pair;            // EPI_SILU_PAIR: seg0/seg1 tiles advance together
+    int total_tiles;
+    const float *x;
+    const float *gamma;
+    float eps;
+    const int8_t *aq;    // ACT_PREQ_Q8K
+    const float *as;
+    const int16_t *ab;
+    int8_t *aq_out;      // optional copy of the quantized activation (CTA 0)
+    float *as_out;
+    int16_t *ab_out;
+    const float *resid;
+    DevStep *step;       // EPI_LOGITS_ARGMAX
+    int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
+};
+
+struct GemvPlan {
+    int rows_per_tile, stages, warps, grid;
+    size_t smem;
+};
+
+// Host launcher.  Validates the shape combination, plans tiles/stages from
+// the device's SM count and shared memory, and launches with PDL.
+ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *plan_out = nullptr);
+
+int block_bytes(int type);  // bytes per 256 (K-quant) or per 32 (Q8_0: 32 + 4)
+
+}  // namespace ovf

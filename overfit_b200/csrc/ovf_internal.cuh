@@ -1,0 +1,78 @@
+// ovf_internal.cuh — launchers and device helpers shared between the
+// translation units of libovf_cuda.so (not part of the public C ABI).
+#pragma once
+
+#include "ovf_common.cuh"
+#include "ovf_gemv.cuh"
+
+namespace ovf {
+
+// ---- element decoders (shared by the codecs and the embedding lookup)
+// Value of element e (0..255) of a Q4_K block, exactly as
+// Loading/GgmlDequant.cs:95-141 computes it: (d*sc)*nib - dmin*m.
+__device__ __forceinline__ float q4k_elem(const uint8_t *b, int e) {
+    const float d = h2f_bits((uint16_t)(b[0] | (b[1] << 8)));
+    const float dmin = h2f_bits((uint16_t)(b[2] | (b[3] << 8)));
+    const int j = e / 32;  // sub-block
+    const uint8_t *q = b + 4;
+    int sc, m;
+    if (j < 4) {
+        sc = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+    const int p = j >> 1, i = e & 31;
+    const uint8_t byte = b[16 + 32 * p + i];
+    const int nib = (j & 1) ? (byte >> 4) : (byte & 0x0F);
+    return fsub(fmul(fmul(d, (float)sc), (float)nib), fmul(dmin, (float)m));
+}
+
+// Loading/GgmlDequant.cs:159-209: (d*sc)*(q-32).
+__device__ __forceinline__ float q6k_elem(const uint8_t *b, int e) {
+    const float d = h2f_bits((uint16_t)(b[208] | (b[209] << 8)));
+    const int h = e / 128, r = e % 128, k = r / 32, l = r % 32;
+    const uint8_t qlb = b[64 * h + l + ((k & 1) ? 32 : 0)];
+    const int low = (k >= 2) ? (qlb >> 4) : (qlb & 0x0F);
+    const int hi = (b[128 + 32 * h + l] >> (2 * k)) & 3;
+    const int q = low | (hi << 4);
+    const int sc = (int)(int8_t)b[192 + 8 * h + l / 16 + 2 * k];
+    return fmul(fmul(d, (float)sc), (float)(q - 32));
+}
+
+// ---- ovf_quant.cu
+ovf_status launch_quantize_q8k(const float *x, int64_t k, int8_t *q, float *s, int16_t *b, cudaStream_t st);
+ovf_status launch_quantize_q8_0(const float *x, int64_t k, int8_t *q, float *s, cudaStream_t st);
+ovf_status launch_encode(int type, const float *w, int64_t rows, int64_t k, void *out, cudaStream_t st);
+ovf_status launch_q8_0_deinterleave(const void *g, int64_t n, int8_t *q, float *s, cudaStream_t st);
+ovf_status launch_dequant_rows(int type, const void *w, const float *q8s, int64_t row0, int64_t nrows, int64_t k,
+                               float *dst, cudaStream_t st);
+ovf_status launch_requant_q8_0(int type, const void *w, int64_t rows, int64_t k, int8_t *q, float *s,
+                               cudaStream_t st);
+
+// ---- ovf_ops.cu
+struct AttnParams {
+    const float *q;           // [H*hd] query (raw when rope tables are given)
+    const float *k_new;       // [KVH*hd] key of the current token (raw), or null
+    const float *v_new;       // [KVH*hd] value of the current token, or null
+    __half *kc, *vc;          // this layer's cache [KVH][max_ctx][hd]
+    float *out;               // [H*hd]
+    const float *rope_cos;    // [max_ctx][hd/2] or null
+    const float *rope_sin;
+    const int *pos_dev;       // position of the current token on the device, or null
+    float *partial;           // [H][n_splits][hd+2]
+    int *counters;            // [KVH], zero on entry and on exit
+    int split_half, H, KVH, hd, max_ctx, seq_len_host, n_splits, chunk_max;
+    float scale;
+};
+int attn_splits(int n_kv_heads);
+int64_t attn_scratch_bytes(int H, int KVH, int hd);
+ovf_status launch_attention(const AttnParams &p, cudaStream_t st, bool pdl);
+ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
+ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
+ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
+                        DevStep *step_mut, cudaStream_t st, bool pdl);
+ovf_status launch_silu_mul(const float *g, const float *u, float *h, int64_t n, cudaStream_t st, bool pdl);
+
+}  // namespace ovf

@@ -1,0 +1,8 @@
+// ovf_lib.cu — single translation unit of libovf_cuda.so.  The device-side
+// error word (g_dev_error) is shared by every kernel, so the library is
+// compiled as one unit instead of with relocatable device code.
+#include "ovf_api.cu"
+#include "ovf_quant.cu"
+#include "ovf_gemv.cu"
+#include "ovf_ops.cu"
+#include "ovf_model.cu"

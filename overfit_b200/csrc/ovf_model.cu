@@ -1,0 +1,601 @@
+// ovf_model.cu — device-resident model and decode session behind the C ABI
+// (ovf_model_create / ovf_session_*), the GPU counterpart of
+// CachedLlamaInferenceEngine + CachedLlamaSession (Runtime/
+// CachedLlamaInferenceEngine.cs:33, Runtime/CachedLlamaSession.cs:26).
+//
+// One decode step is 2 + 4*n_layers kernels, all launched with programmatic
+// dependent launch and captured once into a CUDA graph per session:
+//   embed(token)                                   EmbedAndAdvance
+//   per layer:
+//     GEMV  rmsnorm+Q8_K | Wq,Wk,Wv (+bias)        RmsNormalize, ProjectKv/Q
+//     ATTN  RoPE(q,k), KV append, flash-decode     RopeKernel, WriteKey/Value, ComputeSingleHead
+//     GEMV  Q8_0 Wo per head, + residual           AttendAndProjectO, head-ordered sum, AddResidual
+//     GEMV  rmsnorm+Q8_K | gate,up -> silu*up      DecodeSwiGluDispatched (fused gate/up)
+//     GEMV  Q8_K | down, + residual                down projection, AddResidual
+//   GEMV  rmsnorm | lm head -> logits + argmax     final norm, ProjectLogits, TokenSampler.ArgMax
+// The argmax is fed back on the device, so greedy generation replays the
+// graph with no host round trip.
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "ovf_internal.cuh"
+
+using namespace ovf;
+
+namespace {
+
+struct DevWeight {
+    int type = -1;         // OVF_TYPE_* as resident on the device
+    uint8_t *data = nullptr;  // K-quant bytes / Q8_0 int8 quants / f32
+    float *scales = nullptr;  // Q8_0 fp32 scales
+    int64_t rows = 0, cols = 0;
+    bool owns = true;
+};
+
+struct DevLayer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    DevWeight wq, wk, wv, wo, gate, up, down;
+    float *bq = nullptr, *bk = nullptr, *bv = nullptr, *bo = nullptr;
+};
+
+}  // namespace
+
+struct ovf_model {
+    int device = 0;
+    ovf_model_config cfg{};
+    std::vector<DevLayer> layers;
+    DevWeight embed, lm_head;
+    float *final_norm = nullptr;
+    std::vector<void *> allocs;
+    int64_t weight_bytes = 0;
+};
+
+struct ovf_session {
+    ovf_model *m = nullptr;
+    int max_ctx = 0;
+    int pos = 0;           // host mirror of DevStep::next_pos
+    int n_logits = 0;      // host mirror of DevStep::n_generated
+    cudaStream_t stream = nullptr;
+    __half *kc = nullptr, *vc = nullptr;
+    float *hidden = nullptr, *after = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *h = nullptr,
+          *gtmp = nullptr, *utmp = nullptr, *logits = nullptr, *rope_cos = nullptr, *rope_sin = nullptr,
+          *partial = nullptr;
+    int *counters = nullptr, *tokens_log = nullptr;
+    DevStep *step = nullptr;
+    int32_t *pinned_tok = nullptr;  // host staging
+    int pinned_cap = 0;
+    cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
+    std::vector<void *> allocs;
+};
+
+namespace {
+
+ovf_status dalloc(std::vector<void *> &list, void **p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
+    list.push_back(*p);
+    return OVF_OK;
+}
+
+int64_t tensor_bytes(int type, int64_t rows, int64_t cols) {
+    switch (type) {
+        case OVF_TYPE_F32: return rows * cols * 4;
+        case OVF_TYPE_Q8_0: return rows * cols / 32 * 34;
+        case OVF_TYPE_Q4_K: return rows * cols / 256 * 144;
+        case OVF_TYPE_Q6_K: return rows * cols / 256 * 210;
+        default: return -1;
+    }
+}
+
+// Uploads an f32 vector (norm / bias).
+ovf_status upload_vec(ovf_model *m, const ovf_tensor &t, int64_t n, float **out, const char *what) {
+    *out = nullptr;
+    if (!t.data) return OVF_OK;
+    OVF_CHECK_ARG(t.type == OVF_TYPE_F32, "%s must be F32", what);
+    OVF_CHECK_ARG(t.rows * t.cols == n, "%s has %lld elements, expected %lld", what, (long long)(t.rows * t.cols),
+                  (long long)n);
+    ovf_status st = dalloc(m->allocs, (void **)out, n * 4);
+    if (st) return st;
+    OVF_CUDA_TRY(cudaMemcpy(*out, t.data, n * 4, cudaMemcpyHostToDevice));
+    return OVF_OK;
+}
+
+// Uploads a matrix following the reference's residency rules
+// (GgufLlamaLoader.cs:941-1203): K-quants stay verbatim; Q8_0 is
+// de-interleaved to int8 + fp32 scales; everything else, and any matrix
+// `force_q8` asks for (attn_output), becomes Q8_0 with fp32 scales.
+ovf_status upload_matrix(ovf_model *m, const ovf_tensor &t, int64_t rows, int64_t cols, bool force_q8, DevWeight *w,
+                         const char *what) {
+    OVF_CHECK_ARG(t.data, "%s is missing", what);
+    OVF_CHECK_ARG(t.rows == rows && t.cols == cols, "%s is %lldx%lld, expected %lldx%lld", what, (long long)t.rows,
+                  (long long)t.cols, (long long)rows, (long long)cols);
+    const int64_t nbytes = tensor_bytes(t.type, rows, cols);
+    OVF_CHECK_ARG(nbytes > 0, "%s has unsupported type %d", what, t.type);
+    const bool kq = t.type == OVF_TYPE_Q4_K || t.type == OVF_TYPE_Q6_K;
+    OVF_CHECK_ARG(!kq || cols % 256 == 0, "%s: K-quant rows must be multiples of 256", what);
+    OVF_CHECK_ARG(cols % 32 == 0, "%s: row length must be a multiple of 32", what);
+    void *staging = nullptr;
+    ovf_status st = OVF_OK;
+    w->rows = rows;
+    w->cols = cols;
+    if (kq && !force_q8) {
+        w->type = t.type;
+        st = dalloc(m->allocs, (void **)&w->data, nbytes);
+        if (st) return st;
+        OVF_CUDA_TRY(cudaMemcpy(w->data, t.data, nbytes, cudaMemcpyHostToDevice));
+        m->weight_bytes += nbytes;
+        return OVF_OK;
+    }
+    w->type = OVF_TYPE_Q8_0;
+    st = dalloc(m->allocs, (void **)&w->data, rows * cols);
+    if (!st) st = dalloc(m->allocs, (void **)&w->scales, rows * cols / 32 * 4);
+    if (st) return st;
+    m->weight_bytes += rows * cols + rows * cols / 8;
+    OVF_CUDA_TRY(cudaMalloc(&staging, nbytes));
+    cudaError_t e = cudaMemcpy(staging, t.data, nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        if (t.type == OVF_TYPE_Q8_0) st = launch_q8_0_deinterleave(staging, rows * cols, (int8_t *)w->data, w->scales, 0);
+        else st = launch_requant_q8_0(t.type, staging, rows, cols, (int8_t *)w->data, w->scales, 0);
+        if (!st) e = cudaDeviceSynchronize();
+    }
+    cudaFree(staging);
+    if (e != cudaSuccess) return cuda_status(e, what);
+    return st;
+}
+
+ovf_status fill_rope_tables(ovf_session *s) {
+    // Rope/RopeTable.cs:109-133: freq_i = 1/theta^(2i/hd), angle = pos*freq.
+    const int hd = s->m->cfg.head_dim, half = hd / 2;
+    std::vector<float> c((size_t)s->max_ctx * half), sn((size_t)s->max_ctx * half);
+    for (int i = 0; i < half; ++i) {
+        volatile float e = 2.0f * (float)i;
+        e = e / (float)hd;
+        const float freq = 1.0f / powf(s->m->cfg.rope_theta, e);
+        for (int p = 0; p < s->max_ctx; ++p) {
+            volatile float angle = (float)p * freq;
+            c[(size_t)p * half + i] = cosf(angle);
+            sn[(size_t)p * half + i] = sinf(angle);
+        }
+    }
+    OVF_CUDA_TRY(cudaMemcpy(s->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    OVF_CUDA_TRY(cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    return OVF_OK;
+}
+
+GemvSeg seg_of(const DevWeight &w, const float *bias, float *out) {
+    return GemvSeg{w.data, w.scales, bias, out, w.type, (int)w.rows, 0};
+}
+
+bool is_kq(int t) { return t == OVF_TYPE_Q4_K || t == OVF_TYPE_Q6_K; }
+
+// Enqueues one token's kernels on s->stream.
+ovf_status enqueue_step(ovf_session *s, bool with_logits) {
+    ovf_model *m = s->m;
+    const ovf_model_config &c = m->cfg;
+    const cudaStream_t st = s->stream;
+    const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim;
+    ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step, st, true);
+    if (r) return r;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const DevLayer &L = m->layers[l];
+        // Q/K/V: one launch when the three share an activation format.
+        const bool kq = is_kq(L.wq.type);
+        const bool same_family = is_kq(L.wk.type) == kq && is_kq(L.wv.type) == kq;
+        if (same_family) {
+            GemvParams p{};
+            p.nseg = 3;
+            p.seg[0] = seg_of(L.wq, L.bq, s->q);
+            p.seg[1] = seg_of(L.wk, L.bk, s->k);
+            p.seg[2] = seg_of(L.wv, L.bv, s->v);
+            p.K = D;
+            p.act_mode = ACT_F32_RMSNORM;
+            p.x = s->hidden;
+            p.gamma = L.attn_norm;
+            p.eps = c.eps;
+            p.epi = EPI_STORE;
+            if ((r = gemv_launch(p, st, true))) return r;
+        } else {
+            const DevWeight *ws[3] = {&L.wq, &L.wk, &L.wv};
+            const float *bs[3] = {L.bq, L.bk, L.bv};
+            float *os[3] = {s->q, s->k, s->v};
+            for (int i = 0; i < 3; ++i) {
+                GemvParams p{};
+                p.nseg = 1;
+                p.seg[0] = seg_of(*ws[i], bs[i], os[i]);
+                p.K = D;
+                p.act_mode = ACT_F32_RMSNORM;
+                p.x = s->hidden;
+                p.gamma = L.attn_norm;
+                p.eps = c.eps;
+                p.epi = EPI_STORE;
+                if ((r = gemv_launch(p, st, true))) return r;
+            }
+        }
+        AttnParams a{};
+        a.q = s->q;
+        a.k_new = s->k;
+        a.v_new = s->v;
+        a.kc = s->kc + (size_t)l * KVH * s->max_ctx * hd;
+        a.vc = s->vc + (size_t)l * KVH * s->max_ctx * hd;
+        a.out = s->attn;
+        a.rope_cos = s->rope_cos;
+        a.rope_sin = s->rope_sin;
+        a.pos_dev = &s->step->cur_pos;
+        a.partial = s->partial;
+        a.counters = s->counters;
+        a.split_half = c.rope_split_half;
+        a.H = H;
+        a.KVH = KVH;
+        a.hd = hd;
+        a.max_ctx = s->max_ctx;
+        a.scale = 1.0f / sqrtf((float)hd);
+        if ((r = launch_attention(a, st, true))) return r;
+        {
+            // Wo: per-head Q8_0 (G = hd/32 blocks per head), heads summed in
+            // ascending order on top of the bias, then the residual.
+            GemvParams p{};
+            p.nseg = 1;
+            p.seg[0] = seg_of(L.wo, L.bo, s->after);
+            p.K = H * hd;
+            p.q8_group = hd / 32;
+            p.act_mode = ACT_F32;
+            p.x = s->attn;
+            p.epi = EPI_RESIDUAL;
+            p.resid = s->hidden;
+            if ((r = gemv_launch(p, st, true))) return r;
+        }
+        if (L.gate.type == L.up.type) {
+            GemvParams p{};
+            p.nseg = 2;
+            p.pair = 1;
+            p.seg[0] = seg_of(L.gate, nullptr, s->h);
+            p.seg[1] = seg_of(L.up, nullptr, s->h);
+            p.K = D;
+            p.act_mode = ACT_F32_RMSNORM;
+            p.x = s->after;
+            p.gamma = L.ffn_norm;
+            p.eps = c.eps;
+            p.epi = EPI_SILU_PAIR;
+            if ((r = gemv_launch(p, st, true))) return r;
+        } else {
+            const DevWeight *ws[2] = {&L.gate, &L.up};
+            float *os[2] = {s->gtmp, s->utmp};
+            for (int i = 0; i < 2; ++i) {
+                GemvParams p{};
+                p.nseg = 1;
+                p.seg[0] = seg_of(*ws[i], nullptr, os[i]);
+                p.K = D;
+                p.act_mode = ACT_F32_RMSNORM;
+                p.x = s->after;
+                p.gamma = L.ffn_norm;
+                p.eps = c.eps;
+                p.epi = EPI_STORE;
+                if ((r = gemv_launch(p, st, true))) return r;
+            }
+            if ((r = launch_silu_mul(s->gtmp, s->utmp, s->h, c.d_ff, st, true))) return r;
+        }
+        {
+            GemvParams p{};
+            p.nseg = 1;
+            p.seg[0] = seg_of(L.down, nullptr, s->hidden);
+            p.K = c.d_ff;
+            p.act_mode = ACT_F32;
+            p.x = s->h;
+            p.epi = EPI_RESIDUAL;
+            p.resid = s->after;
+            if ((r = gemv_launch(p, st, true))) return r;
+        }
+    }
+    if (with_logits) {
+        GemvParams p{};
+        p.nseg = 1;
+        p.seg[0] = seg_of(m->lm_head, nullptr, s->logits);
+        p.K = D;
+        p.act_mode = ACT_F32_RMSNORM;
+        p.x = s->hidden;
+        p.gamma = m->final_norm;
+        p.eps = c.eps;
+        p.epi = EPI_LOGITS_ARGMAX;
+        p.step = s->step;
+        p.tokens_out = s->tokens_log;
+        if ((r = gemv_launch(p, st, true))) return r;
+    }
+    return OVF_OK;
+}
+
+ovf_status capture(ovf_session *s, bool with_logits, cudaGraphExec_t *out) {
+    cudaGraph_t g = nullptr;
+    OVF_CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    ovf_status r = enqueue_step(s, with_logits);
+    cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+    if (r) {
+        if (g) cudaGraphDestroy(g);
+        return r;
+    }
+    if (e != cudaSuccess) return cuda_status(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return cuda_status(e, "cudaGraphInstantiate");
+}
+
+// OVF_EAGER=1 launches the step's kernels directly instead of replaying a
+// CUDA graph (profiling and debugging); OVF_NO_PDL=1 drops programmatic
+// dependent launch.
+static bool env_flag(const char *name) {
+    const char *v = getenv(name);
+    return v && v[0] == '1';
+}
+
+ovf_status run_step(ovf_session *s, bool with_logits) {
+    cudaGraphExec_t *gx = with_logits ? &s->graph_logits : &s->graph_nologits;
+    if (env_flag("OVF_EAGER")) {
+        ovf_status r = enqueue_step(s, with_logits);
+        if (r) return r;
+        s->pos += 1;
+        if (with_logits) s->n_logits += 1;
+        return OVF_OK;
+    }
+    if (!*gx) {
+        ovf_status r = capture(s, with_logits, gx);
+        if (r) return r;
+    }
+    OVF_CUDA_TRY(cudaGraphLaunch(*gx, s->stream));
+    s->pos += 1;
+    if (with_logits) s->n_logits += 1;
+    return OVF_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int d) {
+        cudaGetDevice(&prev);
+        cudaSetDevice(d);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const ovf_tensor *t, int32_t n_tensors,
+                            ovf_model **out) {
+    OVF_CHECK_ARG(cfg && t && out, "ovf_model_create: null argument");
+    const ovf_model_config &c = *cfg;
+    OVF_CHECK_ARG(c.n_layers > 0 && c.d_model > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.head_dim > 0 &&
+                      c.d_ff > 0 && c.vocab > 0,
+                  "ovf_model_create: config dimensions must be positive");
+    OVF_CHECK_ARG(c.n_heads % c.n_kv_heads == 0, "ovf_model_create: n_heads must be a multiple of n_kv_heads");
+    OVF_CHECK_ARG(c.head_dim % 32 == 0 && c.head_dim <= 256, "ovf_model_create: head_dim must be a multiple of 32, <= 256");
+    OVF_CHECK_ARG(c.n_experts == 0, "ovf_model_create: mixture-of-experts layers are not supported by this build");
+    OVF_CHECK_ARG(n_tensors == c.n_layers * OVF_TENSORS_PER_LAYER + 3, "ovf_model_create: expected %d tensors, got %d",
+                  c.n_layers * OVF_TENSORS_PER_LAYER + 3, n_tensors);
+    int ndev = 0;
+    OVF_CUDA_TRY(cudaGetDeviceCount(&ndev));
+    OVF_CHECK_ARG(device >= 0 && device < ndev, "ovf_model_create: device %d not present", device);
+    DeviceGuard guard(device);
+    ovf_model *m = new ovf_model();
+    m->device = device;
+    m->cfg = c;
+    m->layers.resize(c.n_layers);
+    const int64_t D = c.d_model, QD = (int64_t)c.n_heads * c.head_dim, KD = (int64_t)c.n_kv_heads * c.head_dim;
+    ovf_status st = OVF_OK;
+    for (int l = 0; l < c.n_layers && !st; ++l) {
+        const ovf_tensor *lt = t + (size_t)l * OVF_TENSORS_PER_LAYER;
+        DevLayer &L = m->layers[l];
+        if (!st) st = upload_vec(m, lt[0], D, &L.attn_norm, "attn_norm");
+        if (!st) st = upload_matrix(m, lt[1], QD, D, false, &L.wq, "attn_q");
+        if (!st) st = upload_matrix(m, lt[2], KD, D, false, &L.wk, "attn_k");
+        if (!st) st = upload_matrix(m, lt[3], KD, D, false, &L.wv, "attn_v");
+        if (!st) st = upload_matrix(m, lt[4], D, QD, true, &L.wo, "attn_output");
+        if (!st) st = upload_vec(m, lt[5], QD, &L.bq, "attn_q.bias");
+        if (!st) st = upload_vec(m, lt[6], KD, &L.bk, "attn_k.bias");
+        if (!st) st = upload_vec(m, lt[7], KD, &L.bv, "attn_v.bias");
+        if (!st) st = upload_vec(m, lt[8], D, &L.bo, "attn_output.bias");
+        if (!st) st = upload_vec(m, lt[9], D, &L.ffn_norm, "ffn_norm");
+        if (!st) st = upload_matrix(m, lt[10], c.d_ff, D, false, &L.gate, "ffn_gate");
+        if (!st) st = upload_matrix(m, lt[11], c.d_ff, D, false, &L.up, "ffn_up");
+        if (!st) st = upload_matrix(m, lt[12], D, c.d_ff, false, &L.down, "ffn_down");
+        if (!st && (!L.attn_norm || !L.ffn_norm)) {
+            set_error("layer %d: norms are required", l);
+            st = OVF_EINVAL;
+        }
+    }
+    const ovf_tensor *tail = t + (size_t)c.n_layers * OVF_TENSORS_PER_LAYER;
+    if (!st) {
+        // Embedding (GgufLlamaLoader.cs:546-572): K-quants stay; Q8_0 is held
+        // de-interleaved (its row decode equals the reference's F32 dequant);
+        // F32 stays F32.
+        const ovf_tensor &e = tail[0];
+        if (!e.data || e.rows != c.vocab || e.cols != D) {
+            set_error("token_embd must be vocab x d_model");
+            st = OVF_EINVAL;
+        } else if (e.type == OVF_TYPE_F32) {
+            m->embed.type = OVF_TYPE_F32;
+            m->embed.rows = e.rows;
+            m->embed.cols = e.cols;
+            st = dalloc(m->allocs, (void **)&m->embed.data, D * c.vocab * 4);
+            if (!st) st = cuda_status(cudaMemcpy(m->embed.data, e.data, D * c.vocab * 4, cudaMemcpyHostToDevice), "embed");
+        } else {
+            st = upload_matrix(m, e, c.vocab, D, false, &m->embed, "token_embd");
+            m->weight_bytes -= (m->embed.type == OVF_TYPE_Q8_0) ? (int64_t)c.vocab * D * 9 / 8
+                                                                : tensor_bytes(m->embed.type, c.vocab, D);
+        }
+    }
+    if (!st) st = upload_vec(m, tail[1], D, &m->final_norm, "output_norm");
+    if (!st) {
+        const ovf_tensor &o = tail[2];
+        if (o.data && o.type >= 0) {
+            st = upload_matrix(m, o, c.vocab, D, o.type == OVF_TYPE_F32, &m->lm_head, "output");
+        } else if (m->embed.type == OVF_TYPE_F32) {
+            // Tied F32 embedding: the reference re-quantizes it to Q8_0 (GgufLlamaLoader.cs:478-483).
+            ovf_tensor tt{OVF_TYPE_F32, tail[0].data, c.vocab, D};
+            st = upload_matrix(m, tt, c.vocab, D, true, &m->lm_head, "output(tied)");
+        } else {
+            m->lm_head = m->embed;  // tied: same resident bytes
+            m->lm_head.owns = false;
+            m->weight_bytes += (m->embed.type == OVF_TYPE_Q8_0) ? (int64_t)c.vocab * D * 9 / 8
+                                                                : tensor_bytes(m->embed.type, c.vocab, D);
+        }
+    }
+    if (st) {
+        ovf_model_destroy(m);
+        return st;
+    }
+    *out = m;
+    return OVF_OK;
+}
+
+ovf_status ovf_model_destroy(ovf_model *m) {
+    if (!m) return OVF_OK;
+    DeviceGuard guard(m->device);
+    for (void *p : m->allocs) cudaFree(p);
+    delete m;
+    return OVF_OK;
+}
+
+int64_t ovf_model_weight_bytes(const ovf_model *m) { return m ? m->weight_bytes : 0; }
+
+ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out) {
+    OVF_CHECK_ARG(m && out, "ovf_session_create: null argument");
+    OVF_CHECK_ARG(max_ctx > 0 && max_ctx <= (1 << 20), "ovf_session_create: bad max_ctx");
+    DeviceGuard guard(m->device);
+    ovf_session *s = new ovf_session();
+    s->m = m;
+    s->max_ctx = max_ctx;
+    const ovf_model_config &c = m->cfg;
+    const size_t D = c.d_model, QD = (size_t)c.n_heads * c.head_dim, KD = (size_t)c.n_kv_heads * c.head_dim;
+    const size_t kv = (size_t)c.n_layers * KD * max_ctx;
+    ovf_status st = OVF_OK;
+    auto A = [&](void **p, size_t bytes) {
+        if (!st) st = dalloc(s->allocs, p, bytes);
+    };
+    A((void **)&s->kc, kv * 2);
+    A((void **)&s->vc, kv * 2);
+    A((void **)&s->hidden, D * 4);
+    A((void **)&s->after, D * 4);
+    A((void **)&s->q, QD * 4);
+    A((void **)&s->k, KD * 4);
+    A((void **)&s->v, KD * 4);
+    A((void **)&s->attn, QD * 4);
+    A((void **)&s->h, (size_t)c.d_ff * 4);
+    A((void **)&s->gtmp, (size_t)c.d_ff * 4);
+    A((void **)&s->utmp, (size_t)c.d_ff * 4);
+    A((void **)&s->logits, (size_t)c.vocab * 4);
+    A((void **)&s->rope_cos, (size_t)max_ctx * c.head_dim / 2 * 4);
+    A((void **)&s->rope_sin, (size_t)max_ctx * c.head_dim / 2 * 4);
+    A((void **)&s->partial, (size_t)attn_scratch_bytes(c.n_heads, c.n_kv_heads, c.head_dim));
+    A((void **)&s->counters, (size_t)c.n_kv_heads * 4);
+    A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
+    A((void **)&s->step, sizeof(DevStep));
+    if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
+    if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->kc, 0, kv * 2), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->vc, 0, kv * 2), "memset");
+    if (!st) st = fill_rope_tables(s);
+    if (!st) {
+        s->pinned_cap = max_ctx + 1;
+        st = cuda_status(cudaMallocHost(&s->pinned_tok, (size_t)s->pinned_cap * 4), "cudaMallocHost");
+    }
+    if (st) {
+        ovf_session_destroy(s);
+        return st;
+    }
+    *out = s;
+    return OVF_OK;
+}
+
+ovf_status ovf_session_destroy(ovf_session *s) {
+    if (!s) return OVF_OK;
+    DeviceGuard guard(s->m->device);
+    if (s->stream) cudaStreamSynchronize(s->stream);
+    if (s->graph_logits) cudaGraphExecDestroy(s->graph_logits);
+    if (s->graph_nologits) cudaGraphExecDestroy(s->graph_nologits);
+    for (void *p : s->allocs) cudaFree(p);
+    if (s->pinned_tok) cudaFreeHost(s->pinned_tok);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    delete s;
+    return OVF_OK;
+}
+
+ovf_status ovf_session_reset(ovf_session *s) {
+    OVF_CHECK_ARG(s, "ovf_session_reset: null session");
+    DeviceGuard guard(s->m->device);
+    OVF_CUDA_TRY(cudaMemsetAsync(s->step, 0, sizeof(DevStep), s->stream));
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    s->pos = 0;
+    s->n_logits = 0;
+    return OVF_OK;
+}
+
+int32_t ovf_session_position(const ovf_session *s) { return s ? s->pos : -1; }
+
+static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host, int32_t *argmax_out) {
+    OVF_CHECK_ARG(s, "decode: null session");
+    OVF_CHECK_ARG(n >= 0 && (n == 0 || tokens), "decode: bad token array");
+    OVF_CHECK_ARG(s->pos + n <= s->max_ctx, "KV cache is full (ContextLength=%d, position %d, %d new tokens)", s->max_ctx,
+                  s->pos, n);
+    if (n == 0) return OVF_OK;
+    for (int i = 0; i < n; ++i)
+        OVF_CHECK_ARG(tokens[i] >= 0 && tokens[i] < s->m->cfg.vocab, "token id %d out of range", tokens[i]);
+    DeviceGuard guard(s->m->device);
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    int done = 0;
+    while (done < n) {
+        const int chunk = std::min(n - done, s->pinned_cap);
+        memcpy(s->pinned_tok, tokens + done, (size_t)chunk * 4);
+        for (int i = 0; i < chunk; ++i) {
+            const bool last = done + i == n - 1;
+            OVF_CUDA_TRY(cudaMemcpyAsync(&s->step->token, s->pinned_tok + i, 4, cudaMemcpyHostToDevice, s->stream));
+            ovf_status r = run_step(s, last);
+            if (r) return r;
+        }
+        OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+        done += chunk;
+    }
+    if (logits_host)
+        OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, s->logits, (size_t)s->m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s->stream));
+    if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, &s->step->token, 4, cudaMemcpyDeviceToHost, s->stream));
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    int code = 0;
+    cudaMemcpyFromSymbol(&code, g_dev_error, sizeof(int));
+    if (code) {
+        set_error("device wait timed out (code %d)", code);
+        return OVF_ETIMEDOUT;
+    }
+    return OVF_OK;
+}
+
+ovf_status ovf_session_decode(ovf_session *s, int32_t token, float *logits_host, int32_t *argmax_out) {
+    return decode_impl(s, &token, 1, logits_host, argmax_out);
+}
+
+ovf_status ovf_session_prefill(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host,
+                               int32_t *argmax_out) {
+    return decode_impl(s, tokens, n, logits_host, argmax_out);
+}
+
+ovf_status ovf_session_generate_greedy(ovf_session *s, int32_t n_steps, int32_t *tokens_out) {
+    OVF_CHECK_ARG(s && n_steps >= 0 && (n_steps == 0 || tokens_out), "generate: bad arguments");
+    OVF_CHECK_ARG(s->n_logits > 0, "Session is empty. Call Reset with at least one prompt token first.");
+    OVF_CHECK_ARG(s->pos + n_steps <= s->max_ctx, "KV cache is full (ContextLength=%d)", s->max_ctx);
+    DeviceGuard guard(s->m->device);
+    const int first = s->n_logits - 1;  // the token sampled from the current logits
+    for (int i = 0; i < n_steps; ++i) {
+        ovf_status r = run_step(s, true);
+        if (r) return r;
+    }
+    OVF_CUDA_TRY(cudaMemcpyAsync(tokens_out, s->tokens_log + first, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->stream));
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    return OVF_OK;
+}
+
+void *ovf_session_stream(const ovf_session *s) { return s ? (void *)s->stream : nullptr; }
+
+}  // extern "C"

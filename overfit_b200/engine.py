@@ -1,0 +1,250 @@
+"""Engine / session mirror of the reference's LLM runtime interfaces.
+
+``CudaLlamaInferenceEngine`` and ``CudaLlamaSession`` follow
+``ISlmInferenceEngine`` / ``ISlmSession`` (Contracts/ISlmInferenceEngine.cs:9,
+Contracts/ISlmSession.cs:8) as ``CachedLlamaInferenceEngine`` /
+``CachedLlamaSession`` implement them (Runtime/CachedLlamaInferenceEngine.cs:33,
+Runtime/CachedLlamaSession.cs:26): reset, prefill, greedy next token, last
+logits, position.  All device work happens inside libovf_cuda.so
+(ovf_model_* / ovf_session_*); this module only marshals the tensor table.
+
+Weights come in as a *model file* dict holding what a GGUF loader hands over
+(host numpy arrays in on-disk formats), see ``tensor_table``.
+``synthetic_model`` builds such a dict with random-init weights quantized by
+the library's own device codecs (the bench's Llama-3-8B / Qwen2-0.5B shapes).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import (TENSORS_PER_LAYER, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0, ModelConfig, OverfitRuntimeError,
+                   Tensor, check)
+
+LAYER_KEYS = ("attn_norm", "wq", "wk", "wv", "wo", "bq", "bk", "bv", "bo", "ffn_norm", "gate", "up", "down", "router")
+
+# BASELINE model shapes (random-init, synthetic).  eps follows the reference,
+# which uses 1e-6 for every GGUF model (Runtime/CachedLlamaInferenceEngine.cs:139).
+LLAMA3_8B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, d_ff=14336, vocab=128256,
+                 theta=500000.0, eps=1e-6, rope_split_half=0, tied=False, qkv_bias=False, scheme="q4_k_m")
+QWEN2_05B = dict(n_layers=24, d_model=896, n_heads=14, n_kv_heads=2, head_dim=64, d_ff=4864, vocab=151936,
+                 theta=1000000.0, eps=1e-6, rope_split_half=1, tied=True, qkv_bias=True, scheme="q8_0")
+
+# Q4_K_M tensor map (our choice for synthetic files, documented in DESIGN.md):
+# Q6_K for attn_v, ffn_down and the output head, Q4_K elsewhere.
+_Q4KM = dict(wq=TYPE_Q4_K, wk=TYPE_Q4_K, wv=TYPE_Q6_K, wo=TYPE_Q4_K, gate=TYPE_Q4_K, up=TYPE_Q4_K,
+             down=TYPE_Q6_K, embed=TYPE_Q4_K, lm_head=TYPE_Q6_K)
+
+
+def tensor_of(entry) -> tuple:
+    """Normalizes a weight entry to (type, ndarray, rows, cols)."""
+    if entry is None:
+        return (-1, None, 0, 0)
+    if isinstance(entry, np.ndarray):  # f32 vector
+        return (TYPE_F32, np.ascontiguousarray(entry, dtype=np.float32), 1, entry.size)
+    t, data, rows, cols = entry
+    return (t, np.ascontiguousarray(data), rows, cols)
+
+
+def tensor_table(cfg: dict, model_file: dict):
+    """Builds the ovf_tensor table (include/ovf.h) and the list of arrays it
+    points into (keep it alive until ovf_model_create returns)."""
+    nl = cfg["n_layers"]
+    table = (Tensor * (nl * TENSORS_PER_LAYER + 3))()
+    keep = []
+    for l, layer in enumerate(model_file["layers"]):
+        for j, key in enumerate(LAYER_KEYS):
+            t, data, rows, cols = tensor_of(layer.get(key))
+            if data is not None:
+                keep.append(data)
+            table[l * TENSORS_PER_LAYER + j] = Tensor(t, None if data is None else data.ctypes.data, rows, cols)
+    base = nl * TENSORS_PER_LAYER
+    for j, key in enumerate(("embed", "final_norm", "lm_head")):
+        t, data, rows, cols = tensor_of(model_file.get(key))
+        if data is not None:
+            keep.append(data)
+        table[base + j] = Tensor(t, None if data is None else data.ctypes.data, rows, cols)
+    return table, keep
+
+
+def model_config(cfg: dict) -> ModelConfig:
+    return ModelConfig(cfg["n_layers"], cfg["d_model"], cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"],
+                       cfg["d_ff"], cfg["vocab"], int(cfg.get("rope_split_half", 0)), cfg.get("n_experts", 0),
+                       cfg.get("n_experts_used", 0), int(cfg.get("normalize_experts", 1)), float(cfg["eps"]),
+                       float(cfg["theta"]))
+
+
+class CudaLlamaInferenceEngine:
+    """GPU engine behind ISlmInferenceEngine (weights resident on one device)."""
+
+    def __init__(self, cfg: dict, model_file: dict, device: int = 0):
+        self.cfg = dict(cfg)
+        self.device = device
+        lib = _lib.load()
+        table, keep = tensor_table(cfg, model_file)
+        mc = model_config(cfg)
+        handle = C.c_void_p()
+        check(lib.ovf_model_create(device, C.byref(mc), table, len(table), C.byref(handle)), "ovf_model_create")
+        del keep
+        self._h = handle
+
+    @property
+    def weight_bytes(self) -> int:
+        """Bytes of weights one decode step streams from HBM."""
+        return int(_lib.load().ovf_model_weight_bytes(self._h))
+
+    @property
+    def vocabulary_size(self) -> int:
+        return self.cfg["vocab"]
+
+    def create_session(self, max_context: int) -> "CudaLlamaSession":
+        return CudaLlamaSession(self, max_context)
+
+    def close(self):
+        if self._h:
+            _lib.load().ovf_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaLlamaSession:
+    """ISlmSession over the device-resident decode loop (greedy sampling on
+    the device; logits are copied out only when asked for)."""
+
+    def __init__(self, engine: CudaLlamaInferenceEngine, max_context: int):
+        self.engine = engine
+        self.max_context_length = max_context
+        h = C.c_void_p()
+        check(_lib.load().ovf_session_create(engine._h, max_context, C.byref(h)), "ovf_session_create")
+        self._h = h
+        self._logits = np.zeros(engine.cfg["vocab"], np.float32)
+        self._have_logits = False
+
+    @property
+    def vocabulary_size(self) -> int:
+        return self.engine.cfg["vocab"]
+
+    @property
+    def current_position(self) -> int:
+        return int(_lib.load().ovf_session_position(self._h))
+
+    def reset(self, prompt_tokens=None) -> None:
+        """ISlmSession.Reset / Reset(prompt)."""
+        check(_lib.load().ovf_session_reset(self._h), "Reset")
+        self._have_logits = False
+        if prompt_tokens is not None:
+            self.prefill(prompt_tokens)
+
+    def prefill(self, prompt_tokens) -> int:
+        """CachedLlamaSession.Prefill (single-token path); returns the greedy
+        next token and keeps the last logits."""
+        toks = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32))
+        if toks.size == 0:
+            return -1
+        am = C.c_int32()
+        check(_lib.load().ovf_session_prefill(self._h, toks.ctypes.data, toks.size, self._logits.ctypes.data,
+                                              C.byref(am)), "Prefill")
+        self._have_logits = True
+        return am.value
+
+    def decode(self, token: int, want_logits: bool = True) -> int:
+        """Feeds one token (CachedLlamaSession.DecodeToken); returns argmax."""
+        am = C.c_int32()
+        ptr = self._logits.ctypes.data if want_logits else None
+        check(_lib.load().ovf_session_decode(self._h, int(token), ptr, C.byref(am)), "DecodeToken")
+        self._have_logits = want_logits
+        return am.value
+
+    def generate_greedy(self, n_steps: int) -> np.ndarray:
+        """n x GenerateNextToken with greedy sampling; the argmax is fed back on
+        the device.  Returns the sampled tokens (each one was decoded)."""
+        if not self._have_logits and self.current_position == 0:
+            raise OverfitRuntimeError("Session is empty. Call Reset with at least one prompt token first.")
+        out = np.empty(n_steps, np.int32)
+        check(_lib.load().ovf_session_generate_greedy(self._h, n_steps, out.ctypes.data), "GenerateNextToken")
+        self._have_logits = False
+        return out
+
+    @property
+    def stream_handle(self) -> int:
+        """cudaStream_t of the session (for event timing)."""
+        return int(_lib.load().ovf_session_stream(self._h) or 0)
+
+    def get_last_logits(self) -> np.ndarray:
+        if not self._have_logits:
+            raise OverfitRuntimeError("no logits: decode with want_logits=True first")
+        return self._logits.copy()
+
+    def close(self):
+        if self._h:
+            _lib.load().ovf_session_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------- synthetic
+def synthetic_model(cfg: dict, seed: int = 1, device: int = 0, std: float = 0.02, n_layers: int | None = None):
+    """Random-init model file with the given shape, N(0, std) weights drawn
+    on the device (torch generator, `seed`) and quantized by the library's
+    device encoders (Q4_K: the reference's GgmlQuant scheme; Q6_K / Q8_0:
+    ours).  Norm weights are 1 (the usual RMSNorm init), biases N(0, std).
+    Returns host numpy arrays in on-disk formats."""
+    import torch
+
+    from .kernels import GgmlQuant
+
+    dev = torch.device("cuda", device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    nl = cfg["n_layers"] if n_layers is None else n_layers
+    D, H, KVH, hd, FF, V = (cfg[k] for k in ("d_model", "n_heads", "n_kv_heads", "head_dim", "d_ff", "vocab"))
+    scheme = cfg.get("scheme", "q4_k_m")
+
+    def qtype(key):
+        return _Q4KM[key] if scheme == "q4_k_m" else TYPE_Q8_0
+
+    def mat(rows, cols, t):
+        chunks = []
+        step = max(1, (1 << 27) // cols)
+        for r0 in range(0, rows, step):
+            r = min(step, rows - r0)
+            w = torch.randn(r, cols, generator=g, device=dev, dtype=torch.float32) * std
+            if t == TYPE_Q4_K:
+                q = GgmlQuant.quantize_q4_k(w, cols, r)
+            elif t == TYPE_Q6_K:
+                q = GgmlQuant.quantize_q6_k(w, cols, r)
+            elif t == TYPE_Q8_0:
+                q = GgmlQuant.quantize_q8_0(w)
+            else:
+                q = w
+            chunks.append(q.reshape(-1).cpu())
+        data = torch.cat(chunks).numpy()
+        return (t, data, rows, cols)
+
+    def vec(n):
+        return (torch.randn(n, generator=g, device=dev) * std).cpu().numpy().astype(np.float32)
+
+    layers = []
+    for _ in range(nl):
+        L = dict(attn_norm=np.ones(D, np.float32), ffn_norm=np.ones(D, np.float32),
+                 wq=mat(H * hd, D, qtype("wq")), wk=mat(KVH * hd, D, qtype("wk")), wv=mat(KVH * hd, D, qtype("wv")),
+                 wo=mat(D, H * hd, qtype("wo")), gate=mat(FF, D, qtype("gate")), up=mat(FF, D, qtype("up")),
+                 down=mat(D, FF, qtype("down")))
+        if cfg.get("qkv_bias"):
+            L.update(bq=vec(H * hd), bk=vec(KVH * hd), bv=vec(KVH * hd))
+        layers.append(L)
+    model = dict(layers=layers, embed=mat(V, D, qtype("embed")), final_norm=np.ones(D, np.float32))
+    model["lm_head"] = None if cfg.get("tied") else mat(V, D, qtype("lm_head"))
+    return model

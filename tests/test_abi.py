@@ -1,0 +1,67 @@
+"""The C-ABI library loads without a GPU, exports every entry point that
+include/ovf.h declares, and rejects bad arguments on the host before any
+CUDA call (the reference's ArgumentException cases)."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from overfit_b200 import build
+    build.build()
+    from overfit_b200 import _lib
+    return _lib.load()
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "ovf.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(ovf_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_symbols()
+    assert len(names) >= 30
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/ovf.h but not exported"
+
+
+def test_binding_covers_header():
+    from overfit_b200 import _lib
+    assert set(declared_symbols()) == set(_lib.SIGNATURES), "ctypes signature table out of sync with include/ovf.h"
+
+
+def test_version(lib):
+    assert lib.ovf_version() == 10000
+
+
+def test_argument_errors_without_gpu(lib):
+    from overfit_b200 import _lib
+    # QuantizeActivationQ8K: length not a multiple of 256
+    assert lib.ovf_quantize_q8k(None, 100, None, None, None, None) == _lib.OVF_EINVAL
+    assert b"multiple of 256" in lib.ovf_last_error()
+    # Q8 Quantize: length not a multiple of 32
+    assert lib.ovf_quantize_q8_0(None, 33, None, None, None) == _lib.OVF_EINVAL
+    # projection: not a K-quant type / bad K / unaligned weight
+    assert lib.ovf_kq_project(8, None, None, 4, 256, None, None, None, None, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project(12, None, None, 4, 300, None, None, None, None, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project(12, None, C.c_void_p(17), 4, 256, None, None, None, None, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_q8_0_project(None, None, None, 4, 48, None, None, None, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_dequant_rows(3, None, None, 0, 1, 256, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_rope_apply(None, 1, 63, None, None, 0, None) == _lib.OVF_EINVAL
+    assert lib.ovf_model_create(0, None, None, 0, None) == _lib.OVF_EINVAL
+    assert lib.ovf_session_decode(None, 0, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_attention_scratch_bytes(32, 8, 128) > 0
+
+
+def test_python_mirror_raises_value_error():
+    from overfit_b200 import _lib
+    with pytest.raises(ValueError):
+        _lib.check(_lib.OVF_EINVAL, "x")
+    with pytest.raises(_lib.OverfitRuntimeError):
+        _lib.check(_lib.OVF_ESTATE, "x")
