@@ -144,6 +144,20 @@ ovf_status ovf_attention_decode(const float *q, const void *k_cache, const void 
                                 int32_t max_ctx, int32_t seq_len, float scale, void *scratch,
                                 int32_t *counters, void *stream);
 
+/* No counterpart in the reference (its attention allocates nothing on the
+ * GPU because it has no GPU path).  Same computation as ovf_attention_decode
+ * for callers that cannot call cudaMalloc (a host whose device memory is
+ * owned by one sanctioned allocator, or an allocation-free hot path): the
+ * scratch lives in a file-scope device array of 1 MiB (plus 1 KiB of
+ * counters) that every GPU loading the library holds until exit.  Layouts
+ * whose ovf_attention_scratch_bytes exceed 1 MiB, or with more than 256 KV
+ * heads, return OVF_EINVAL.  The first call on each device looks up the
+ * array's address (make it before any stream capture).  All calls on a
+ * device share the array: calls that overlap on the GPU race. */
+ovf_status ovf_attention_decode_noalloc(const float *q, const void *k_cache, const void *v_cache, float *out,
+                                        int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
+                                        int32_t seq_len, float scale, void *stream);
+
 /* ------------------------------------------------------------- sessions */
 typedef struct ovf_model ovf_model;
 typedef struct ovf_session ovf_session;

@@ -6,3 +6,4 @@
 #include "ovf_gemv.cu"
 #include "ovf_ops.cu"
 #include "ovf_model.cu"
+#include "ovf_noalloc.cu"
