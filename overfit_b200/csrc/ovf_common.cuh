@@ -122,6 +122,13 @@ __device__ __forceinline__ float h2f_bits(uint16_t u) { return __half2float(__us
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // Q8_K / Q8_0 element quantizer: clamp(round_half_even(x * inv), -127, 127).
 __device__ __forceinline__ int quant_elem(float x, float inv) {
     float r = rintf(fmul(x, inv));

@@ -1,31 +1,39 @@
 // ovf_gemv.cu — quantized decode GEMV for sm_100a (see ovf_gemv.cuh).
 //
-// Work decomposition.  The weight matrix is cut into warp-tiles of a few
-// whole rows (one K-quant super-block or 4 Q8_0 blocks per lane).  Every
-// warp owns a private ring of `stages` shared-memory buffers; lane 0 streams
-// its next tiles into them with cp.async.bulk (1-D TMA) while the warp
-// contracts the current one, so each SM keeps ~100-200 KB of weight bytes in
-// flight and no CTA-wide barrier sits on the streaming path.  The first
-// `stages` tiles are requested before griddepcontrol.wait, i.e. while the
-// previous kernel of the decode step is still finishing (PDL).
+// Work decomposition ("lanes own rows").  A warp owns a group of 32/L
+// consecutive weight rows; L lanes (1, 2 or 4) share a row.  The warp streams
+// its rows through a private ring of shared-memory stages, C blocks of every
+// row per stage: each row's chunk is one 1-D bulk copy (the TMA engine) issued
+// by the row's first lane, so every stage is 32/L independent contiguous
+// copies landing on one mbarrier.  The first stages are requested before
+// griddepcontrol.wait, while the previous kernel of the decode step is still
+// finishing (programmatic dependent launch).
 //
-// Exactness.  Integer parts (dp4a over nibbles/6-bit quants x int8) are exact;
-// the per-block fp32 tails use explicitly rounded multiplies/adds in the
-// reference's operand order, and each row's block terms are summed by one
-// lane in ascending block order.  The result equals the reference's
-// sequential loop (Runtime/Q4KDotKernel.cs:528-552, Q6KDotKernel.cs:364-380,
-// Q8DotKernel.cs:311-328) bit for bit.
+// Because a lane group owns whole rows, every lane contracts the same
+// activation block at the same time (shared-memory broadcast), and the row's
+// block terms are accumulated in registers in ascending block order — the
+// reference's sequential fp32 loop (Runtime/Q4KDotKernel.cs:528-552,
+// Q6KDotKernel.cs:364-380, Q8DotKernel.cs:311-328) — with no reduction pass.
+// Integer parts are exact and the fp32 tails use explicitly rounded ops in
+// the reference's operand order, so results are bit-identical to it.
+//
+// Chunks are copied from the 16-byte boundary at or below their first byte
+// (Q6_K blocks are 210 bytes), so a block may start 4/8/12 bytes into its
+// smem row; the Q6_K unit reads through a funnel shift.  A copy that would
+// run past the end of the weight buffer stops at the last 16-byte boundary
+// and its last few bytes are copied by the lane itself.
 #include "ovf_gemv.cuh"
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 
 namespace ovf {
 
-static constexpr int kMaxTermsPerWarp = 512;  // units (blocks) per warp-tile
-static constexpr int kQ8kActStride = 272;     // 256 quants + 16 pad (bank-conflict free)
-static constexpr int kQ8kMetaStride = 48;     // int16 bsums[16] + f32 scale + pad
-static constexpr int kQ80ActStride = 48;      // 32 quants + f32 scale + pad
+static constexpr int kQ8kActStride = 272;  // 256 quants + 16 pad
+static constexpr int kQ8kMetaStride = 48;  // int16 bsums[16] + f32 scale + pad
+static constexpr int kQ80ActStride = 48;   // 32 quants + f32 scale + pad
+static constexpr int kMaxUnits = 4;        // blocks per lane per chunk
 
 int block_bytes(int type) {
     switch (type) {
@@ -37,40 +45,33 @@ int block_bytes(int type) {
 }
 
 static __host__ __device__ inline bool is_kquant(int t) { return t == OVF_TYPE_Q4_K || t == OVF_TYPE_Q6_K; }
-
 static __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
-struct Layout {
-    // byte offsets inside dynamic shared memory
-    int bar_off, act_q_off, act_meta_off, red_off, terms_off, vals_off, stage_off;
-    int stage_bytes, q8_scale_off;  // Q8_0: scales region offset inside a stage
-    int nb, row_bytes;
-};
-
 static __host__ __device__ inline int kq_block_bytes(int type) { return type == OVF_TYPE_Q4_K ? 144 : 210; }
 
-// Bytes of one weight row of `type` (Q8_0: quants + fp32 scales).
-static __host__ __device__ inline int row_bytes_of(int type, int K) {
-    return is_kquant(type) ? (K / 256) * kq_block_bytes(type) : K + K / 8;
+// Row stride in shared memory for a copied span of `bytes` that may start up
+// to 15 bytes before its data: an odd number of 16-byte units, so the lanes'
+// 16-byte reads of 8 consecutive rows fall in distinct banks.
+static __host__ __device__ inline int smem_stride(int bytes) {
+    int s = (int)align_up((size_t)bytes + 30, 16);
+    if (((s / 16) & 1) == 0) s += 16;
+    return s;
 }
 
-// Largest row of the launch's segments (K-quant segments of one launch may
-// mix Q4_K and Q6_K); stage buffers are sized for it.
-static __host__ __device__ inline int max_row_bytes(const GemvParams &p) {
-    int m = 0;
-    for (int s = 0; s < p.nseg; ++s) m = max(m, row_bytes_of(p.seg[s].type, p.K));
-    return m;
-}
+struct Layout {
+    int bar_off, act_q_off, act_meta_off, red_off, terms_off, stage_off;
+    int stage_bytes, q_stride, s_stride, s_region;  // Q8_0: quants rows then scales rows
+    int nb;
+};
 
-static __host__ __device__ inline Layout make_layout(int type, int K, int rpt, int mult, int stages, int warps,
-                                                     int row_bytes_max) {
+// Stage size: the largest over the launch's segments (K-quant launches may
+// mix Q4_K and Q6_K rows).
+static __host__ __device__ inline Layout make_layout(const GemvParams &p, int warps) {
     Layout L{};
-    const bool kq = is_kquant(type);
-    L.nb = kq ? K / 256 : K / 32;
-    L.row_bytes = row_bytes_max;
-    size_t off = 0;
-    L.bar_off = 0;
-    off = align_up(sizeof(uint64_t) * warps * stages, 128);
+    const int type0 = p.seg[0].type;
+    const bool kq = is_kquant(type0);
+    L.nb = kq ? p.K / 256 : p.K / 32;
+    const int slots = 32 / p.lanes_per_row;  // rows per stage (pair: 16 + 16)
+    size_t off = align_up(sizeof(uint64_t) * warps * p.stages, 128);
     L.act_q_off = (int)off;
     if (kq) {
         off = align_up(off + (size_t)L.nb * kQ8kActStride, 128);
@@ -83,118 +84,26 @@ static __host__ __device__ inline Layout make_layout(int type, int K, int rpt, i
     L.red_off = (int)off;
     off = align_up(off + 64 * sizeof(float) + warps * sizeof(unsigned long long), 128);
     L.terms_off = (int)off;
-    off = align_up(off + (size_t)warps * kMaxTermsPerWarp * sizeof(float), 128);
-    L.vals_off = (int)off;
-    off = align_up(off + (size_t)warps * 32 * sizeof(float), 128);
+    off = align_up(off + (size_t)warps * 32 * kMaxUnits * sizeof(float), 128);
     L.stage_off = (int)off;
-    const int rows = rpt * mult;
     if (kq) {
-        L.stage_bytes = (int)align_up((size_t)rows * L.row_bytes + 16, 128);
-        L.q8_scale_off = 0;
+        int mx = 0;
+        for (int s = 0; s < p.nseg; ++s) mx = max(mx, smem_stride(p.chunk * kq_block_bytes(p.seg[s].type)));
+        L.q_stride = mx;
+        L.s_stride = 0;
+        L.s_region = 0;
+        L.stage_bytes = (int)align_up((size_t)slots * mx, 128);
     } else {
-        L.q8_scale_off = (int)align_up((size_t)rows * K, 16);
-        L.stage_bytes = (int)align_up((size_t)L.q8_scale_off + (size_t)rows * (K / 8) + 16, 128);
+        L.q_stride = smem_stride(32 * p.chunk);
+        L.s_stride = smem_stride(4 * p.chunk);
+        L.s_region = slots * L.q_stride;
+        L.stage_bytes = (int)align_up((size_t)slots * (L.q_stride + L.s_stride), 128);
     }
     return L;
 }
 
 static __host__ __device__ inline size_t layout_smem(const Layout &L, int stages, int warps) {
     return (size_t)L.stage_off + (size_t)stages * warps * L.stage_bytes;
-}
-
-// ------------------------------------------------------------ tile helpers
-struct TileRef {
-    int seg, r0, nr;
-};
-
-__device__ __forceinline__ TileRef locate(const GemvParams &p, int t) {
-    TileRef tr{0, 0, 0};
-    int s = 0;
-    if (!p.pair) {
-        while (s < p.nseg - 1 && t >= p.seg[s].tiles) {
-            t -= p.seg[s].tiles;
-            ++s;
-        }
-    }
-    tr.seg = s;
-    tr.r0 = t * p.rows_per_tile;
-    tr.nr = min(p.rows_per_tile, p.seg[s].rows - tr.r0);
-    return tr;
-}
-
-// Issues the bulk copies of one warp-tile (both matrices in pair mode).  A
-// ragged (<16 B) tail of a final partial tile is left to fix_tails.
-__device__ __forceinline__ void issue_tile(const GemvParams &p, const Layout &L, int t, uint8_t *stage,
-                                           uint64_t *bar, uint64_t pol) {
-    TileRef tr = locate(p, t);
-    const GemvSeg &sg = p.seg[tr.seg];
-    const int K = p.K;
-    if (is_kquant(sg.type)) {
-        const int rb = row_bytes_of(sg.type, K);
-        const uint32_t bytes = (uint32_t)(tr.nr * rb);
-        const uint32_t main = bytes & ~15u;
-        const int ncopy = p.pair ? 2 : 1;
-        mbar_arrive_expect_tx(bar, main * ncopy);
-        for (int c = 0; c < ncopy; ++c) {
-            const GemvSeg &g = p.seg[p.pair ? c : tr.seg];
-            uint8_t *dst = stage + (size_t)c * p.rows_per_tile * rb;
-            if (main) bulk_g2s(dst, g.w + (size_t)tr.r0 * rb, main, bar, pol);
-        }
-    } else {
-        const uint32_t qb = (uint32_t)(tr.nr * K);
-        const uint32_t sb = (uint32_t)(tr.nr * (K / 8));
-        const uint32_t qm = qb & ~15u, sm = sb & ~15u;
-        const int ncopy = p.pair ? 2 : 1;
-        mbar_arrive_expect_tx(bar, (qm + sm) * ncopy);
-        for (int c = 0; c < ncopy; ++c) {
-            const GemvSeg &g = p.seg[p.pair ? c : tr.seg];
-            const size_t rq = (size_t)c * p.rows_per_tile;
-            if (qm) bulk_g2s(stage + rq * K, g.w + (size_t)tr.r0 * K, qm, bar, pol);
-            if (sm)
-                bulk_g2s(stage + L.q8_scale_off + rq * (K / 8),
-                         reinterpret_cast<const uint8_t *>(g.ws + (size_t)tr.r0 * (K / 32)), sm, bar, pol);
-        }
-    }
-}
-
-// Copies the ragged (<16 B) tails the bulk engine cannot move.  Only final
-// partial tiles of unusual shapes have one.
-__device__ __forceinline__ void fix_tails(const GemvParams &p, const Layout &L, int t, uint8_t *stage, int lane) {
-    TileRef tr = locate(p, t);
-    const GemvSeg &sg = p.seg[tr.seg];
-    const int K = p.K;
-    if (is_kquant(sg.type)) {
-        const int rb = row_bytes_of(sg.type, K);
-        const uint32_t bytes = (uint32_t)(tr.nr * rb);
-        const uint32_t main = bytes & ~15u;
-        if (main == bytes) return;
-        const int ncopy = p.pair ? 2 : 1;
-        for (int c = 0; c < ncopy; ++c) {
-            const GemvSeg &g = p.seg[p.pair ? c : tr.seg];
-            uint8_t *dst = stage + (size_t)c * p.rows_per_tile * rb;
-            const uint8_t *src = g.w + (size_t)tr.r0 * rb;
-            for (uint32_t i = main + lane; i < bytes; i += 32) dst[i] = src[i];
-        }
-    } else {
-        const uint32_t qb = (uint32_t)(tr.nr * K), sb = (uint32_t)(tr.nr * (K / 8));
-        const uint32_t qm = qb & ~15u, sm = sb & ~15u;
-        const int ncopy = p.pair ? 2 : 1;
-        for (int c = 0; c < ncopy; ++c) {
-            const GemvSeg &g = p.seg[p.pair ? c : tr.seg];
-            const size_t rq = (size_t)c * p.rows_per_tile;
-            const uint8_t *qs = g.w + (size_t)tr.r0 * K;
-            const uint8_t *ss = reinterpret_cast<const uint8_t *>(g.ws + (size_t)tr.r0 * (K / 32));
-            for (uint32_t i = qm + lane; i < qb; i += 32) stage[rq * K + i] = qs[i];
-            for (uint32_t i = sm + lane; i < sb; i += 32) stage[L.q8_scale_off + rq * (K / 8) + i] = ss[i];
-        }
-    }
-}
-
-__device__ __forceinline__ bool tile_has_tail(const GemvParams &p, const Layout &L, int t) {
-    TileRef tr = locate(p, t);
-    const GemvSeg &sg = p.seg[tr.seg];
-    if (is_kquant(sg.type)) return ((tr.nr * row_bytes_of(sg.type, p.K)) & 15) != 0;
-    return ((tr.nr * p.K) & 15) != 0 || ((tr.nr * (p.K / 8)) & 15) != 0;
 }
 
 // ------------------------------------------------------------- dot units
@@ -213,7 +122,7 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
         sc[j + 4] = (int)((byte_of(h.w, j) & 0xFu) | ((byte_of(h.y, j) >> 6) << 4));
         mn[j + 4] = (int)((byte_of(h.w, j) >> 4) | ((byte_of(h.z, j) >> 6) << 4));
     }
-    int mainAcc = 0;
+    int mainAcc = 0, mainAccH = 0;  // mainAccH: exact multiple of 16
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
         const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
@@ -223,24 +132,28 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
         const uint4 h0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 32);
         const uint4 h1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 48);
         const uint32_t M = 0x0F0F0F0Fu;
-        int lo = 0, hi = 0;
+        // High nibbles stay in place (16 * nibble as the unsigned operand):
+        // the sum is 16x the nibble dot and is divided out exactly below.
+        const uint32_t HM = 0xF0F0F0F0u;
+        int lo = 0, lo2 = 0, hi = 0, hi2 = 0;
         lo = dp4a((int)(qa.x & M), (int)l0.x, lo);
+        lo2 = dp4a((int)(qb.x & M), (int)l1.x, lo2);
+        hi = dp4a_us(qa.x & HM, (int)h0.x, hi);
+        hi2 = dp4a_us(qb.x & HM, (int)h1.x, hi2);
         lo = dp4a((int)(qa.y & M), (int)l0.y, lo);
+        lo2 = dp4a((int)(qb.y & M), (int)l1.y, lo2);
+        hi = dp4a_us(qa.y & HM, (int)h0.y, hi);
+        hi2 = dp4a_us(qb.y & HM, (int)h1.y, hi2);
         lo = dp4a((int)(qa.z & M), (int)l0.z, lo);
+        lo2 = dp4a((int)(qb.z & M), (int)l1.z, lo2);
+        hi = dp4a_us(qa.z & HM, (int)h0.z, hi);
+        hi2 = dp4a_us(qb.z & HM, (int)h1.z, hi2);
         lo = dp4a((int)(qa.w & M), (int)l0.w, lo);
-        lo = dp4a((int)(qb.x & M), (int)l1.x, lo);
-        lo = dp4a((int)(qb.y & M), (int)l1.y, lo);
-        lo = dp4a((int)(qb.z & M), (int)l1.z, lo);
-        lo = dp4a((int)(qb.w & M), (int)l1.w, lo);
-        hi = dp4a((int)((qa.x >> 4) & M), (int)h0.x, hi);
-        hi = dp4a((int)((qa.y >> 4) & M), (int)h0.y, hi);
-        hi = dp4a((int)((qa.z >> 4) & M), (int)h0.z, hi);
-        hi = dp4a((int)((qa.w >> 4) & M), (int)h0.w, hi);
-        hi = dp4a((int)((qb.x >> 4) & M), (int)h1.x, hi);
-        hi = dp4a((int)((qb.y >> 4) & M), (int)h1.y, hi);
-        hi = dp4a((int)((qb.z >> 4) & M), (int)h1.z, hi);
-        hi = dp4a((int)((qb.w >> 4) & M), (int)h1.w, hi);
-        mainAcc += sc[2 * p] * lo + sc[2 * p + 1] * hi;
+        lo2 = dp4a((int)(qb.w & M), (int)l1.w, lo2);
+        hi = dp4a_us(qa.w & HM, (int)h0.w, hi);
+        hi2 = dp4a_us(qb.w & HM, (int)h1.w, hi2);
+        mainAcc += sc[2 * p] * (lo + lo2);
+        mainAccH += sc[2 * p + 1] * (hi + hi2);
     }
     const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
     const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
@@ -252,6 +165,7 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
         const int pairsum = (int)(int16_t)(bw[s] & 0xFFFFu) + (int)(int16_t)(bw[s] >> 16);
         minAcc += mn[s] * pairsum;
     }
+    mainAcc += mainAccH >> 4;
     return fmul(q8s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
 }
 
@@ -358,6 +272,27 @@ __device__ float block_rms_scale(const float *x, int K, float eps, float *red) {
     return red[32];
 }
 
+// Block-wide sum of one value per thread (fixed order), broadcast to all.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < nw ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// Activation prologue, Q8_K form.  Every lane first issues the loads of all
+// its elements (independent 16-byte loads, one memory round trip), then the
+// CTA reduces the RMSNorm sum of squares (Runtime/CachedTransformerBlock.cs:
+// 525-552; fixed-order tree, so equal to the reference's sequential sum up to
+// rounding) and quantizes per 256 (Runtime/Q4KDotKernel.cs:71-136).
 __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint8_t *aq = smem + L.act_q_off;
@@ -372,68 +307,138 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
         }
         return;
     }
-    float s = 1.0f;
     float *red = reinterpret_cast<float *>(smem + L.red_off);
-    if (p.act_mode == ACT_F32_RMSNORM) s = block_rms_scale(p.x, p.K, p.eps, red);
+    const bool norm = p.act_mode == ACT_F32_RMSNORM;
     const bool write_out = blockIdx.x == 0 && p.aq_out != nullptr;
-    for (int b = warp; b < nsb; b += nw) {
-        const int e0 = b * 256 + 8 * lane;
-        float v[8];
-        const float4 x0 = *reinterpret_cast<const float4 *>(p.x + e0);
-        const float4 x1 = *reinterpret_cast<const float4 *>(p.x + e0 + 4);
-        v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-        v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
-        if (p.act_mode == ACT_F32_RMSNORM) {
+    constexpr int MB = 8;  // blocks per warp held in registers per batch
+    float s = 1.0f;
+    if (norm) {
+        float ss = 0.0f;
+        for (int b0 = warp; b0 < nsb; b0 += nw * MB) {
+            float4 x0[MB], x1[MB];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = p.gamma ? fmul(fmul(v[i], s), p.gamma[e0 + i]) : fmul(v[i], s);
+            for (int i = 0; i < MB; ++i) {
+                const int b = b0 + i * nw;
+                if (b < nsb) {
+                    x0[i] = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane);
+                    x1[i] = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane + 4);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < MB; ++i) {
+                if (b0 + i * nw < nsb) {
+                    ss = fadd(ss, fmul(x0[i].x, x0[i].x)); ss = fadd(ss, fmul(x0[i].y, x0[i].y));
+                    ss = fadd(ss, fmul(x0[i].z, x0[i].z)); ss = fadd(ss, fmul(x0[i].w, x0[i].w));
+                    ss = fadd(ss, fmul(x1[i].x, x1[i].x)); ss = fadd(ss, fmul(x1[i].y, x1[i].y));
+                    ss = fadd(ss, fmul(x1[i].z, x1[i].z)); ss = fadd(ss, fmul(x1[i].w, x1[i].w));
+                }
+            }
         }
-        float amax = 0.0f;
+        const float tot = block_sum(ss, red);
+        s = fdiv(1.0f, sqrtf(fadd(fdiv(tot, (float)p.K), p.eps)));
+    }
+    for (int b0 = warp; b0 < nsb; b0 += nw * MB) {
+        float v[MB][8];
+        float gm[MB][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        amax = warp_max(amax);
-        const float scale = fdiv(amax, 127.0f);
-        const float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
-        uint32_t w0 = 0, w1 = 0;
-        int sum8 = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int q = quant_elem(v[i], inv);
-            sum8 += q;
-            if (i < 4) w0 |= ((uint32_t)(q & 0xFF)) << (8 * i);
-            else w1 |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
+        for (int i = 0; i < MB; ++i) {
+            const int b = b0 + i * nw;
+            if (b < nsb) {
+                const float4 x0 = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane);
+                const float4 x1 = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane + 4);
+                v[i][0] = x0.x; v[i][1] = x0.y; v[i][2] = x0.z; v[i][3] = x0.w;
+                v[i][4] = x1.x; v[i][5] = x1.y; v[i][6] = x1.z; v[i][7] = x1.w;
+                if (norm && p.gamma) {
+                    const float4 g0 = *reinterpret_cast<const float4 *>(p.gamma + b * 256 + 8 * lane);
+                    const float4 g1 = *reinterpret_cast<const float4 *>(p.gamma + b * 256 + 8 * lane + 4);
+                    gm[i][0] = g0.x; gm[i][1] = g0.y; gm[i][2] = g0.z; gm[i][3] = g0.w;
+                    gm[i][4] = g1.x; gm[i][5] = g1.y; gm[i][6] = g1.z; gm[i][7] = g1.w;
+                }
+            }
         }
-        const int g16 = sum8 + __shfl_xor_sync(0xFFFFFFFFu, sum8, 1);
-        *reinterpret_cast<uint2 *>(aq + b * kQ8kActStride + 8 * lane) = make_uint2(w0, w1);
-        if ((lane & 1) == 0) reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride)[lane >> 1] = (int16_t)g16;
-        if (lane == 0) *reinterpret_cast<float *>(meta + b * kQ8kMetaStride + 32) = scale;
-        if (write_out) {
-            *reinterpret_cast<uint2 *>(p.aq_out + e0) = make_uint2(w0, w1);
-            if ((lane & 1) == 0) p.ab_out[(size_t)b * 16 + (lane >> 1)] = (int16_t)g16;
-            if (lane == 0) p.as_out[b] = scale;
+#pragma unroll
+        for (int i = 0; i < MB; ++i) {
+            const int b = b0 + i * nw;
+            if (b >= nsb) continue;
+            if (norm) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] = p.gamma ? fmul(fmul(v[i][j], s), gm[i][j]) : fmul(v[i][j], s);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+            amax = warp_max(amax);
+            const float scale = fdiv(amax, 127.0f);
+            const float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
+            uint32_t w0 = 0, w1 = 0;
+            int sum8 = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int q = quant_elem(v[i][j], inv);
+                sum8 += q;
+                if (j < 4) w0 |= ((uint32_t)(q & 0xFF)) << (8 * j);
+                else w1 |= ((uint32_t)(q & 0xFF)) << (8 * (j - 4));
+            }
+            const int g16 = sum8 + __shfl_xor_sync(0xFFFFFFFFu, sum8, 1);
+            *reinterpret_cast<uint2 *>(aq + b * kQ8kActStride + 8 * lane) = make_uint2(w0, w1);
+            if ((lane & 1) == 0) reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride)[lane >> 1] = (int16_t)g16;
+            if (lane == 0) *reinterpret_cast<float *>(meta + b * kQ8kMetaStride + 32) = scale;
+            if (write_out) {
+                *reinterpret_cast<uint2 *>(p.aq_out + b * 256 + 8 * lane) = make_uint2(w0, w1);
+                if ((lane & 1) == 0) p.ab_out[(size_t)b * 16 + (lane >> 1)] = (int16_t)g16;
+                if (lane == 0) p.as_out[b] = scale;
+            }
         }
     }
 }
 
+// Activation prologue, Q8_0 form (Runtime/Q8DotKernel.cs:42-91), same
+// load-everything-first structure.
 __device__ void prep_q80(const GemvParams &p, const Layout &L, uint8_t *smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint8_t *act = smem + L.act_q_off;
-    float s = 1.0f;
     float *red = reinterpret_cast<float *>(smem + L.red_off);
-    if (p.act_mode == ACT_F32_RMSNORM) s = block_rms_scale(p.x, p.K, p.eps, red);
+    const bool norm = p.act_mode == ACT_F32_RMSNORM;
     const bool write_out = blockIdx.x == 0 && p.aq_out != nullptr;
-    for (int b = warp; b < L.nb; b += nw) {
-        const int e = b * 32 + lane;
-        float v = p.x[e];
-        if (p.act_mode == ACT_F32_RMSNORM) v = p.gamma ? fmul(fmul(v, s), p.gamma[e]) : fmul(v, s);
-        const float amax = warp_max(fabsf(v));
-        const float scale = fdiv(amax, 127.0f);
-        const float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
-        const int q = quant_elem(v, inv);
-        act[b * kQ80ActStride + lane] = (uint8_t)(int8_t)q;
-        if (lane == 0) *reinterpret_cast<float *>(act + b * kQ80ActStride + 32) = scale;
-        if (write_out) {
-            p.aq_out[e] = (int8_t)q;
-            if (lane == 0) p.as_out[b] = scale;
+    constexpr int MB = 16;
+    const int nb = L.nb;
+    float s = 1.0f;
+    if (norm) {
+        float ss = 0.0f;
+        for (int b0 = warp; b0 < nb; b0 += nw * MB) {
+            float xv[MB];
+#pragma unroll
+            for (int i = 0; i < MB; ++i) xv[i] = (b0 + i * nw < nb) ? p.x[(b0 + i * nw) * 32 + lane] : 0.0f;
+#pragma unroll
+            for (int i = 0; i < MB; ++i) ss = fadd(ss, fmul(xv[i], xv[i]));
+        }
+        const float tot = block_sum(ss, red);
+        s = fdiv(1.0f, sqrtf(fadd(fdiv(tot, (float)p.K), p.eps)));
+    }
+    for (int b0 = warp; b0 < nb; b0 += nw * MB) {
+        float xv[MB], gv[MB];
+#pragma unroll
+        for (int i = 0; i < MB; ++i) {
+            const int b = b0 + i * nw;
+            xv[i] = b < nb ? p.x[b * 32 + lane] : 0.0f;
+            gv[i] = (norm && p.gamma && b < nb) ? p.gamma[b * 32 + lane] : 1.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < MB; ++i) {
+            const int b = b0 + i * nw;
+            if (b >= nb) continue;
+            float v = xv[i];
+            if (norm) v = p.gamma ? fmul(fmul(v, s), gv[i]) : fmul(v, s);
+            const float amax = warp_max(fabsf(v));
+            const float scale = fdiv(amax, 127.0f);
+            const float inv = scale > 0.0f ? fdiv(1.0f, scale) : 0.0f;
+            const int q = quant_elem(v, inv);
+            act[b * kQ80ActStride + lane] = (uint8_t)(int8_t)q;
+            if (lane == 0) *reinterpret_cast<float *>(act + b * kQ80ActStride + 32) = scale;
+            if (write_out) {
+                p.aq_out[b * 32 + lane] = (int8_t)q;
+                if (lane == 0) p.as_out[b] = scale;
+            }
         }
     }
 }
@@ -444,21 +449,110 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
     return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
 }
 
+
+// ------------------------------------------------------------ row groups
+struct GroupRef {
+    int seg, r0, nr;  // nr: valid rows (per matrix in pair mode)
+};
+
+__device__ __forceinline__ GroupRef locate(const GemvParams &p, int g) {
+    int s = 0;
+    if (!p.pair) {
+        while (s < p.nseg - 1 && g >= p.seg[s].groups) {
+            g -= p.seg[s].groups;
+            ++s;
+        }
+    }
+    GroupRef r;
+    r.seg = s;
+    r.r0 = g * p.rows_per_group;
+    r.nr = min(p.rows_per_group, p.seg[s].rows - r.r0);
+    return r;
+}
+
+// Row slot `slot` of a group -> (segment, row) or false when the slot is empty.
+__device__ __forceinline__ bool slot_row(const GemvParams &p, const GroupRef &g, int slot, int *seg, int *row) {
+    if (p.pair) {  // slots [0, half) gate rows, [half, 2*half) the same up rows
+        const int half = p.rows_per_group;
+        const int m = slot >= half ? 1 : 0, i = slot - m * half;
+        *seg = m;
+        *row = g.r0 + i;
+        return i < g.nr;
+    }
+    *seg = g.seg;
+    *row = g.r0 + slot;
+    return slot < g.nr;
+}
+
+// Copies bytes [off, off+len) of `src` (total `total` bytes) so that they sit
+// at dst + (off & 15): the bulk engine moves whole 16-byte units, the lane
+// itself the bytes past the buffer's last 16-byte boundary.  Returns the bulk
+// bytes (for the stage's transaction count); `issue` false only counts.
+__device__ __forceinline__ uint32_t copy_span(uint8_t *dst, const uint8_t *src, size_t off, size_t len, size_t total,
+                                              uint64_t *bar, uint64_t pol, bool issue) {
+    const size_t a = off & ~size_t(15);
+    const size_t e = min(align_up(off + len, 16), total);
+    const size_t be = e & ~size_t(15);
+    const uint32_t bulk = be > a ? (uint32_t)(be - a) : 0u;
+    if (issue) {
+        if (bulk) bulk_g2s(dst, src + a, bulk, bar, pol);
+        for (size_t i = max(a, be); i < e; ++i) dst[i - a] = src[i];
+    }
+    return bulk;
+}
+
+// Issues stage `it` of this warp (row group `g`, chunk `c`): one copy per
+// row (two for Q8_0: quants and scales) by the row's first lane.
+__device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L, const GroupRef &g, int c,
+                                            uint8_t *stage, uint64_t *bar, uint64_t pol, int lane) {
+    const int Lr = p.lanes_per_row;
+    const int slot = lane / Lr;
+    int seg = 0, row = 0;
+    const bool mine = (lane % Lr) == 0 && slot_row(p, g, slot, &seg, &row);
+    uint32_t bytes = 0;
+    const GemvSeg &sg = p.seg[seg];
+    const int type = sg.type;
+    for (int pass = 0; pass < 2; ++pass) {
+        const bool issue = pass == 1;
+        if (issue) {
+            const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, bytes);
+            if (lane == 0) mbar_arrive_expect_tx(bar, total);
+            __syncwarp();
+        }
+        if (!mine) continue;
+        const int nbk = is_kquant(type) ? p.K / 256 : p.K / 32;
+        const int cc = min(p.chunk, nbk - c * p.chunk);  // the last chunk may be short
+        if (is_kquant(type)) {
+            const int bb = kq_block_bytes(type), nb = p.K / 256;
+            const size_t rb = (size_t)nb * bb;
+            const size_t off = (size_t)row * rb + (size_t)c * p.chunk * bb;
+            bytes = copy_span(stage + slot * L.q_stride, sg.w, off, (size_t)cc * bb, (size_t)sg.rows * rb, bar, pol,
+                              issue);
+        } else {
+            const size_t K = p.K;
+            const size_t offq = (size_t)row * K + (size_t)c * p.chunk * 32;
+            const size_t offs = (size_t)row * (K / 8) + (size_t)c * p.chunk * 4;
+            uint32_t b1 = copy_span(stage + slot * L.q_stride, sg.w, offq, (size_t)cc * 32, (size_t)sg.rows * K,
+                                    bar, pol, issue);
+            uint32_t b2 = copy_span(stage + L.s_region + slot * L.s_stride, reinterpret_cast<const uint8_t *>(sg.ws),
+                                    offs, (size_t)cc * 4, (size_t)sg.rows * (K / 8), bar, pol, issue);
+            bytes = b1 + b2;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(384, 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const int type0 = p.seg[0].type;
-    const int mult = p.pair ? 2 : 1;
-    const Layout L = make_layout(type0, p.K, p.rows_per_tile, mult, p.stages, W, max_row_bytes(p));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off) + warp * p.stages;
-    uint8_t *my_stages = smem + L.stage_off + (size_t)warp * p.stages * L.stage_bytes;
-    float *terms = reinterpret_cast<float *>(smem + L.terms_off) + warp * kMaxTermsPerWarp;
-    float *vals = reinterpret_cast<float *>(smem + L.vals_off) + warp * 32;
-
-    const int gw = blockIdx.x * W + warp;
-    const int nwarps = gridDim.x * W;
-    uint64_t pol = l2_evict_first_policy();
+    const Layout L = make_layout(p, W);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * p.stages;
+    uint8_t *ring = smem + L.stage_off + (size_t)warp * p.stages * L.stage_bytes;
+    float *wterms = reinterpret_cast<float *>(smem + L.terms_off) + warp * 32 * kMaxUnits;
+    const int gw = blockIdx.x * W + warp, nwarps = gridDim.x * W;
+    const int my_groups = gw < p.total_groups ? (p.total_groups - gw + nwarps - 1) / nwarps : 0;
+    const int items = my_groups * p.nchunks;
+    const uint64_t pol = l2_evict_first_policy();
 
     if (lane == 0) {
         for (int s = 0; s < p.stages; ++s) mbar_init(&bars[s], 1);
@@ -466,113 +560,129 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvParams p) {
     }
     __syncwarp();
     // Weights do not depend on the previous kernel: start streaming now.
-    if (lane == 0) {
-        for (int s = 0; s < p.stages; ++s) {
-            const int t = gw + s * nwarps;
-            if (t >= p.total_tiles) break;
-            issue_tile(p, L, t, my_stages + (size_t)s * L.stage_bytes, &bars[s], pol);
-        }
+    for (int it = 0; it < p.stages && it < items; ++it) {
+        const GroupRef g = locate(p, gw + (it / p.nchunks) * nwarps);
+        issue_stage(p, L, g, it % p.nchunks, ring + (size_t)it * L.stage_bytes, &bars[it], pol, lane);
     }
+
     pdl_wait();
-    if (is_kquant(type0)) prep_q8k(p, L, smem);
+    if (is_kquant(p.seg[0].type)) prep_q8k(p, L, smem);
     else prep_q80(p, L, smem);
     __syncthreads();
     pdl_launch_dependents();
 
-    const uint8_t *act_q = smem + L.act_q_off;
-    const uint8_t *act_meta = smem + L.act_meta_off;
-    const int nb = L.nb;
-    const int G = is_kquant(type0) ? nb : p.q8_group;
+    const int Lr = p.lanes_per_row, sub = lane % Lr, slot = lane / Lr;
+    const int base_lane = lane - sub;
+    const int nb = L.nb, C = p.chunk, U = p.units_per_lane;
+    const bool kq = is_kquant(p.seg[0].type);
+    const int G = kq ? nb : p.q8_group;
+    const bool grouped = G < nb;
     unsigned long long best = 0ull;
+    float sum = 0.0f, grp = 0.0f, acc = 0.0f;
+    int gpos = 0;
+    GroupRef g{0, 0, 0};
 
-    for (int i = 0;; ++i) {
-        const int t = gw + i * nwarps;
-        if (t >= p.total_tiles) break;
-        const int s = i % p.stages;
-        const uint32_t parity = (uint32_t)((i / p.stages) & 1);
-        uint8_t *stage = my_stages + (size_t)s * L.stage_bytes;
-        if (!mbar_wait_bounded(&bars[s], parity)) {
-            // Give the copies still in flight (tiles i+1 .. i+stages-1) a
-            // bounded chance to land, then stop streaming; the CTA still runs
-            // its common exit path so no barrier is left waiting.
-            for (int j = i + 1; j < i + p.stages; ++j)
-                if (gw + j * nwarps < p.total_tiles)
-                    mbar_wait_bounded(&bars[j % p.stages], (uint32_t)((j / p.stages) & 1));
+    for (int it = 0; it < items; ++it) {
+        const int s = it % p.stages;
+        const int c = it % p.nchunks;
+        uint8_t *stage = ring + (size_t)s * L.stage_bytes;
+        if (!mbar_wait_bounded(&bars[s], (uint32_t)((it / p.stages) & 1))) {
+            // Give the copies still in flight a bounded chance to land, then
+            // stop streaming; the common exit path below still runs.
+            for (int j = it + 1; j < it + p.stages && j < items; ++j)
+                mbar_wait_bounded(&bars[j % p.stages], (uint32_t)((j / p.stages) & 1));
             break;
         }
-        if (tile_has_tail(p, L, t)) {
-            fix_tails(p, L, t, stage, lane);
-            __syncwarp();
+        __syncwarp();  // orders lanes' byte copies of ragged tails
+        if (c == 0) g = locate(p, gw + (it / p.nchunks) * nwarps);
+        int seg = 0, row = 0;
+        const bool valid = slot_row(p, g, slot, &seg, &row);
+        const int type = p.seg[seg].type;
+        if (c == 0) {
+            sum = 0.0f;
+            grp = 0.0f;
+            gpos = 0;
+            acc = (valid && p.seg[seg].bias) ? p.seg[seg].bias[row] : 0.0f;
         }
-        const TileRef tr = locate(p, t);
-        const int type = p.seg[tr.seg].type;
-        const int nrs = tr.nr * mult;  // rows in this stage
-        const int units = nrs * nb;
-        for (int u = lane; u < units; u += 32) {
-            const int sr = u / nb, b = u - sr * nb;
-            const int srow = (p.pair && sr >= tr.nr) ? p.rows_per_tile + (sr - tr.nr) : sr;
-            float term;
-            if (type == OVF_TYPE_Q4_K) {
-                term = q4k_unit(stage + (size_t)(srow * nb + b) * 144, act_q + b * kQ8kActStride,
-                                act_meta + b * kQ8kMetaStride);
-            } else if (type == OVF_TYPE_Q6_K) {
-                term = q6k_unit(stage + (size_t)(srow * nb + b) * 210, act_q + b * kQ8kActStride,
-                                act_meta + b * kQ8kMetaStride);
-            } else {
-                const float ws = reinterpret_cast<const float *>(stage + L.q8_scale_off)[srow * nb + b];
-                term = q80_unit(stage + (size_t)srow * p.K + 32 * b, ws, act_q + b * kQ80ActStride);
-            }
-            terms[u] = term;
-        }
-        __syncwarp();
-        // Stage s is consumed: refill it with the tile `stages` ahead.
-        if (lane == 0) {
-            const int tn = t + p.stages * nwarps;
-            if (tn < p.total_tiles) {
-                fence_proxy_async_smem();
-                issue_tile(p, L, tn, stage, &bars[s], pol);
-            }
-        }
-        // Row sums in ascending block order, one lane per row.
-        if (lane < nrs) {
-            const int seg = (p.pair && lane >= tr.nr) ? 1 : tr.seg;
-            const int row = tr.r0 + ((p.pair && lane >= tr.nr) ? lane - tr.nr : lane);
-            const float *bias = p.seg[seg].bias;
-            const float *tr_terms = terms + lane * nb;
-            float y;
-            if (G >= nb) {
-                float acc = tr_terms[0];
-                for (int b = 1; b < nb; ++b) acc = fadd(acc, tr_terms[b]);
-                y = bias ? fadd(bias[row], acc) : acc;
-            } else {
-                y = bias ? bias[row] : 0.0f;
-                for (int g0 = 0; g0 < nb; g0 += G) {
-                    float acc = tr_terms[g0];
-                    for (int b = 1; b < G; ++b) acc = fadd(acc, tr_terms[g0 + b]);
-                    y = fadd(y, acc);
+        // This lane's blocks of the chunk: j = c*C + sub + Lr*k.
+        const int cc = min(C, nb - c * C);  // blocks in this chunk (the last may be short)
+        float t[kMaxUnits];
+#pragma unroll
+        for (int k = 0; k < kMaxUnits; ++k) {
+            t[k] = 0.0f;
+            if (k < U && valid && !p.skip_compute && sub + Lr * k < cc) {
+                const int m = sub + Lr * k;
+                const int j = c * C + m;
+                if (kq) {
+                    const int bb = kq_block_bytes(type);
+                    const size_t off = (size_t)row * nb * bb + (size_t)c * C * bb;
+                    const uint8_t *blk = stage + slot * L.q_stride + (off & 15) + (size_t)m * bb;
+                    const uint8_t *aq = smem + L.act_q_off + j * kQ8kActStride;
+                    const uint8_t *am = smem + L.act_meta_off + j * kQ8kMetaStride;
+                    t[k] = type == OVF_TYPE_Q4_K ? q4k_unit(blk, aq, am) : q6k_unit(blk, aq, am);
+                } else {
+                    const size_t offq = (size_t)row * p.K + (size_t)c * C * 32;
+                    const size_t offs = (size_t)row * (p.K / 8) + (size_t)c * C * 4;
+                    const uint8_t *wq = stage + slot * L.q_stride + (offq & 15) + 32 * m;
+                    const float ws =
+                        *reinterpret_cast<const float *>(stage + L.s_region + slot * L.s_stride + (offs & 15) + 4 * m);
+                    t[k] = q80_unit(wq, ws, smem + L.act_q_off + j * kQ80ActStride);
                 }
             }
-            vals[lane] = y;
         }
         __syncwarp();
-        if (p.epi == EPI_SILU_PAIR) {
-            if (lane < tr.nr) {
-                const float g = vals[lane], u = vals[tr.nr + lane];
-                const float sg = fdiv(1.0f, fadd(1.0f, expf(-g)));
-                p.seg[0].out[tr.r0 + lane] = fmul(fmul(g, sg), u);
+        // Stage s is consumed: refill it with this warp's item it + stages.
+        {
+            const int nx = it + p.stages;
+            if (nx < items) {
+                fence_proxy_async_smem();
+                const GroupRef gn = locate(p, gw + (nx / p.nchunks) * nwarps);
+                issue_stage(p, L, gn, nx % p.nchunks, stage, &bars[s], pol, lane);
             }
-        } else if (lane < nrs) {
-            const int row = tr.r0 + lane;
-            const float y = vals[lane];
-            float *out = p.seg[tr.seg].out;
-            if (p.epi == EPI_RESIDUAL) out[row] = fadd(p.resid[row], y);
-            else out[row] = y;
-            if (p.epi == EPI_LOGITS_ARGMAX) {
-                const unsigned long long k = argmax_key(y, row);
-                best = k > best ? k : best;
+        }
+        // Ascending block order within the row: the terms go through shared
+        // memory and the row's first lane adds them one by one (independent
+        // loads, then a chain of single fp32 adds).
+#pragma unroll
+        for (int k = 0; k < kMaxUnits; ++k)
+            if (k < U) wterms[slot * C + sub + Lr * k] = t[k];
+        __syncwarp();
+        if (sub == 0) {
+            const float *tr = wterms + slot * C;
+            for (int m = 0; m < cc; ++m) {
+                const float v = tr[m];
+                if (grouped) {
+                    grp = gpos == 0 ? fadd(0.0f, v) : fadd(grp, v);
+                    if (++gpos == G) {
+                        acc = fadd(acc, grp);
+                        gpos = 0;
+                    }
+                } else {
+                    sum = fadd(sum, v);
+                }
             }
         }
         __syncwarp();
+        if (c == p.nchunks - 1) {
+            float y;
+            if (grouped) y = acc;
+            else y = (valid && p.seg[seg].bias) ? fadd(p.seg[seg].bias[row], sum) : sum;
+            if (p.epi == EPI_SILU_PAIR) {
+                const float u = __shfl_down_sync(0xFFFFFFFFu, y, 16);
+                if (slot < p.rows_per_group && valid && sub == 0) {
+                    const float sg = fdiv(1.0f, fadd(1.0f, expf(-y)));
+                    p.seg[0].out[row] = fmul(fmul(y, sg), u);
+                }
+            } else if (valid && sub == 0) {
+                float *out = p.seg[seg].out;
+                if (p.epi == EPI_RESIDUAL) out[row] = fadd(p.resid[row], y);
+                else out[row] = y;
+                if (p.epi == EPI_LOGITS_ARGMAX) {
+                    const unsigned long long kk = argmax_key(y, row);
+                    best = kk > best ? kk : best;
+                }
+            }
+        }
     }
 
     if (p.epi == EPI_LOGITS_ARGMAX) {
@@ -644,7 +754,6 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     }
     OVF_CHECK_ARG(p.K > 0 && (kq ? p.K % 256 == 0 : p.K % 32 == 0), "gemv: K=%d must be a multiple of %d", p.K,
                   kq ? 256 : 32);
-    OVF_CHECK_ARG(kq || p.K % 16 == 0, "gemv: Q8_0 K must be a multiple of 16");
     if (p.act_mode == ACT_PREQ_Q8K) {
         OVF_CHECK_ARG(kq, "gemv: pre-quantized Q8_K activations need K-quant weights");
         OVF_CHECK_ARG(p.aq && p.as && p.ab && aligned16(p.aq), "gemv: pre-quantized activation buffers");
@@ -652,7 +761,8 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
         OVF_CHECK_ARG(p.x && aligned16(p.x), "gemv: x must be non-null and 16-byte aligned");
     }
     if (p.pair)
-        OVF_CHECK_ARG(p.nseg == 2 && p.seg[0].rows == p.seg[1].rows && p.seg[0].type == p.seg[1].type,
+        OVF_CHECK_ARG(p.nseg == 2 && p.seg[0].rows == p.seg[1].rows && p.seg[0].type == p.seg[1].type &&
+                          p.epi == EPI_SILU_PAIR,
                       "gemv: pair mode needs 2 segments of equal shape and type");
     if (p.epi == EPI_RESIDUAL) OVF_CHECK_ARG(p.resid != nullptr, "gemv: residual epilogue without residual");
     if (p.epi == EPI_LOGITS_ARGMAX) OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
@@ -661,60 +771,84 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     OVF_CUDA_TRY(cudaGetDevice(&device));
     const int nsm = sm_count(device);
     const int nb = kq ? p.K / 256 : p.K / 32;
-    const int row_bytes = max_row_bytes(p);
-    // Rows per warp-tile: a multiple of the alignment step that keeps every
-    // full tile's bulk copies 16-byte sized, with ~1 super-block (K-quant) or
-    // ~4 blocks (Q8_0) per lane.
-    int ralign = 1;
-    while (ralign < 16) {
-        bool ok = true;
-        for (int s = 0; s < p.nseg; ++s) {
-            const int rb = row_bytes_of(p.seg[s].type, p.K);
-            ok = ok && (kq ? ((ralign * rb) % 16 == 0) : ((ralign * p.K) % 16 == 0 && (ralign * (p.K / 8)) % 16 == 0));
-        }
-        if (ok) break;
-        ++ralign;
-    }
-    const int mult = p.pair ? 2 : 1;
-    const int units_target = kq ? 32 : 128;
-    int rpt = ralign * std::max(1, units_target / (ralign * nb * mult));
-    while (rpt > ralign && rpt * mult * nb > kMaxTermsPerWarp) rpt -= ralign;
-    OVF_CHECK_ARG(rpt * mult * nb <= kMaxTermsPerWarp && rpt * mult <= 32,
-                  "gemv: K=%d too long for one warp-tile (max %d blocks per row)", p.K, kMaxTermsPerWarp);
-    int total = 0;
-    for (int s = 0; s < p.nseg; ++s) {
-        p.seg[s].tiles = (p.seg[s].rows + rpt - 1) / rpt;
-        if (!p.pair) total += p.seg[s].tiles;
-    }
-    if (p.pair) total = p.seg[0].tiles;
-    p.total_tiles = total;
-    p.rows_per_tile = rpt;
     if (!kq && p.q8_group <= 0) p.q8_group = nb;
     OVF_CHECK_ARG(kq || nb % p.q8_group == 0, "gemv: Q8_0 group must divide the block count");
+    int rows = 0;
+    for (int s = 0; s < p.nseg; ++s) rows += p.seg[s].rows;
+    if (p.pair) rows = p.seg[0].rows * 2;
+    // Lanes per row: enough row groups (32/L rows each) for ~7 warps per SM,
+    // since a warp's rows are its unit of latency hiding.  Blocks per lane:
+    // each row's chunk near 1 KB, one bulk copy (small copies starve the copy
+    // engine).  OVF_GEMV_LR / OVF_GEMV_U override for experiments.
+    const int bb = kq ? kq_block_bytes(type0) : 36;
+    // Lanes per row and blocks per lane (measured on B200 at the Llama-3-8B
+    // shapes): 8 lanes x 2 blocks, i.e. 4 rows per warp and 16 blocks
+    // (2.3-3.4 KB) per row copy; a short last chunk is allowed.
+    int Lr = 1;
+    while (Lr < 8 && 2 * Lr <= nb) Lr *= 2;
+    int U = std::max(1, std::min(2, (nb + Lr - 1) / Lr));
+    if (const char *e = getenv("OVF_GEMV_LR")) Lr = std::max(1, std::min(32, atoi(e)));
+    if (const char *e = getenv("OVF_GEMV_U")) U = std::max(1, std::min(kMaxUnits, atoi(e)));
+    p.lanes_per_row = Lr;
+    p.units_per_lane = U;
+    p.chunk = Lr * U;
+    p.nchunks = (nb + p.chunk - 1) / p.chunk;
+    p.rows_per_group = p.pair ? 16 / Lr : 32 / Lr;
+    int total = 0;
+    for (int s = 0; s < p.nseg; ++s) {
+        p.seg[s].groups = (p.seg[s].rows + p.rows_per_group - 1) / p.rows_per_group;
+        if (!p.pair) total += p.seg[s].groups;
+    }
+    if (p.pair) total = p.seg[0].groups;
+    p.total_groups = total;
     if (total == 0) return OVF_OK;
 
-    // Warps and stages: as many bytes in flight as shared memory allows.
+    // One persistent CTA per SM; each warp has a private ring.  Prefer deep
+    // rings (bytes in flight) while keeping >= 8 warps when the work allows.
     const int budget = smem_optin(device) - 1024;
-    int warps = 16, stages = 0;
-    Layout L{};
-    for (; warps >= 4; warps /= 2) {
-        for (stages = 6; stages >= 2; --stages) {
-            L = make_layout(type0, p.K, rpt, mult, stages, warps, row_bytes);
-            if (layout_smem(L, stages, warps) <= (size_t)budget) break;
+    const int grid = std::min(nsm, total);
+    const int want = std::min(12, (total + grid - 1) / grid);
+    int warps = 0, stages = 0;
+    size_t smem = 0;
+    int s_hi = 6, s_lo = 2, w_force = 0;
+    if (const char *e = getenv("OVF_GEMV_S")) s_hi = s_lo = std::max(2, std::min(8, atoi(e)));
+    if (const char *e = getenv("OVF_GEMV_W")) w_force = std::max(1, std::min(12, atoi(e)));
+    if (const char *e = getenv("OVF_GEMV_SKIP")) p.skip_compute = atoi(e);
+    // Warps per CTA: balance the row groups over the warps (a warp's last
+    // group sets the kernel's end), then the deepest ring that fits.
+    double best_eff = -1.0;
+    const int w_lo = w_force ? w_force : std::max(1, std::min(want, 6));
+    for (int w = w_force ? w_force : want; w >= w_lo; --w) {
+        p.stages = s_lo;
+        if (layout_smem(make_layout(p, w), s_lo, w) > (size_t)budget) continue;
+        const int64_t slots = (int64_t)grid * w;
+        const int64_t rounds = (total + slots - 1) / slots;
+        const double eff = (double)total / (double)(slots * rounds);
+        if (eff > best_eff + 1e-3) {
+            best_eff = eff;
+            warps = w;
         }
-        if (stages >= 3 || (warps == 4 && stages >= 2)) break;
     }
-    OVF_CHECK_ARG(stages >= 2, "gemv: K=%d does not fit shared memory", p.K);
+    if (warps) {
+        for (int S = s_hi; S >= s_lo; --S) {
+            p.stages = S;
+            const Layout L = make_layout(p, warps);
+            if (layout_smem(L, S, warps) <= (size_t)budget) {
+                stages = S;
+                smem = layout_smem(L, S, warps);
+                break;
+            }
+        }
+    }
+    OVF_CHECK_ARG(warps >= 1, "gemv: K=%d does not fit shared memory", p.K);
     p.stages = stages;
-    const size_t smem = layout_smem(L, stages, warps);
-    int grid = std::min(nsm, (total + warps - 1) / warps);
     static bool attr_done[64] = {false};
     if (device < 64 && !attr_done[device]) {
         OVF_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_optin(device)));
         attr_done[device] = true;
     }
-    if (plan_out) *plan_out = GemvPlan{rpt, stages, warps, grid, smem};
+    if (plan_out) *plan_out = GemvPlan{Lr, p.chunk, stages, warps, grid, smem};
     cudaError_t e = launch_pdl(gemv_kernel, dim3(grid), dim3(warps * 32), smem, stream, pdl, p);
     if (e != cudaSuccess) return cuda_status(e, "gemv_kernel launch");
     return OVF_OK;

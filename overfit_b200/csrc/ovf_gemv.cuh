@@ -45,20 +45,25 @@ struct GemvSeg {
     float *out;
     int type;
     int rows;
-    int tiles;           // warp-tiles in this segment
+    int groups;          // row groups (one warp's rows) in this segment
 };
 
 struct GemvParams {
     GemvSeg seg[3];
     int nseg;
     int K;
-    int rows_per_tile;   // rows of one warp-tile (per matrix in pair mode)
+    int lanes_per_row;   // L: lanes sharing one weight row (1, 2 or 4)
+    int units_per_lane;  // u: blocks a lane contracts per chunk
+    int chunk;           // C = L*u blocks of a row streamed per stage
+    int nchunks;         // blocks per row / C
+    int rows_per_group;  // rows one warp owns (32/L; 16 per matrix in pair mode)
     int stages;
     int q8_group;        // Q8_0 blocks per summation group (== K/32 when ungrouped)
     int act_mode;
     int epi;
-    int pair;            // EPI_SILU_PAIR: seg0/seg1 tiles advance together
-    int total_tiles;
+    int pair;            // EPI_SILU_PAIR: seg0 = gate, seg1 = up, same row groups
+    int total_groups;
+    int skip_compute;    // experiments only: stream the weights, contract nothing
     const float *x;
     const float *gamma;
     float eps;
@@ -74,7 +79,7 @@ struct GemvParams {
 };
 
 struct GemvPlan {
-    int rows_per_tile, stages, warps, grid;
+    int lanes_per_row, chunk, stages, warps, grid;
     size_t smem;
 };
 

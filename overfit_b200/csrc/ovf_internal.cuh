@@ -63,12 +63,15 @@ struct AttnParams {
     const int *pos_dev;       // position of the current token on the device, or null
     float *partial;           // [H][n_splits][hd+2]
     int *counters;            // [KVH], zero on entry and on exit
-    int split_half, H, KVH, hd, max_ctx, seq_len_host, n_splits, chunk_max;
+    int split_half, H, KVH, hd, max_ctx, seq_len_host, n_splits, chunk_max, sc_floats;
     float scale;
 };
 int attn_splits(int n_kv_heads);
 int64_t attn_scratch_bytes(int H, int KVH, int hd);
 ovf_status launch_attention(const AttnParams &p, cudaStream_t st, bool pdl);
+// ovf_attn_cluster.cu: cluster-merged variant used by the decode session.
+bool attn_cluster_supported(int G, int hd);
+ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool pdl);
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,

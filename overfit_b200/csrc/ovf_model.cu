@@ -18,6 +18,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "ovf_internal.cuh"
@@ -171,6 +172,54 @@ GemvSeg seg_of(const DevWeight &w, const float *bias, float *out) {
 
 bool is_kq(int t) { return t == OVF_TYPE_Q4_K || t == OVF_TYPE_Q6_K; }
 
+// OVF_PROFILE_STEP=1 (with OVF_EAGER=1): events after every launch of a
+// step, summed per kernel role and printed when the session is destroyed.
+struct StepProfiler {
+    bool on = false;
+    cudaEvent_t last = nullptr;
+    std::vector<std::pair<std::string, std::pair<double, int>>> acc;
+    std::vector<std::pair<std::string, cudaEvent_t>> pending;
+};
+static StepProfiler g_prof;
+
+static void prof_mark(cudaStream_t st, const char *label) {
+    if (!g_prof.on) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, st);
+    g_prof.pending.push_back({label, e});
+}
+
+static void prof_flush(cudaStream_t st) {
+    if (!g_prof.on || g_prof.pending.empty()) return;
+    cudaStreamSynchronize(st);
+    for (auto &pe : g_prof.pending) {
+        if (g_prof.last) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, g_prof.last, pe.second);
+            bool found = false;
+            for (auto &a : g_prof.acc)
+                if (a.first == pe.first) {
+                    a.second.first += ms;
+                    a.second.second += 1;
+                    found = true;
+                }
+            if (!found) g_prof.acc.push_back({pe.first, {ms, 1}});
+            cudaEventDestroy(g_prof.last);
+        }
+        g_prof.last = pe.second;
+    }
+    g_prof.pending.clear();
+}
+
+static void prof_report() {
+    if (!g_prof.on) return;
+    for (auto &a : g_prof.acc)
+        fprintf(stderr, "[ovf profile] %-8s %8d launches %10.1f us total %8.2f us/launch\n", a.first.c_str(),
+                a.second.second, a.second.first * 1e3, a.second.first * 1e3 / a.second.second);
+    g_prof.acc.clear();
+}
+
 // Enqueues one token's kernels on s->stream.
 ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     ovf_model *m = s->m;
@@ -178,6 +227,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     const cudaStream_t st = s->stream;
     const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim;
     ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step, st, true);
+    prof_mark(st, "embed");
     if (r) return r;
     for (int l = 0; l < c.n_layers; ++l) {
         const DevLayer &L = m->layers[l];
@@ -197,6 +247,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.eps = c.eps;
             p.epi = EPI_STORE;
             if ((r = gemv_launch(p, st, true))) return r;
+            prof_mark(st, "qkv");
         } else {
             const DevWeight *ws[3] = {&L.wq, &L.wk, &L.wv};
             const float *bs[3] = {L.bq, L.bk, L.bv};
@@ -212,6 +263,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
                 if ((r = gemv_launch(p, st, true))) return r;
+                prof_mark(st, "qkv");
             }
         }
         AttnParams a{};
@@ -232,7 +284,12 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         a.hd = hd;
         a.max_ctx = s->max_ctx;
         a.scale = 1.0f / sqrtf((float)hd);
-        if ((r = launch_attention(a, st, true))) return r;
+        if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
+            if ((r = launch_attention_cluster(a, st, true))) return r;
+        } else if ((r = launch_attention(a, st, true))) {
+            return r;
+        }
+        prof_mark(st, "attn");
         {
             // Wo: per-head Q8_0 (G = hd/32 blocks per head), heads summed in
             // ascending order on top of the bias, then the residual.
@@ -246,6 +303,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_RESIDUAL;
             p.resid = s->hidden;
             if ((r = gemv_launch(p, st, true))) return r;
+            prof_mark(st, "wo");
         }
         if (L.gate.type == L.up.type) {
             GemvParams p{};
@@ -260,6 +318,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.eps = c.eps;
             p.epi = EPI_SILU_PAIR;
             if ((r = gemv_launch(p, st, true))) return r;
+            prof_mark(st, "gateup");
         } else {
             const DevWeight *ws[2] = {&L.gate, &L.up};
             float *os[2] = {s->gtmp, s->utmp};
@@ -274,8 +333,10 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
                 if ((r = gemv_launch(p, st, true))) return r;
+                prof_mark(st, "gateup");
             }
             if ((r = launch_silu_mul(s->gtmp, s->utmp, s->h, c.d_ff, st, true))) return r;
+            prof_mark(st, "gateup");
         }
         {
             GemvParams p{};
@@ -287,6 +348,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_RESIDUAL;
             p.resid = s->after;
             if ((r = gemv_launch(p, st, true))) return r;
+            prof_mark(st, "down");
         }
     }
     if (with_logits) {
@@ -302,6 +364,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         p.step = s->step;
         p.tokens_out = s->tokens_log;
         if ((r = gemv_launch(p, st, true))) return r;
+        prof_mark(st, "lmhead");
     }
     return OVF_OK;
 }
@@ -332,7 +395,13 @@ static bool env_flag(const char *name) {
 ovf_status run_step(ovf_session *s, bool with_logits) {
     cudaGraphExec_t *gx = with_logits ? &s->graph_logits : &s->graph_nologits;
     if (env_flag("OVF_EAGER")) {
+        g_prof.on = env_flag("OVF_PROFILE_STEP");
+        if (g_prof.on && !g_prof.last) {
+            cudaEventCreate(&g_prof.last);
+            cudaEventRecord(g_prof.last, s->stream);
+        }
         ovf_status r = enqueue_step(s, with_logits);
+        prof_flush(s->stream);
         if (r) return r;
         s->pos += 1;
         if (with_logits) s->n_logits += 1;
@@ -515,6 +584,7 @@ ovf_status ovf_session_destroy(ovf_session *s) {
     if (!s) return OVF_OK;
     DeviceGuard guard(s->m->device);
     if (s->stream) cudaStreamSynchronize(s->stream);
+    prof_report();
     if (s->graph_logits) cudaGraphExecDestroy(s->graph_logits);
     if (s->graph_nologits) cudaGraphExecDestroy(s->graph_nologits);
     for (void *p : s->allocs) cudaFree(p);

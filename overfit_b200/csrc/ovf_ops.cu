@@ -3,6 +3,7 @@
 #include "ovf_internal.cuh"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace ovf {
 
@@ -18,7 +19,14 @@ namespace ovf {
 // zeros as in the reference (:88-92).
 static constexpr int kAttnThreads = 128;
 
-int attn_splits(int n_kv_heads) { return std::max(1, std::min(64, 296 / std::max(1, n_kv_heads))); }
+int attn_splits(int n_kv_heads) {
+    static const int forced = [] {
+        const char *e = getenv("OVF_ATTN_SPLITS");
+        return e ? atoi(e) : 0;
+    }();
+    if (forced > 0) return std::min(64, forced);
+    return std::max(1, std::min(64, 296 / std::max(1, n_kv_heads)));
+}
 
 int64_t attn_scratch_bytes(int H, int KVH, int hd) {
     return (int64_t)H * attn_splits(KVH) * (hd + 2) * (int64_t)sizeof(float);
@@ -40,15 +48,20 @@ __device__ __forceinline__ void rope_rotate(float *v, int hd, const float *c, co
     }
 }
 
+// GT > 0: the query heads per KV head are a compile-time constant (the
+// per-head accumulators stay in registers); GT == 0: runtime count (<= 16).
+template <int GT, int HD>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
     extern __shared__ __align__(16) float asmem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = kAttnThreads / 32;
     const int split = blockIdx.x, g = blockIdx.y;
-    const int G = p.H / p.KVH, hd = p.hd;
+    const int G = GT > 0 ? GT : p.H / p.KVH, hd = p.hd;
+    constexpr int GM = GT > 0 ? GT : 16;
     float *qs = asmem;                       // [G][hd]
     float *knew = qs + G * hd;               // [hd]
     float *vnew = knew + hd;                 // [hd]
     float *sc = vnew + hd;                   // [G][chunk_max]
+    float *mh = sc + p.sc_floats;            // [G] max, [G] sum
     __shared__ int s_last;
 
     pdl_wait();
@@ -68,6 +81,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
             vnew[i] = p.v_new[(size_t)g * hd + i];
         }
     __syncthreads();
+    pdl_launch_dependents();
     if (p.rope_cos) {
         const float *c = p.rope_cos + (size_t)pos * (hd / 2), *s = p.rope_sin + (size_t)pos * (hd / 2);
         for (int h = 0; h < G; ++h) rope_rotate(qs + h * hd, hd, c, s, p.split_half, tid, kAttnThreads);
@@ -86,29 +100,56 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         __syncthreads();
     }
 
-    // Scores: one warp per key, lanes over the head dimension.
-    const int per_lane = hd / 32;
-    for (int t = warp; t < nt; t += nw) {
-        const int pt = t0 + t;
-        float kv[8];
-        if (owns_new && pt == pos) {
-            for (int j = 0; j < per_lane; ++j) kv[j] = knew[lane * per_lane + j];
-        } else {
-            const __half *kr = p.kc + cache_head + (size_t)pt * hd + lane * per_lane;
-            for (int j = 0; j < per_lane; ++j) kv[j] = __half2float(kr[j]);
-        }
-        for (int h = 0; h < G; ++h) {
-            const float *qh = qs + h * hd + lane * per_lane;
-            float acc = 0.0f;
-            for (int j = 0; j < per_lane; ++j) acc = fadd(acc, fmul(qh[j], kv[j]));
+    // Scores: four threads per key, each a quarter of the head dimension read
+    // with independent 16-byte loads issued together; partial dots for all
+    // query heads of the group are folded with two shuffles.
+    {
+        constexpr int HDQ = HD > 0 ? HD / 4 : 64;  // dims per thread (compile-time bound)
+        const int hq = hd / 4;
+        const int kq = tid & 3, kslot = tid >> 2;  // 32 keys per pass
+        for (int tb = 0; tb < nt; tb += kAttnThreads / 4) {
+            const int t = tb + kslot;
+            const bool ok = t < nt;
+            const int pt = t0 + (ok ? t : 0);
+            float kv[HDQ];
+            if (ok && owns_new && pt == pos) {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc = fadd(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
-            if (lane == 0) sc[h * p.chunk_max + t] = fmul(acc, p.scale);
+                for (int i = 0; i < HDQ; ++i)
+                    if (i < hq) kv[i] = knew[kq * hq + i];
+            } else {
+                const uint4 *kr = reinterpret_cast<const uint4 *>(p.kc + cache_head + (size_t)pt * hd + kq * hq);
+                uint4 w[HDQ / 8];
+#pragma unroll
+                for (int i = 0; i < HDQ / 8; ++i)
+                    if (i < hq / 8) w[i] = kr[i];
+#pragma unroll
+                for (int i = 0; i < HDQ / 8; ++i) {
+                    const __half2 *h2 = reinterpret_cast<const __half2 *>(&w[i]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 f = __half22float2(h2[j]);
+                        kv[8 * i + 2 * j] = f.x;
+                        kv[8 * i + 2 * j + 1] = f.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < GM; ++h) {
+                if (h < G) {
+                    const float *qh = qs + h * hd + kq * hq;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < HDQ; ++i)
+                        if (i < hq) acc = fadd(acc, fmul(qh[i], kv[i]));
+                    acc = fadd(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
+                    acc = fadd(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
+                    if (ok && kq == 0) sc[h * p.chunk_max + t] = fmul(acc, p.scale);
+                }
+            }
         }
     }
     __syncthreads();
     // Per head: max, exp, sum (warp per head).
-    float *mh = reinterpret_cast<float *>(&sc[G * p.chunk_max]);  // [G] max, [G] sum
     for (int h = warp; h < G; h += nw) {
         float m = -INFINITY;
         for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * p.chunk_max + t]);
@@ -128,17 +169,64 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         }
     }
     __syncthreads();
-    // Weighted values: thread per dimension, all heads of the group.
-    for (int d = tid; d < hd; d += kAttnThreads) {
-        float o[16];
-        for (int h = 0; h < G; ++h) o[h] = 0.0f;
-        for (int t = 0; t < nt; ++t) {
-            const int pt = t0 + t;
-            const float v = (owns_new && pt == pos) ? vnew[d] : __half2float(p.vc[cache_head + (size_t)pt * hd + d]);
-            for (int h = 0; h < G; ++h) o[h] = fadd(o[h], fmul(sc[h * p.chunk_max + t], v));
+    // Weighted values: a thread per (dimension pair, quarter of the keys);
+    // loads of consecutive keys are independent, so four are kept in flight.
+    {
+        const int npair = hd / 2;
+        const int part = tid / npair, nparts = kAttnThreads / npair;  // hd=128: 64 pairs x 2 parts
+        const int d2 = tid % npair;
+        float o0[GM], o1[GM];
+#pragma unroll
+        for (int h = 0; h < GM; ++h) o0[h] = o1[h] = 0.0f;
+        if (part < nparts) {
+            // eight keys' values loaded before any is used (independent loads)
+            for (int tb = part; tb < nt; tb += 8 * nparts) {
+                float2 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int t = tb + u * nparts;
+                    const int pt = t0 + t;
+                    if (t >= nt) v[u] = make_float2(0.0f, 0.0f);
+                    else if (owns_new && pt == pos) v[u] = make_float2(vnew[2 * d2], vnew[2 * d2 + 1]);
+                    else v[u] = __half22float2(reinterpret_cast<const __half2 *>(p.vc + cache_head + (size_t)pt * hd)[d2]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int t = tb + u * nparts;
+                    if (t < nt) {
+#pragma unroll
+                        for (int h = 0; h < GM; ++h) {
+                            if (h < G) {
+                                const float pr = sc[h * p.chunk_max + t];
+                                o0[h] = fadd(o0[h], fmul(pr, v[u].x));
+                                o1[h] = fadd(o1[h], fmul(pr, v[u].y));
+                            }
+                        }
+                    }
+                }
+            }
         }
-        for (int h = 0; h < G; ++h)
-            p.partial[((size_t)(g * G + h) * p.n_splits + split) * (hd + 2) + d] = o[h];
+        // Partials of part 0..nparts-1 are written side by side and summed by part 0.
+        float *tmp = sc;  // scores are no longer needed
+        __syncthreads();
+        if (part > 0 && part < nparts)
+            for (int h = 0; h < G; ++h) {
+                tmp[((part - 1) * G + h) * hd + 2 * d2] = o0[h];
+                tmp[((part - 1) * G + h) * hd + 2 * d2 + 1] = o1[h];
+            }
+        __syncthreads();
+        if (part == 0) {
+            for (int q = 1; q < nparts; ++q)
+                for (int h = 0; h < G; ++h) {
+                    o0[h] = fadd(o0[h], tmp[((q - 1) * G + h) * hd + 2 * d2]);
+                    o1[h] = fadd(o1[h], tmp[((q - 1) * G + h) * hd + 2 * d2 + 1]);
+                }
+            for (int h = 0; h < G; ++h) {
+                float *dst = p.partial + ((size_t)(g * G + h) * p.n_splits + split) * (hd + 2);
+                dst[2 * d2] = o0[h];
+                dst[2 * d2 + 1] = o1[h];
+            }
+        }
     }
     if (tid < G) {
         float *pp = p.partial + ((size_t)(g * G + tid) * p.n_splits + split) * (hd + 2) + hd;
@@ -154,30 +242,52 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int h = 0; h < G; ++h) {
-        const float *base = p.partial + (size_t)(g * G + h) * p.n_splits * (hd + 2);
-        float M = -INFINITY;
-        for (int s = 0; s < p.n_splits; ++s) {
-            const float ls = __ldcg(base + (size_t)s * (hd + 2) + hd + 1);
-            if (ls > 0.0f) M = fmaxf(M, __ldcg(base + (size_t)s * (hd + 2) + hd));
+    // Merge: every split's (max, sum) of every head in one parallel pass, the
+    // rescale weights exp(m_s - M) in another, then each dimension loads all
+    // of its splits at once (independent loads) and sums them in split order.
+    {
+        const int ns = p.n_splits;
+        float *mm = sc;              // [G][ns] split maxima (-inf when empty)
+        float *ll = mm + G * ns;     // [G][ns] split sums
+        float *ww = ll + G * ns;     // [G][ns] weights
+        float *hm = ww + G * ns;     // [G] M, [G] 1/L (0 when the sum is not usable)
+        for (int i = tid; i < G * ns; i += kAttnThreads) {
+            const int h = i / ns, s2 = i - h * ns;
+            const float *pp = p.partial + ((size_t)(g * G + h) * ns + s2) * (hd + 2) + hd;
+            const float ls = __ldcg(pp + 1), ms = __ldcg(pp);
+            mm[i] = ls > 0.0f ? ms : -INFINITY;
+            ll[i] = ls;
         }
-        float L = 0.0f;
-        for (int s = 0; s < p.n_splits; ++s) {
-            const float ls = __ldcg(base + (size_t)s * (hd + 2) + hd + 1);
-            if (ls > 0.0f) L = fadd(L, fmul(ls, expf(fsub(__ldcg(base + (size_t)s * (hd + 2) + hd), M))));
+        __syncthreads();
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, mm[tid * ns + s2]);
+            hm[tid] = M;
         }
-        const bool ok = L > 0.0f && isfinite(L);
-        const float inv = ok ? fdiv(1.0f, L) : 0.0f;
-        for (int d = tid; d < hd; d += kAttnThreads) {
-            float acc = 0.0f;
-            for (int s = 0; s < p.n_splits; ++s) {
-                const float ls = __ldcg(base + (size_t)s * (hd + 2) + hd + 1);
-                if (ls > 0.0f) {
-                    const float w = expf(fsub(__ldcg(base + (size_t)s * (hd + 2) + hd), M));
-                    acc = fadd(acc, fmul(w, __ldcg(base + (size_t)s * (hd + 2) + d)));
-                }
+        __syncthreads();
+        for (int i = tid; i < G * ns; i += kAttnThreads)
+            ww[i] = ll[i] > 0.0f ? expf(fsub(mm[i], hm[i / ns])) : 0.0f;
+        __syncthreads();
+        if (tid < G) {
+            float L = 0.0f;
+            for (int s2 = 0; s2 < ns; ++s2) L = fadd(L, fmul(ll[tid * ns + s2], ww[tid * ns + s2]));
+            hm[G + tid] = (L > 0.0f && isfinite(L)) ? fdiv(1.0f, L) : 0.0f;
+        }
+        __syncthreads();
+        for (int h = 0; h < G; ++h) {
+            const float *base = p.partial + (size_t)(g * G + h) * ns * (hd + 2);
+            const float inv = hm[G + h];
+            for (int d = tid; d < hd; d += kAttnThreads) {
+                float v[64];
+#pragma unroll
+                for (int s2 = 0; s2 < 64; ++s2)
+                    v[s2] = s2 < ns ? __ldcg(base + (size_t)s2 * (hd + 2) + d) : 0.0f;
+                float acc = 0.0f;
+#pragma unroll
+                for (int s2 = 0; s2 < 64; ++s2)
+                    if (s2 < ns) acc = fadd(acc, fmul(ww[h * ns + s2], v[s2]));
+                p.out[(size_t)(g * G + h) * hd + d] = inv > 0.0f ? fmul(acc, inv) : 0.0f;
             }
-            p.out[(size_t)(g * G + h) * hd + d] = ok ? fmul(acc, inv) : 0.0f;
         }
     }
     if (tid == 0) p.counters[g] = 0;
@@ -194,14 +304,23 @@ ovf_status launch_attention(const AttnParams &p0, cudaStream_t st, bool pdl) {
     const int span = p.pos_dev ? p.max_ctx : p.seq_len_host;
     p.chunk_max = (span + p.n_splits - 1) / p.n_splits;
     const int G = p.H / p.KVH;
-    const size_t smem = sizeof(float) * ((size_t)G * p.hd + 2 * p.hd + (size_t)G * p.chunk_max + 2 * G);
-    OVF_CHECK_ARG(smem <= 200 * 1024, "attention: context too long for one split's score buffer");
-    static bool attr_done = false;
-    if (!attr_done) {
-        OVF_CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        attr_done = true;
-    }
-    cudaError_t e = launch_pdl(attention_kernel, dim3(p.n_splits, p.KVH), dim3(kAttnThreads), smem, st, pdl, p);
+    const int nparts = kAttnThreads / (p.hd / 2);
+    const size_t scratch_f = std::max({(size_t)G * p.chunk_max, (size_t)(nparts - 1) * G * p.hd,
+                                       (size_t)3 * G * p.n_splits + 2 * G});
+    p.sc_floats = (int)scratch_f;
+    const size_t smem = sizeof(float) * ((size_t)G * p.hd + 2 * p.hd + scratch_f + 2 * G);
+    OVF_CHECK_ARG(smem <= 48 * 1024, "attention: context too long for one split's score buffer");
+    cudaError_t e;
+    const dim3 grid(p.n_splits, p.KVH), block(kAttnThreads);
+#define OVF_ATTN(gt, hdv) e = launch_pdl(attention_kernel<gt, hdv>, grid, block, smem, st, pdl, p)
+    if (p.hd == 128 && G == 4) OVF_ATTN(4, 128);
+    else if (p.hd == 128 && G == 8) OVF_ATTN(8, 128);
+    else if (p.hd == 128 && G == 1) OVF_ATTN(1, 128);
+    else if (p.hd == 64 && G == 7) OVF_ATTN(7, 64);
+    else if (p.hd == 64 && G == 4) OVF_ATTN(4, 64);
+    else if (p.hd == 64 && G == 8) OVF_ATTN(8, 64);
+    else OVF_ATTN(0, 0);
+#undef OVF_ATTN
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "attention_kernel launch");
 }
 
