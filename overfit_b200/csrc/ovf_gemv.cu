@@ -31,7 +31,7 @@
 namespace ovf {
 
 static constexpr int kQ8kActStride = 272;  // 256 quants + 16 pad
-static constexpr int kQ8kMetaStride = 48;  // int16 bsums[16] + f32 scale + pad
+static constexpr int kQ8kMetaStride = 64;  // int16 bsums[16] | f32 scale | pad | int16 pair sums[8]
 static constexpr int kQ80ActStride = 48;   // 32 quants + f32 scale + pad
 static constexpr int kMaxUnits = 4;        // blocks per lane per chunk
 
@@ -58,20 +58,22 @@ static __host__ __device__ inline int smem_stride(int bytes) {
 }
 
 struct Layout {
-    int bar_off, act_q_off, act_meta_off, red_off, terms_off, stage_off;
+    int act_q_off, act_meta_off, red_off, terms_off, stage_off;
     int stage_bytes, q_stride, s_stride, s_region;  // Q8_0: quants rows then scales rows
+    int part_bytes, s_part;                         // whole-row stages: bytes per matrix part
     int nb;
 };
 
-// Stage size: the largest over the launch's segments (K-quant launches may
-// mix Q4_K and Q6_K rows).
-static __host__ __device__ inline Layout make_layout(const GemvParams &p, int warps) {
+// Shared memory: mbarriers | activation | reduction scratch | two term
+// buffers [T][C] | stage ring.  Stage rows are sized for the launch's
+// largest block (K-quant launches may mix Q4_K and Q6_K rows).
+static __host__ __device__ inline Layout make_layout(const GemvParams &p) {
     Layout L{};
     const int type0 = p.seg[0].type;
     const bool kq = is_kquant(type0);
     L.nb = kq ? p.K / 256 : p.K / 32;
-    const int slots = 32 / p.lanes_per_row;  // rows per stage (pair: 16 + 16)
-    size_t off = align_up(sizeof(uint64_t) * warps * p.stages, 128);
+    const int T = p.rows_per_group;
+    size_t off = align_up(sizeof(uint64_t) * 2 * p.stages, 128);
     L.act_q_off = (int)off;
     if (kq) {
         off = align_up(off + (size_t)L.nb * kQ8kActStride, 128);
@@ -82,28 +84,48 @@ static __host__ __device__ inline Layout make_layout(const GemvParams &p, int wa
         L.act_meta_off = L.act_q_off;
     }
     L.red_off = (int)off;
-    off = align_up(off + 64 * sizeof(float) + warps * sizeof(unsigned long long), 128);
+    off = align_up(off + 64 * sizeof(float) + 32 * sizeof(unsigned long long), 128);
     L.terms_off = (int)off;
-    off = align_up(off + (size_t)warps * 32 * kMaxUnits * sizeof(float), 128);
+    off = align_up(off + (size_t)p.stages * T * p.chunk * sizeof(float), 128);
     L.stage_off = (int)off;
-    if (kq) {
+    if (p.chunk == L.nb) {
+        // Whole rows: a tile's rows are contiguous in the weight buffer, so a
+        // stage is one copy per matrix (quants and scales for Q8_0).
+        const int parts = p.pair ? 2 : 1, per = T / parts;
+        if (kq) {
+            int rb = 0;
+            for (int s = 0; s < p.nseg; ++s) rb = max(rb, L.nb * kq_block_bytes(p.seg[s].type));
+            L.q_stride = rb;
+            L.part_bytes = (int)align_up((size_t)per * rb + 16, 16);
+            L.s_stride = 0;
+            L.s_part = 0;
+            L.s_region = parts * L.part_bytes;
+        } else {
+            L.q_stride = p.K;
+            L.part_bytes = (int)align_up((size_t)per * p.K + 16, 16);
+            L.s_stride = p.K / 8;
+            L.s_part = (int)align_up((size_t)per * (p.K / 8) + 16, 16);
+            L.s_region = parts * L.part_bytes;
+        }
+        L.stage_bytes = (int)align_up((size_t)L.s_region + (size_t)parts * L.s_part, 128);
+    } else if (kq) {
         int mx = 0;
         for (int s = 0; s < p.nseg; ++s) mx = max(mx, smem_stride(p.chunk * kq_block_bytes(p.seg[s].type)));
         L.q_stride = mx;
         L.s_stride = 0;
         L.s_region = 0;
-        L.stage_bytes = (int)align_up((size_t)slots * mx, 128);
+        L.stage_bytes = (int)align_up((size_t)T * mx, 128);
     } else {
         L.q_stride = smem_stride(32 * p.chunk);
         L.s_stride = smem_stride(4 * p.chunk);
-        L.s_region = slots * L.q_stride;
-        L.stage_bytes = (int)align_up((size_t)slots * (L.q_stride + L.s_stride), 128);
+        L.s_region = T * L.q_stride;
+        L.stage_bytes = (int)align_up((size_t)T * (L.q_stride + L.s_stride), 128);
     }
     return L;
 }
 
-static __host__ __device__ inline size_t layout_smem(const Layout &L, int stages, int warps) {
-    return (size_t)L.stage_off + (size_t)stages * warps * L.stage_bytes;
+static __host__ __device__ inline size_t layout_smem(const Layout &L, int stages) {
+    return (size_t)L.stage_off + (size_t)stages * L.stage_bytes;
 }
 
 // ------------------------------------------------------------- dot units
@@ -114,14 +136,10 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
     const uint4 h = *reinterpret_cast<const uint4 *>(blk);
     const float d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
     const float dmin = h2f_bits((uint16_t)(h.x >> 16));
-    int sc[8], mn[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        sc[j] = (int)(byte_of(h.y, j) & 63u);
-        mn[j] = (int)(byte_of(h.z, j) & 63u);
-        sc[j + 4] = (int)((byte_of(h.w, j) & 0xFu) | ((byte_of(h.y, j) >> 6) << 4));
-        mn[j + 4] = (int)((byte_of(h.w, j) >> 4) | ((byte_of(h.z, j) >> 6) << 4));
-    }
+    // 6-bit scales and mins (Loading/GgmlDequant.cs:49-77), four per word
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
     int mainAcc = 0, mainAccH = 0;  // mainAccH: exact multiple of 16
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
@@ -131,15 +149,13 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
         const uint4 l1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 16);
         const uint4 h0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 32);
         const uint4 h1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 48);
-        const uint32_t M = 0x0F0F0F0Fu;
+        const uint32_t M = 0x0F0F0F0Fu, HM = 0xF0F0F0F0u;
         // High nibbles stay in place (16 * nibble as the unsigned operand):
-        // the sum is 16x the nibble dot and is divided out exactly below.
-        const uint32_t HM = 0xF0F0F0F0u;
-        int lo = 0, lo2 = 0, hi = 0, hi2 = 0;
-        lo = dp4a((int)(qa.x & M), (int)l0.x, lo);
-        lo2 = dp4a((int)(qb.x & M), (int)l1.x, lo2);
-        hi = dp4a_us(qa.x & HM, (int)h0.x, hi);
-        hi2 = dp4a_us(qb.x & HM, (int)h1.x, hi2);
+        // that sum is 16x the nibble dot and is divided out exactly below.
+        int lo = dp4a((int)(qa.x & M), (int)l0.x, 0);
+        int lo2 = dp4a((int)(qb.x & M), (int)l1.x, 0);
+        int hi = dp4a_us(qa.x & HM, (int)h0.x, 0);
+        int hi2 = dp4a_us(qb.x & HM, (int)h1.x, 0);
         lo = dp4a((int)(qa.y & M), (int)l0.y, lo);
         lo2 = dp4a((int)(qb.y & M), (int)l1.y, lo2);
         hi = dp4a_us(qa.y & HM, (int)h0.y, hi);
@@ -152,20 +168,18 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
         lo2 = dp4a((int)(qb.w & M), (int)l1.w, lo2);
         hi = dp4a_us(qa.w & HM, (int)h0.w, hi);
         hi2 = dp4a_us(qb.w & HM, (int)h1.w, hi2);
-        mainAcc += sc[2 * p] * (lo + lo2);
-        mainAccH += sc[2 * p + 1] * (hi + hi2);
-    }
-    const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
-    const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
-    const float q8s = *reinterpret_cast<const float *>(meta + 32);
-    const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-    int minAcc = 0;
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        const int pairsum = (int)(int16_t)(bw[s] & 0xFFFFu) + (int)(int16_t)(bw[s] >> 16);
-        minAcc += mn[s] * pairsum;
+        const uint32_t scw = p < 2 ? sc03 : sc47;
+        mainAcc += (int)byte_of(scw, (2 * p) & 3) * (lo + lo2);
+        mainAccH += (int)byte_of(scw, (2 * p + 1) & 3) * (hi + hi2);
     }
     mainAcc += mainAccH >> 4;
+    // min correction: sum_s m[s] * (bsum[2s] + bsum[2s+1]) as four dp2a
+    const uint4 ps = *reinterpret_cast<const uint4 *>(meta + 48);
+    const float q8s = *reinterpret_cast<const float *>(meta + 32);
+    int minAcc = __dp2a_lo((int)ps.x, (int)mn03, 0);
+    minAcc = __dp2a_hi((int)ps.y, (int)mn03, minAcc);
+    minAcc = __dp2a_lo((int)ps.z, (int)mn47, minAcc);
+    minAcc = __dp2a_hi((int)ps.w, (int)mn47, minAcc);
     return fmul(q8s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
 }
 
@@ -303,6 +317,9 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
             *reinterpret_cast<uint2 *>(aq + b * kQ8kActStride + 8 * lane) =
                 *reinterpret_cast<const uint2 *>(p.aq + (size_t)b * 256 + 8 * lane);
             if (lane < 16) reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride)[lane] = p.ab[(size_t)b * 16 + lane];
+            if (lane < 8)
+                reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride + 48)[lane] =
+                    (int16_t)(p.ab[(size_t)b * 16 + 2 * lane] + p.ab[(size_t)b * 16 + 2 * lane + 1]);
             if (lane == 0) *reinterpret_cast<float *>(meta + b * kQ8kMetaStride + 32) = p.as[b];
         }
         return;
@@ -310,7 +327,7 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
     float *red = reinterpret_cast<float *>(smem + L.red_off);
     const bool norm = p.act_mode == ACT_F32_RMSNORM;
     const bool write_out = blockIdx.x == 0 && p.aq_out != nullptr;
-    constexpr int MB = 8;  // blocks per warp held in registers per batch
+    constexpr int MB = 4;  // blocks per warp held in registers per batch
     float s = 1.0f;
     if (norm) {
         float ss = 0.0f;
@@ -380,8 +397,10 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
                 else w1 |= ((uint32_t)(q & 0xFF)) << (8 * (j - 4));
             }
             const int g16 = sum8 + __shfl_xor_sync(0xFFFFFFFFu, sum8, 1);
+            const int g32 = g16 + __shfl_xor_sync(0xFFFFFFFFu, g16, 2);
             *reinterpret_cast<uint2 *>(aq + b * kQ8kActStride + 8 * lane) = make_uint2(w0, w1);
             if ((lane & 1) == 0) reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride)[lane >> 1] = (int16_t)g16;
+            if ((lane & 3) == 0) reinterpret_cast<int16_t *>(meta + b * kQ8kMetaStride + 48)[lane >> 2] = (int16_t)g32;
             if (lane == 0) *reinterpret_cast<float *>(meta + b * kQ8kMetaStride + 32) = scale;
             if (write_out) {
                 *reinterpret_cast<uint2 *>(p.aq_out + b * 256 + 8 * lane) = make_uint2(w0, w1);
@@ -450,13 +469,14 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
 }
 
 
-// ------------------------------------------------------------ row groups
+// ------------------------------------------------------------ row tiles
 struct GroupRef {
     int seg, r0, nr;  // nr: valid rows (per matrix in pair mode)
 };
 
 __device__ __forceinline__ GroupRef locate(const GemvParams &p, int g) {
     int s = 0;
+    const int rows_per = p.pair ? p.rows_per_group / 2 : p.rows_per_group;
     if (!p.pair) {
         while (s < p.nseg - 1 && g >= p.seg[s].groups) {
             g -= p.seg[s].groups;
@@ -465,15 +485,16 @@ __device__ __forceinline__ GroupRef locate(const GemvParams &p, int g) {
     }
     GroupRef r;
     r.seg = s;
-    r.r0 = g * p.rows_per_group;
-    r.nr = min(p.rows_per_group, p.seg[s].rows - r.r0);
+    r.r0 = g * rows_per;
+    r.nr = min(rows_per, p.seg[s].rows - r.r0);
     return r;
 }
 
-// Row slot `slot` of a group -> (segment, row) or false when the slot is empty.
+// Row slot of a tile -> (segment, row); false for an empty slot.  Pair
+// mode: slots [0, T/2) are gate rows, [T/2, T) the same up rows.
 __device__ __forceinline__ bool slot_row(const GemvParams &p, const GroupRef &g, int slot, int *seg, int *row) {
-    if (p.pair) {  // slots [0, half) gate rows, [half, 2*half) the same up rows
-        const int half = p.rows_per_group;
+    if (p.pair) {
+        const int half = p.rows_per_group / 2;
         const int m = slot >= half ? 1 : 0, i = slot - m * half;
         *seg = m;
         *row = g.r0 + i;
@@ -501,17 +522,60 @@ __device__ __forceinline__ uint32_t copy_span(uint8_t *dst, const uint8_t *src, 
     return bulk;
 }
 
-// Issues stage `it` of this warp (row group `g`, chunk `c`): one copy per
-// row (two for Q8_0: quants and scales) by the row's first lane.
+// Issued by warp 0: chunk `c` of every row of tile `g`, one copy per row
+// (two for Q8_0: quants and scales), lane i copying row slot i.
 __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L, const GroupRef &g, int c,
                                             uint8_t *stage, uint64_t *bar, uint64_t pol, int lane) {
-    const int Lr = p.lanes_per_row;
-    const int slot = lane / Lr;
+    if (p.chunk == L.nb) {
+        // Whole rows: lane `part` copies the tile's rows of its matrix.
+        const int parts = p.pair ? 2 : 1;
+        const GemvSeg &sg = p.seg[p.pair ? min(lane, 1) : g.seg];
+        uint32_t bytes = 0;
+        const bool mine = lane < parts && g.nr > 0;
+        for (int pass = 0; pass < 2; ++pass) {
+            const bool issue = pass == 1;
+            if (issue) {
+                const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, bytes);
+                if (lane == 0) mbar_arrive_expect_tx(bar, total);
+                __syncwarp();
+            }
+            if (!mine) continue;
+            if (is_kquant(sg.type)) {
+                // The part is cut into `split` copies issued by consecutive
+                // lanes: more copies in flight keep more DRAM requests open.
+                const size_t rb = (size_t)L.nb * kq_block_bytes(sg.type);
+                const size_t off = (size_t)g.r0 * rb, len = (size_t)g.nr * rb;
+                const size_t a0 = off & ~size_t(15);
+                const size_t piece = align_up((len + (off - a0) + p.copy_split - 1) / p.copy_split, 16);
+                bytes = 0;
+                for (int q = 0; q < p.copy_split; ++q) {
+                    const size_t ps = a0 + q * piece;
+                    if (ps >= off + len) break;
+                    const size_t s0 = q == 0 ? off : ps;
+                    const size_t e0 = min(off + len, ps + piece);
+                    bytes += copy_span(stage + lane * L.part_bytes + (s0 - a0) - (s0 & 15), sg.w, s0, e0 - s0,
+                                       (size_t)sg.rows * rb, bar, pol, issue);
+                }
+            } else {
+                const size_t K = p.K;
+                const uint32_t b1 = copy_span(stage + lane * L.part_bytes, sg.w, (size_t)g.r0 * K, (size_t)g.nr * K,
+                                              (size_t)sg.rows * K, bar, pol, issue);
+                const uint32_t b2 = copy_span(stage + L.s_region + lane * L.s_part,
+                                              reinterpret_cast<const uint8_t *>(sg.ws), (size_t)g.r0 * (K / 8),
+                                              (size_t)g.nr * (K / 8), (size_t)sg.rows * (K / 8), bar, pol, issue);
+                bytes = b1 + b2;
+            }
+        }
+        return;
+    }
+    const int slot = lane;
     int seg = 0, row = 0;
-    const bool mine = (lane % Lr) == 0 && slot_row(p, g, slot, &seg, &row);
+    const bool mine = slot < p.rows_per_group && slot_row(p, g, slot, &seg, &row);
     uint32_t bytes = 0;
     const GemvSeg &sg = p.seg[seg];
     const int type = sg.type;
+    const int nbk = is_kquant(type) ? p.K / 256 : p.K / 32;
+    const int cc = min(p.chunk, nbk - c * p.chunk);  // the last chunk may be short
     for (int pass = 0; pass < 2; ++pass) {
         const bool issue = pass == 1;
         if (issue) {
@@ -520,11 +584,9 @@ __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L
             __syncwarp();
         }
         if (!mine) continue;
-        const int nbk = is_kquant(type) ? p.K / 256 : p.K / 32;
-        const int cc = min(p.chunk, nbk - c * p.chunk);  // the last chunk may be short
         if (is_kquant(type)) {
-            const int bb = kq_block_bytes(type), nb = p.K / 256;
-            const size_t rb = (size_t)nb * bb;
+            const int bb = kq_block_bytes(type);
+            const size_t rb = (size_t)nbk * bb;
             const size_t off = (size_t)row * rb + (size_t)c * p.chunk * bb;
             bytes = copy_span(stage + slot * L.q_stride, sg.w, off, (size_t)cc * bb, (size_t)sg.rows * rb, bar, pol,
                               issue);
@@ -532,38 +594,56 @@ __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L
             const size_t K = p.K;
             const size_t offq = (size_t)row * K + (size_t)c * p.chunk * 32;
             const size_t offs = (size_t)row * (K / 8) + (size_t)c * p.chunk * 4;
-            uint32_t b1 = copy_span(stage + slot * L.q_stride, sg.w, offq, (size_t)cc * 32, (size_t)sg.rows * K,
-                                    bar, pol, issue);
-            uint32_t b2 = copy_span(stage + L.s_region + slot * L.s_stride, reinterpret_cast<const uint8_t *>(sg.ws),
-                                    offs, (size_t)cc * 4, (size_t)sg.rows * (K / 8), bar, pol, issue);
+            const uint32_t b1 = copy_span(stage + slot * L.q_stride, sg.w, offq, (size_t)cc * 32, (size_t)sg.rows * K,
+                                          bar, pol, issue);
+            const uint32_t b2 =
+                copy_span(stage + L.s_region + slot * L.s_stride, reinterpret_cast<const uint8_t *>(sg.ws), offs,
+                          (size_t)cc * 4, (size_t)sg.rows * (K / 8), bar, pol, issue);
             bytes = b1 + b2;
         }
     }
 }
 
 // ------------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(384, 1) gemv_kernel(const GemvParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const Layout L = make_layout(p, W);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem) + warp * p.stages;
-    uint8_t *ring = smem + L.stage_off + (size_t)warp * p.stages * L.stage_bytes;
-    float *wterms = reinterpret_cast<float *>(smem + L.terms_off) + warp * 32 * kMaxUnits;
-    const int gw = blockIdx.x * W + warp, nwarps = gridDim.x * W;
-    const int my_groups = gw < p.total_groups ? (p.total_groups - gw + nwarps - 1) / nwarps : 0;
-    const int items = my_groups * p.nchunks;
-    const uint64_t pol = l2_evict_first_policy();
+// A CTA owns T-row tiles (persistent, tile = blockIdx.x + i*gridDim.x) and
+// streams each through a ring of `stages` shared-memory buffers, C blocks of
+// every row per stage.  Warp specialisation: the last warp issues the bulk
+// copies and keeps the ordered row sums; the other (compute) warps contract
+// each stage (thread -> row slot and block, so the lanes of a warp read at
+// most two activation blocks) into the stage's [T][C] term buffer and
+// arrive on the stage's `done` mbarrier.  The row warp then adds row r's
+// terms in ascending block order (lane r), refills the stage and, after a
+// row's last chunk, runs the epilogue.  No CTA-wide barrier sits in the loop.
+static constexpr int kComputeWarps = 8;
 
-    if (lane == 0) {
-        for (int s = 0; s < p.stages; ++s) mbar_init(&bars[s], 1);
+__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 1) gemv_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const Layout L = make_layout(p);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *done = full + p.stages;
+    uint8_t *ring = smem + L.stage_off;
+    float *tbuf = reinterpret_cast<float *>(smem + L.terms_off);
+    const int T = p.rows_per_group, C = p.chunk, nb = L.nb;
+    const int my_tiles = blockIdx.x < p.total_groups ? (p.total_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const int items = my_tiles * p.nchunks;
+    const uint64_t pol = l2_evict_first_policy();
+    const bool row_warp = warp == kComputeWarps;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&done[s], kComputeWarps);
+        }
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
     // Weights do not depend on the previous kernel: start streaming now.
-    for (int it = 0; it < p.stages && it < items; ++it) {
-        const GroupRef g = locate(p, gw + (it / p.nchunks) * nwarps);
-        issue_stage(p, L, g, it % p.nchunks, ring + (size_t)it * L.stage_bytes, &bars[it], pol, lane);
-    }
+    if (row_warp)
+        for (int it = 0; it < p.stages && it < items; ++it) {
+            const GroupRef g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
+            issue_stage(p, L, g, it % p.nchunks, ring + (size_t)it * L.stage_bytes, &full[it], pol, lane);
+        }
 
     pdl_wait();
     if (is_kquant(p.seg[0].type)) prep_q8k(p, L, smem);
@@ -571,84 +651,107 @@ __global__ void __launch_bounds__(384, 1) gemv_kernel(const GemvParams p) {
     __syncthreads();
     pdl_launch_dependents();
 
-    const int Lr = p.lanes_per_row, sub = lane % Lr, slot = lane / Lr;
-    const int base_lane = lane - sub;
-    const int nb = L.nb, C = p.chunk, U = p.units_per_lane;
     const bool kq = is_kquant(p.seg[0].type);
+    if (!row_warp) {
+        // ------------------------------------------------ compute warps
+        const int ct = warp * 32 + lane, nct = kComputeWarps * 32;
+        const int rs = ct % T, m0 = ct / T, mstep = nct / T;
+        GroupRef g{0, 0, 0};
+        for (int it = 0; it < items; ++it) {
+            const int s = it % p.stages;
+            const int c = it % p.nchunks;
+            if (c == 0) g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
+            if (!mbar_wait_bounded(&full[s], (uint32_t)((it / p.stages) & 1))) break;
+            const uint8_t *stage = ring + (size_t)s * L.stage_bytes;
+            float *tb = tbuf + (size_t)s * T * C;
+            int seg = 0, row = 0;
+            const bool valid = slot_row(p, g, rs, &seg, &row);
+            const int type = p.seg[seg].type;
+            const int cc = min(C, nb - c * C);
+            if (C == nb) {
+                // Whole rows: unit u -> (row slot u / nb, block u % nb); the
+                // lanes of a warp walk consecutive blocks of one or two rows.
+                if (!p.skip_compute) {
+                    const int half = p.pair ? T / 2 : T;
+                    for (int u = ct; u < T * nb; u += nct) {
+                        const int us = u / nb, m = u - us * nb;
+                        int useg = 0, urow = 0;
+                        if (!slot_row(p, g, us, &useg, &urow)) continue;
+                        const int part = us / half, i = us - part * half;
+                        const int utype = p.seg[useg].type;
+                        float t;
+                        if (kq) {
+                            const int bb = kq_block_bytes(utype);
+                            const size_t off0 = (size_t)g.r0 * nb * bb;
+                            const uint8_t *blk = stage + part * L.part_bytes + (off0 & 15) + (size_t)i * L.q_stride +
+                                                 (size_t)m * bb;
+                            t = utype == OVF_TYPE_Q4_K
+                                    ? q4k_unit(blk, smem + L.act_q_off + m * kQ8kActStride,
+                                               smem + L.act_meta_off + m * kQ8kMetaStride)
+                                    : q6k_unit(blk, smem + L.act_q_off + m * kQ8kActStride,
+                                               smem + L.act_meta_off + m * kQ8kMetaStride);
+                        } else {
+                            const size_t offq0 = (size_t)g.r0 * p.K, offs0 = (size_t)g.r0 * (p.K / 8);
+                            const uint8_t *wq = stage + part * L.part_bytes + (offq0 & 15) + (size_t)i * p.K + 32 * m;
+                            const float ws = *reinterpret_cast<const float *>(
+                                stage + L.s_region + part * L.s_part + (offs0 & 15) + (size_t)i * (p.K / 8) + 4 * m);
+                            t = q80_unit(wq, ws, smem + L.act_q_off + m * kQ80ActStride);
+                        }
+                        tb[us * C + m] = t;
+                    }
+                }
+            } else if (valid && !p.skip_compute) {
+                for (int m = m0; m < cc; m += mstep) {
+                    const int j = c * C + m;
+                    float t;
+                    if (kq) {
+                        const int bb = kq_block_bytes(type);
+                        const size_t off = (size_t)row * nb * bb + (size_t)c * C * bb;
+                        const uint8_t *blk = stage + rs * L.q_stride + (off & 15) + (size_t)m * bb;
+                        const uint8_t *aq = smem + L.act_q_off + j * kQ8kActStride;
+                        const uint8_t *am = smem + L.act_meta_off + j * kQ8kMetaStride;
+                        t = type == OVF_TYPE_Q4_K ? q4k_unit(blk, aq, am) : q6k_unit(blk, aq, am);
+                    } else {
+                        const size_t offq = (size_t)row * p.K + (size_t)c * C * 32;
+                        const size_t offs = (size_t)row * (p.K / 8) + (size_t)c * C * 4;
+                        const uint8_t *wq = stage + rs * L.q_stride + (offq & 15) + 32 * m;
+                        const float ws = *reinterpret_cast<const float *>(stage + L.s_region + rs * L.s_stride +
+                                                                          (offs & 15) + 4 * m);
+                        t = q80_unit(wq, ws, smem + L.act_q_off + j * kQ80ActStride);
+                    }
+                    tb[rs * C + m] = t;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&done[s]);
+        }
+        return;
+    }
+
+    // ------------------------------------------------------ row warp
     const int G = kq ? nb : p.q8_group;
     const bool grouped = G < nb;
     unsigned long long best = 0ull;
-    float sum = 0.0f, grp = 0.0f, acc = 0.0f;
+    float sum = 0.0f, grp = 0.0f, acc = 0.0f;  // lane r: running sums of row slot r
     int gpos = 0;
     GroupRef g{0, 0, 0};
-
     for (int it = 0; it < items; ++it) {
         const int s = it % p.stages;
         const int c = it % p.nchunks;
-        uint8_t *stage = ring + (size_t)s * L.stage_bytes;
-        if (!mbar_wait_bounded(&bars[s], (uint32_t)((it / p.stages) & 1))) {
-            // Give the copies still in flight a bounded chance to land, then
-            // stop streaming; the common exit path below still runs.
-            for (int j = it + 1; j < it + p.stages && j < items; ++j)
-                mbar_wait_bounded(&bars[j % p.stages], (uint32_t)((j / p.stages) & 1));
-            break;
-        }
-        __syncwarp();  // orders lanes' byte copies of ragged tails
-        if (c == 0) g = locate(p, gw + (it / p.nchunks) * nwarps);
+        if (c == 0) g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
+        if (!mbar_wait_bounded(&done[s], (uint32_t)((it / p.stages) & 1))) break;
         int seg = 0, row = 0;
-        const bool valid = slot_row(p, g, slot, &seg, &row);
-        const int type = p.seg[seg].type;
-        if (c == 0) {
-            sum = 0.0f;
-            grp = 0.0f;
-            gpos = 0;
-            acc = (valid && p.seg[seg].bias) ? p.seg[seg].bias[row] : 0.0f;
-        }
-        // This lane's blocks of the chunk: j = c*C + sub + Lr*k.
-        const int cc = min(C, nb - c * C);  // blocks in this chunk (the last may be short)
-        float t[kMaxUnits];
-#pragma unroll
-        for (int k = 0; k < kMaxUnits; ++k) {
-            t[k] = 0.0f;
-            if (k < U && valid && !p.skip_compute && sub + Lr * k < cc) {
-                const int m = sub + Lr * k;
-                const int j = c * C + m;
-                if (kq) {
-                    const int bb = kq_block_bytes(type);
-                    const size_t off = (size_t)row * nb * bb + (size_t)c * C * bb;
-                    const uint8_t *blk = stage + slot * L.q_stride + (off & 15) + (size_t)m * bb;
-                    const uint8_t *aq = smem + L.act_q_off + j * kQ8kActStride;
-                    const uint8_t *am = smem + L.act_meta_off + j * kQ8kMetaStride;
-                    t[k] = type == OVF_TYPE_Q4_K ? q4k_unit(blk, aq, am) : q6k_unit(blk, aq, am);
-                } else {
-                    const size_t offq = (size_t)row * p.K + (size_t)c * C * 32;
-                    const size_t offs = (size_t)row * (p.K / 8) + (size_t)c * C * 4;
-                    const uint8_t *wq = stage + slot * L.q_stride + (offq & 15) + 32 * m;
-                    const float ws =
-                        *reinterpret_cast<const float *>(stage + L.s_region + slot * L.s_stride + (offs & 15) + 4 * m);
-                    t[k] = q80_unit(wq, ws, smem + L.act_q_off + j * kQ80ActStride);
-                }
+        const bool valid = lane < T && slot_row(p, g, lane, &seg, &row);
+        const int cc = min(C, nb - c * C);
+        const float *tb = tbuf + (size_t)s * T * C;
+        if (lane < T) {
+            if (c == 0) {
+                sum = 0.0f;
+                grp = 0.0f;
+                gpos = 0;
+                acc = (valid && p.seg[seg].bias) ? p.seg[seg].bias[row] : 0.0f;
             }
-        }
-        __syncwarp();
-        // Stage s is consumed: refill it with this warp's item it + stages.
-        {
-            const int nx = it + p.stages;
-            if (nx < items) {
-                fence_proxy_async_smem();
-                const GroupRef gn = locate(p, gw + (nx / p.nchunks) * nwarps);
-                issue_stage(p, L, gn, nx % p.nchunks, stage, &bars[s], pol, lane);
-            }
-        }
-        // Ascending block order within the row: the terms go through shared
-        // memory and the row's first lane adds them one by one (independent
-        // loads, then a chain of single fp32 adds).
-#pragma unroll
-        for (int k = 0; k < kMaxUnits; ++k)
-            if (k < U) wterms[slot * C + sub + Lr * k] = t[k];
-        __syncwarp();
-        if (sub == 0) {
-            const float *tr = wterms + slot * C;
+            const float *tr = tb + lane * C;
             for (int m = 0; m < cc; ++m) {
                 const float v = tr[m];
                 if (grouped) {
@@ -663,17 +766,26 @@ __global__ void __launch_bounds__(384, 1) gemv_kernel(const GemvParams p) {
             }
         }
         __syncwarp();
+        // The stage and its terms are consumed: refill with item it + stages.
+        const int nx = it + p.stages;
+        if (nx < items) {
+            if (lane == 0) fence_proxy_async_smem();
+            __syncwarp();
+            const GroupRef gn = locate(p, blockIdx.x + (nx / p.nchunks) * gridDim.x);
+            issue_stage(p, L, gn, nx % p.nchunks, ring + (size_t)s * L.stage_bytes, &full[s], pol, lane);
+        }
         if (c == p.nchunks - 1) {
             float y;
             if (grouped) y = acc;
             else y = (valid && p.seg[seg].bias) ? fadd(p.seg[seg].bias[row], sum) : sum;
             if (p.epi == EPI_SILU_PAIR) {
-                const float u = __shfl_down_sync(0xFFFFFFFFu, y, 16);
-                if (slot < p.rows_per_group && valid && sub == 0) {
+                const int half = T / 2;
+                const float u = __shfl_down_sync(0xFFFFFFFFu, y, half);
+                if (lane < half && valid) {
                     const float sg = fdiv(1.0f, fadd(1.0f, expf(-y)));
                     p.seg[0].out[row] = fmul(fmul(y, sg), u);
                 }
-            } else if (valid && sub == 0) {
+            } else if (valid) {
                 float *out = p.seg[seg].out;
                 if (p.epi == EPI_RESIDUAL) out[row] = fadd(p.resid[row], y);
                 else out[row] = y;
@@ -686,20 +798,15 @@ __global__ void __launch_bounds__(384, 1) gemv_kernel(const GemvParams p) {
     }
 
     if (p.epi == EPI_LOGITS_ARGMAX) {
-        // warp max -> CTA max -> one global atomic per CTA; the last CTA to
-        // finish turns the winning key into the next token.
+        // the row warp holds the CTA's rows: warp max -> one global atomic per
+        // CTA; the last CTA to finish turns the winning key into the next token.
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
             best = other > best ? other : best;
         }
-        unsigned long long *wbest = reinterpret_cast<unsigned long long *>(smem + L.red_off + 64 * sizeof(float));
-        if (lane == 0) wbest[warp] = best;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            unsigned long long b = 0;
-            for (int w = 0; w < W; ++w) b = wbest[w] > b ? wbest[w] : b;
-            atomicMax(&p.step->argmax_key, b);
+        if (lane == 0) {
+            atomicMax(&p.step->argmax_key, best);
             __threadfence();
             const int ticket = atomicAdd(&p.step->done_ctas, 1);
             if (ticket == (int)gridDim.x - 1) {
@@ -773,74 +880,52 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     const int nb = kq ? p.K / 256 : p.K / 32;
     if (!kq && p.q8_group <= 0) p.q8_group = nb;
     OVF_CHECK_ARG(kq || nb % p.q8_group == 0, "gemv: Q8_0 group must divide the block count");
-    int rows = 0;
-    for (int s = 0; s < p.nseg; ++s) rows += p.seg[s].rows;
-    if (p.pair) rows = p.seg[0].rows * 2;
-    // Lanes per row: enough row groups (32/L rows each) for ~7 warps per SM,
-    // since a warp's rows are its unit of latency hiding.  Blocks per lane:
-    // each row's chunk near 1 KB, one bulk copy (small copies starve the copy
-    // engine).  OVF_GEMV_LR / OVF_GEMV_U override for experiments.
-    const int bb = kq ? kq_block_bytes(type0) : 36;
-    // Lanes per row and blocks per lane (measured on B200 at the Llama-3-8B
-    // shapes): 8 lanes x 2 blocks, i.e. 4 rows per warp and 16 blocks
-    // (2.3-3.4 KB) per row copy; a short last chunk is allowed.
-    int Lr = 1;
-    while (Lr < 8 && 2 * Lr <= nb) Lr *= 2;
-    int U = std::max(1, std::min(2, (nb + Lr - 1) / Lr));
-    if (const char *e = getenv("OVF_GEMV_LR")) Lr = std::max(1, std::min(32, atoi(e)));
-    if (const char *e = getenv("OVF_GEMV_U")) U = std::max(1, std::min(kMaxUnits, atoi(e)));
-    p.lanes_per_row = Lr;
-    p.units_per_lane = U;
-    p.chunk = Lr * U;
-    p.nchunks = (nb + p.chunk - 1) / p.chunk;
-    p.rows_per_group = p.pair ? 16 / Lr : 32 / Lr;
+    // Whole-row tiles of T rows (~40 KB of weights, up to 16 rows; pair
+    // launches take T/2 gate + T/2 up rows): one bulk copy per matrix per
+    // stage.  OVF_GEMV_C selects the per-row chunked mode instead.
+    int T = 16, C = nb;
+    int rb = 0;
+    for (int s = 0; s < p.nseg; ++s) rb = std::max(rb, kq ? nb * kq_block_bytes(p.seg[s].type) : p.K + p.K / 8);
+    T = (int)std::max<int64_t>(1, std::min<int64_t>(16, (40 * 1024) / rb));
+    if (p.pair) T = std::max(2, T & ~1);
+    if (const char *e = getenv("OVF_GEMV_T")) T = std::max(1, std::min(32, atoi(e)));
+    if (const char *e = getenv("OVF_GEMV_C")) if (atoi(e) > 0) C = std::max(1, std::min(nb, atoi(e)));
+    p.copy_split = 1;
+    if (const char *e = getenv("OVF_GEMV_SPLIT")) p.copy_split = std::max(1, std::min(16, atoi(e)));
+    OVF_CHECK_ARG(T * C <= 32 * 128, "gemv: tile too large");
+    p.rows_per_group = T;
+    p.chunk = C;
+    p.nchunks = (nb + C - 1) / C;
+    p.lanes_per_row = 1;
+    p.units_per_lane = 1;
+    const int rows_per = p.pair ? T / 2 : T;
     int total = 0;
     for (int s = 0; s < p.nseg; ++s) {
-        p.seg[s].groups = (p.seg[s].rows + p.rows_per_group - 1) / p.rows_per_group;
+        p.seg[s].groups = (p.seg[s].rows + rows_per - 1) / rows_per;
         if (!p.pair) total += p.seg[s].groups;
     }
     if (p.pair) total = p.seg[0].groups;
     p.total_groups = total;
     if (total == 0) return OVF_OK;
 
-    // One persistent CTA per SM; each warp has a private ring.  Prefer deep
-    // rings (bytes in flight) while keeping >= 8 warps when the work allows.
     const int budget = smem_optin(device) - 1024;
     const int grid = std::min(nsm, total);
-    const int want = std::min(12, (total + grid - 1) / grid);
-    int warps = 0, stages = 0;
+    const int warps = kComputeWarps + 1;
+    int stages = 0;
     size_t smem = 0;
-    int s_hi = 6, s_lo = 2, w_force = 0;
+    int s_hi = 6, s_lo = 2;
     if (const char *e = getenv("OVF_GEMV_S")) s_hi = s_lo = std::max(2, std::min(8, atoi(e)));
-    if (const char *e = getenv("OVF_GEMV_W")) w_force = std::max(1, std::min(12, atoi(e)));
     if (const char *e = getenv("OVF_GEMV_SKIP")) p.skip_compute = atoi(e);
-    // Warps per CTA: balance the row groups over the warps (a warp's last
-    // group sets the kernel's end), then the deepest ring that fits.
-    double best_eff = -1.0;
-    const int w_lo = w_force ? w_force : std::max(1, std::min(want, 6));
-    for (int w = w_force ? w_force : want; w >= w_lo; --w) {
-        p.stages = s_lo;
-        if (layout_smem(make_layout(p, w), s_lo, w) > (size_t)budget) continue;
-        const int64_t slots = (int64_t)grid * w;
-        const int64_t rounds = (total + slots - 1) / slots;
-        const double eff = (double)total / (double)(slots * rounds);
-        if (eff > best_eff + 1e-3) {
-            best_eff = eff;
-            warps = w;
+    for (int S = s_hi; S >= s_lo; --S) {
+        p.stages = S;
+        const Layout L = make_layout(p);
+        if (layout_smem(L, S) <= (size_t)budget) {
+            stages = S;
+            smem = layout_smem(L, S);
+            break;
         }
     }
-    if (warps) {
-        for (int S = s_hi; S >= s_lo; --S) {
-            p.stages = S;
-            const Layout L = make_layout(p, warps);
-            if (layout_smem(L, S, warps) <= (size_t)budget) {
-                stages = S;
-                smem = layout_smem(L, S, warps);
-                break;
-            }
-        }
-    }
-    OVF_CHECK_ARG(warps >= 1, "gemv: K=%d does not fit shared memory", p.K);
+    OVF_CHECK_ARG(stages >= 2, "gemv: K=%d does not fit shared memory", p.K);
     p.stages = stages;
     static bool attr_done[64] = {false};
     if (device < 64 && !attr_done[device]) {
@@ -848,7 +933,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
                                           smem_optin(device)));
         attr_done[device] = true;
     }
-    if (plan_out) *plan_out = GemvPlan{Lr, p.chunk, stages, warps, grid, smem};
+    if (plan_out) *plan_out = GemvPlan{T, p.chunk, stages, warps, grid, smem};
     cudaError_t e = launch_pdl(gemv_kernel, dim3(grid), dim3(warps * 32), smem, stream, pdl, p);
     if (e != cudaSuccess) return cuda_status(e, "gemv_kernel launch");
     return OVF_OK;

@@ -64,6 +64,7 @@ struct GemvParams {
     int pair;            // EPI_SILU_PAIR: seg0 = gate, seg1 = up, same row groups
     int total_groups;
     int skip_compute;    // experiments only: stream the weights, contract nothing
+    int copy_split;      // bulk copies per matrix part of a whole-row stage
     const float *x;
     const float *gamma;
     float eps;
