@@ -68,7 +68,7 @@ static ovf_status check_kq(int32_t type, const void *w, int64_t n, int64_t k) {
     OVF_CHECK_ARG(type == OVF_TYPE_Q4_K || type == OVF_TYPE_Q6_K, "projection: type %d is not a K-quant", type);
     OVF_CHECK_ARG(n >= 0 && n <= 0x7FFFFFFF, "projection: bad output size");
     OVF_CHECK_ARG(k > 0 && k % 256 == 0, "projection: inputSize %lld must be a multiple of 256", (long long)k);
-    OVF_CHECK_ARG(k <= 256 * 512, "projection: inputSize %lld too large", (long long)k);
+    OVF_CHECK_ARG(k <= 32768, "projection: inputSize %lld too large (at most 32768)", (long long)k);
     OVF_CHECK_ARG(w && aligned16(w), "projection: weight must be non-null and 16-byte aligned");
     return OVF_OK;
 }

@@ -1,27 +1,32 @@
 // ovf_gemv.cu — quantized decode GEMV for sm_100a (see ovf_gemv.cuh).
 //
-// Work decomposition ("lanes own rows").  A warp owns a group of 32/L
-// consecutive weight rows; L lanes (1, 2 or 4) share a row.  The warp streams
-// its rows through a private ring of shared-memory stages, C blocks of every
-// row per stage: each row's chunk is one 1-D bulk copy (the TMA engine) issued
-// by the row's first lane, so every stage is 32/L independent contiguous
-// copies landing on one mbarrier.  The first stages are requested before
-// griddepcontrol.wait, while the previous kernel of the decode step is still
-// finishing (programmatic dependent launch).
+// Work decomposition.  The rows of a launch (up to three weight segments,
+// e.g. Q/K/V, or a gate/up pair) are cut into tiles of T whole rows; each
+// CTA (one per SM, persistent) takes tiles blockIdx.x, blockIdx.x + grid, ...
+// A tile's rows are contiguous in HBM, so one 1-D bulk copy (the TMA engine)
+// per matrix part fills a shared-memory stage; a ring of stages keeps
+// several copies in flight.  A dedicated producer thread does nothing but
+// wait for a free stage and issue its copies, so the copy engine is never
+// starved by arithmetic; the first stages are requested before
+// griddepcontrol.wait, while the previous kernel of the decode step is
+// still finishing (programmatic dependent launch).
 //
-// Because a lane group owns whole rows, every lane contracts the same
-// activation block at the same time (shared-memory broadcast), and the row's
-// block terms are accumulated in registers in ascending block order — the
-// reference's sequential fp32 loop (Runtime/Q4KDotKernel.cs:528-552,
-// Q6KDotKernel.cs:364-380, Q8DotKernel.cs:311-328) — with no reduction pass.
-// Integer parts are exact and the fp32 tails use explicitly rounded ops in
-// the reference's operand order, so results are bit-identical to it.
+// Six compute warps contract a stage with dp4a: one thread per (row,
+// block), each thread holding the quantized activation of its block (Q8_K
+// or Q8_0, quantized in the prologue, optionally after RMSNorm) in
+// registers for the whole launch.  A sum warp then adds each row's terms in
+// ascending block order — the reference's sequential fp32 loop
+// (Runtime/Q4KDotKernel.cs:528-552, Q6KDotKernel.cs:364-380,
+// Q8DotKernel.cs:311-328) — and runs the fused epilogue, overlapped with
+// the next tiles' contraction.  Integer parts are exact and the fp32 tails
+// use explicitly rounded ops in the reference's operand order, so results
+// are bit-identical to it.
 //
-// Chunks are copied from the 16-byte boundary at or below their first byte
-// (Q6_K blocks are 210 bytes), so a block may start 4/8/12 bytes into its
-// smem row; the Q6_K unit reads through a funnel shift.  A copy that would
-// run past the end of the weight buffer stops at the last 16-byte boundary
-// and its last few bytes are copied by the lane itself.
+// Spans are copied from the 16-byte boundary at or below their first byte
+// (Q6_K blocks are 210 bytes), so a row may start 4/8/12 bytes into its
+// stage; the Q6_K unit reads through a funnel shift.  A copy that would run
+// past the end of the weight buffer stops at the last 16-byte boundary and
+// its last few bytes are stored by the producer thread itself.
 #include "ovf_gemv.cuh"
 
 #include <algorithm>
@@ -33,7 +38,7 @@ namespace ovf {
 static constexpr int kQ8kActStride = 272;  // 256 quants + 16 pad
 static constexpr int kQ8kMetaStride = 64;  // int16 bsums[16] | f32 scale | pad | int16 pair sums[8]
 static constexpr int kQ80ActStride = 48;   // 32 quants + f32 scale + pad
-static constexpr int kMaxUnits = 4;        // blocks per lane per chunk
+static constexpr int kTermBufs = 4;        // term buffers between the compute warps and the sum warp
 
 int block_bytes(int type) {
     switch (type) {
@@ -48,32 +53,31 @@ static __host__ __device__ inline bool is_kquant(int t) { return t == OVF_TYPE_Q
 static __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 static __host__ __device__ inline int kq_block_bytes(int type) { return type == OVF_TYPE_Q4_K ? 144 : 210; }
 
-// Row stride in shared memory for a copied span of `bytes` that may start up
-// to 15 bytes before its data: an odd number of 16-byte units, so the lanes'
-// 16-byte reads of 8 consecutive rows fall in distinct banks.
-static __host__ __device__ inline int smem_stride(int bytes) {
-    int s = (int)align_up((size_t)bytes + 30, 16);
-    if (((s / 16) & 1) == 0) s += 16;
-    return s;
-}
-
 struct Layout {
     int act_q_off, act_meta_off, red_off, terms_off, stage_off;
-    int stage_bytes, q_stride, s_stride, s_region;  // Q8_0: quants rows then scales rows
-    int part_bytes, s_part;                         // whole-row stages: bytes per matrix part
-    int nb;
+    int stage_bytes;
+    int part_bytes;  // quants of one matrix part of a stage (16 bytes of slack for an unaligned start)
+    int s_region;    // Q8_0: offset of the scales parts in a stage
+    int s_part;      // Q8_0: scales of one matrix part
+    int nb;          // blocks per row
 };
 
-// Shared memory: mbarriers | activation | reduction scratch | two term
-// buffers [T][C] | stage ring.  Stage rows are sized for the launch's
-// largest block (K-quant launches may mix Q4_K and Q6_K rows).
+// Shared memory: mbarriers | activation | reduction scratch | kTermBufs
+// term buffers [T][nb] | stage ring.  A stage holds one tile: the tile's rows of
+// each matrix part (pair launches: gate part, up part), copied as one
+// contiguous span each; Q8_0 stages append the parts' fp32 scale spans.
+// Parts are sized for the launch's largest row (K-quant launches may mix
+// Q4_K and Q6_K segments).
+static __host__ __device__ inline int row_bytes(int type, int K) {
+    return is_kquant(type) ? (K / 256) * kq_block_bytes(type) : K;
+}
+
 static __host__ __device__ inline Layout make_layout(const GemvParams &p) {
     Layout L{};
-    const int type0 = p.seg[0].type;
-    const bool kq = is_kquant(type0);
+    const bool kq = is_kquant(p.seg[0].type);
     L.nb = kq ? p.K / 256 : p.K / 32;
     const int T = p.rows_per_group;
-    size_t off = align_up(sizeof(uint64_t) * 2 * p.stages, 128);
+    size_t off = align_up(sizeof(uint64_t) * (2 * p.stages + 2 * kTermBufs) + 16, 128);
     L.act_q_off = (int)off;
     if (kq) {
         off = align_up(off + (size_t)L.nb * kQ8kActStride, 128);
@@ -86,41 +90,15 @@ static __host__ __device__ inline Layout make_layout(const GemvParams &p) {
     L.red_off = (int)off;
     off = align_up(off + 64 * sizeof(float) + 32 * sizeof(unsigned long long), 128);
     L.terms_off = (int)off;
-    off = align_up(off + (size_t)p.stages * T * p.chunk * sizeof(float), 128);
+    off = align_up(off + (size_t)kTermBufs * T * L.nb * sizeof(float), 128);
     L.stage_off = (int)off;
-    if (p.chunk == L.nb) {
-        // Whole rows: a tile's rows are contiguous in the weight buffer, so a
-        // stage is one copy per matrix (quants and scales for Q8_0).
-        const int parts = p.pair ? 2 : 1, per = T / parts;
-        if (kq) {
-            int rb = 0;
-            for (int s = 0; s < p.nseg; ++s) rb = max(rb, L.nb * kq_block_bytes(p.seg[s].type));
-            L.q_stride = rb;
-            L.part_bytes = (int)align_up((size_t)per * rb + 16, 16);
-            L.s_stride = 0;
-            L.s_part = 0;
-            L.s_region = parts * L.part_bytes;
-        } else {
-            L.q_stride = p.K;
-            L.part_bytes = (int)align_up((size_t)per * p.K + 16, 16);
-            L.s_stride = p.K / 8;
-            L.s_part = (int)align_up((size_t)per * (p.K / 8) + 16, 16);
-            L.s_region = parts * L.part_bytes;
-        }
-        L.stage_bytes = (int)align_up((size_t)L.s_region + (size_t)parts * L.s_part, 128);
-    } else if (kq) {
-        int mx = 0;
-        for (int s = 0; s < p.nseg; ++s) mx = max(mx, smem_stride(p.chunk * kq_block_bytes(p.seg[s].type)));
-        L.q_stride = mx;
-        L.s_stride = 0;
-        L.s_region = 0;
-        L.stage_bytes = (int)align_up((size_t)T * mx, 128);
-    } else {
-        L.q_stride = smem_stride(32 * p.chunk);
-        L.s_stride = smem_stride(4 * p.chunk);
-        L.s_region = T * L.q_stride;
-        L.stage_bytes = (int)align_up((size_t)T * (L.q_stride + L.s_stride), 128);
-    }
+    const int parts = p.pair ? 2 : 1, per = T / parts;
+    int rb = 0;
+    for (int s = 0; s < p.nseg; ++s) rb = max(rb, row_bytes(p.seg[s].type, p.K));
+    L.part_bytes = (int)align_up((size_t)per * rb + 16, 16);
+    L.s_region = parts * L.part_bytes;
+    L.s_part = kq ? 0 : (int)align_up((size_t)per * (p.K / 8) + 16, 16);
+    L.stage_bytes = (int)align_up((size_t)L.s_region + (size_t)parts * L.s_part, 128);
     return L;
 }
 
@@ -129,10 +107,53 @@ static __host__ __device__ inline size_t layout_smem(const Layout &L, int stages
 }
 
 // ------------------------------------------------------------- dot units
+// One thread contracts one block of a row: a K-quant super-block (256
+// weights) or a Q8_0 block (32).  A thread keeps the activation of its
+// block in registers for the whole launch (the activation is the same for
+// every row), so a row costs only its weight bytes from shared memory.  The
+// integer parts are exact and the fp32 tail of every block follows the
+// reference's operand order.
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
 
+struct KqAct {        // Q8_K block: 256 quants, 16-element sums, scale
+    uint32_t q[64];
+    uint32_t bs[8];   // int16 pairs: sums (2i, 2i+1) of 16 elements
+    float s;
+};
+struct Q8Act {        // Q8_0 block: 32 quants + scale
+    uint32_t q[8];
+    float s;
+};
+
+__device__ __forceinline__ void load_kq_act(const uint8_t *aq, const uint8_t *meta, KqAct &a) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(aq + 16 * i);
+        a.q[4 * i] = v.x;
+        a.q[4 * i + 1] = v.y;
+        a.q[4 * i + 2] = v.z;
+        a.q[4 * i + 3] = v.w;
+    }
+    const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
+    const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
+    a.bs[0] = b0.x; a.bs[1] = b0.y; a.bs[2] = b0.z; a.bs[3] = b0.w;
+    a.bs[4] = b1.x; a.bs[5] = b1.y; a.bs[6] = b1.z; a.bs[7] = b1.w;
+    a.s = *reinterpret_cast<const float *>(meta + 32);
+}
+
+__device__ __forceinline__ void load_q8_act(const uint8_t *act, Q8Act &a) {
+    const uint4 v0 = *reinterpret_cast<const uint4 *>(act);
+    const uint4 v1 = *reinterpret_cast<const uint4 *>(act + 16);
+    a.q[0] = v0.x; a.q[1] = v0.y; a.q[2] = v0.z; a.q[3] = v0.w;
+    a.q[4] = v1.x; a.q[5] = v1.y; a.q[6] = v1.z; a.q[7] = v1.w;
+    a.s = *reinterpret_cast<const float *>(act + 32);
+}
+
+__device__ __forceinline__ int lo16(uint32_t w) { return (int)(int16_t)(w & 0xFFFFu); }
+__device__ __forceinline__ int hi16(uint32_t w) { return (int)(int16_t)(w >> 16); }
+
 // Q4_K x Q8_K over one super-block (Runtime/Q4KDotKernel.cs:216-256).
-__device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8, const uint8_t *meta) {
+__device__ __forceinline__ float q4k_block(const uint8_t *blk, const KqAct &a) {
     const uint4 h = *reinterpret_cast<const uint4 *>(blk);
     const float d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
     const float dmin = h2f_bits((uint16_t)(h.x >> 16));
@@ -145,55 +166,56 @@ __device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8,
     for (int p = 0; p < 4; ++p) {
         const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
         const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
-        const uint4 l0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p);
-        const uint4 l1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 16);
-        const uint4 h0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 32);
-        const uint4 h1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 48);
+        const uint32_t *l0 = a.q + 16 * p, *l1 = l0 + 4, *h0 = l0 + 8, *h1 = l0 + 12;
         const uint32_t M = 0x0F0F0F0Fu, HM = 0xF0F0F0F0u;
-        // High nibbles stay in place (16 * nibble as the unsigned operand):
+        // High nibbles stay in place (16 x nibble as the unsigned operand):
         // that sum is 16x the nibble dot and is divided out exactly below.
-        int lo = dp4a((int)(qa.x & M), (int)l0.x, 0);
-        int lo2 = dp4a((int)(qb.x & M), (int)l1.x, 0);
-        int hi = dp4a_us(qa.x & HM, (int)h0.x, 0);
-        int hi2 = dp4a_us(qb.x & HM, (int)h1.x, 0);
-        lo = dp4a((int)(qa.y & M), (int)l0.y, lo);
-        lo2 = dp4a((int)(qb.y & M), (int)l1.y, lo2);
-        hi = dp4a_us(qa.y & HM, (int)h0.y, hi);
-        hi2 = dp4a_us(qb.y & HM, (int)h1.y, hi2);
-        lo = dp4a((int)(qa.z & M), (int)l0.z, lo);
-        lo2 = dp4a((int)(qb.z & M), (int)l1.z, lo2);
-        hi = dp4a_us(qa.z & HM, (int)h0.z, hi);
-        hi2 = dp4a_us(qb.z & HM, (int)h1.z, hi2);
-        lo = dp4a((int)(qa.w & M), (int)l0.w, lo);
-        lo2 = dp4a((int)(qb.w & M), (int)l1.w, lo2);
-        hi = dp4a_us(qa.w & HM, (int)h0.w, hi);
-        hi2 = dp4a_us(qb.w & HM, (int)h1.w, hi2);
+        int lo = dp4a((int)(qa.x & M), (int)l0[0], 0);
+        int lo2 = dp4a((int)(qb.x & M), (int)l1[0], 0);
+        int hi = dp4a_us(qa.x & HM, (int)h0[0], 0);
+        int hi2 = dp4a_us(qb.x & HM, (int)h1[0], 0);
+        lo = dp4a((int)(qa.y & M), (int)l0[1], lo);
+        lo2 = dp4a((int)(qb.y & M), (int)l1[1], lo2);
+        hi = dp4a_us(qa.y & HM, (int)h0[1], hi);
+        hi2 = dp4a_us(qb.y & HM, (int)h1[1], hi2);
+        lo = dp4a((int)(qa.z & M), (int)l0[2], lo);
+        lo2 = dp4a((int)(qb.z & M), (int)l1[2], lo2);
+        hi = dp4a_us(qa.z & HM, (int)h0[2], hi);
+        hi2 = dp4a_us(qb.z & HM, (int)h1[2], hi2);
+        lo = dp4a((int)(qa.w & M), (int)l0[3], lo);
+        lo2 = dp4a((int)(qb.w & M), (int)l1[3], lo2);
+        hi = dp4a_us(qa.w & HM, (int)h0[3], hi);
+        hi2 = dp4a_us(qb.w & HM, (int)h1[3], hi2);
         const uint32_t scw = p < 2 ? sc03 : sc47;
         mainAcc += (int)byte_of(scw, (2 * p) & 3) * (lo + lo2);
         mainAccH += (int)byte_of(scw, (2 * p + 1) & 3) * (hi + hi2);
     }
     mainAcc += mainAccH >> 4;
-    // min correction: sum_s m[s] * (bsum[2s] + bsum[2s+1]) as four dp2a
-    const uint4 ps = *reinterpret_cast<const uint4 *>(meta + 48);
-    const float q8s = *reinterpret_cast<const float *>(meta + 32);
-    int minAcc = __dp2a_lo((int)ps.x, (int)mn03, 0);
-    minAcc = __dp2a_hi((int)ps.y, (int)mn03, minAcc);
-    minAcc = __dp2a_lo((int)ps.z, (int)mn47, minAcc);
-    minAcc = __dp2a_hi((int)ps.w, (int)mn47, minAcc);
-    return fmul(q8s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
+    // min correction: sum_s m[s] * (sum of the sub-block's 32 activations)
+    int minAcc = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        const uint32_t mw = s < 4 ? mn03 : mn47;
+        const int ps = lo16(a.bs[s]) + hi16(a.bs[s]);
+        minAcc += (int)byte_of(mw, s & 3) * ps;
+    }
+    return fmul(a.s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
 }
 
-// 32-bit word `w` of a 210-byte block that may start 2 bytes past a word.
+// 32-bit word `w` of a block that may start 2 bytes past a word boundary.
 __device__ __forceinline__ uint32_t ldw_shifted(const uint32_t *base, int w, int sh) {
     return __funnelshift_r(base[w], base[w + 1], sh);
 }
 
 // Q6_K x Q8_K over one super-block (Runtime/Q6KDotKernel.cs:77-121 with the
-// unsigned dot :186-215).
-__device__ __forceinline__ float q6k_unit(const uint8_t *blk, const uint8_t *q8, const uint8_t *meta) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
-    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    const int sh = (int)(a & 3u) * 8;
+// unsigned dot :186-215): weight (k, l) of half h is ql[l + 32(k&1)] (low
+// nibble for k < 2, high for k >= 2) with qh[l] bits 2k..2k+1 and scale
+// sc[8h + l/16 + 2k]; the unsigned 6-bit dot minus 32 x the scaled
+// 16-element activation sums gives the signed dot exactly.
+__device__ __forceinline__ float q6k_block(const uint8_t *blk, const KqAct &a) {
+    const uintptr_t ad = reinterpret_cast<uintptr_t>(blk);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(ad & ~uintptr_t(3));
+    const int sh = (int)(ad & 3u) * 8;
     int sc[16];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -202,7 +224,6 @@ __device__ __forceinline__ float q6k_unit(const uint8_t *blk, const uint8_t *q8,
         for (int j = 0; j < 4; ++j) sc[4 * i + j] = (int)(int8_t)byte_of(w, j);
     }
     const float d = h2f_bits((uint16_t)(ldw_shifted(base, 52, sh) & 0xFFFFu));
-    const uint32_t *q8w = reinterpret_cast<const uint32_t *>(q8);
     int sum = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -217,42 +238,33 @@ __device__ __forceinline__ float q6k_unit(const uint8_t *blk, const uint8_t *q8,
             const int q3 = (int)(((qla >> 4) & M) | (qhw & H));
             const int q4 = (int)(((qlb >> 4) & M) | ((qhw >> 2) & H));
             const int is = lw >> 2;
-            const int base8 = 32 * h + lw;
-            sum += sc[8 * h + is] * dp4a(q1, (int)q8w[base8], 0) + sc[8 * h + is + 2] * dp4a(q2, (int)q8w[base8 + 8], 0) +
-                   sc[8 * h + is + 4] * dp4a(q3, (int)q8w[base8 + 16], 0) +
-                   sc[8 * h + is + 6] * dp4a(q4, (int)q8w[base8 + 24], 0);
+            const int b8 = 32 * h + lw;
+            sum += sc[8 * h + is] * dp4a(q1, (int)a.q[b8], 0) + sc[8 * h + is + 2] * dp4a(q2, (int)a.q[b8 + 8], 0) +
+                   sc[8 * h + is + 4] * dp4a(q3, (int)a.q[b8 + 16], 0) +
+                   sc[8 * h + is + 6] * dp4a(q4, (int)a.q[b8 + 24], 0);
         }
     }
-    const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
-    const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
-    const float q8s = *reinterpret_cast<const float *>(meta + 32);
-    const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
     int bsumTerm = 0;
 #pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        bsumTerm += sc[2 * s] * (int)(int16_t)(bw[s] & 0xFFFFu) + sc[2 * s + 1] * (int)(int16_t)(bw[s] >> 16);
-    }
+    for (int s = 0; s < 8; ++s) bsumTerm += sc[2 * s] * lo16(a.bs[s]) + sc[2 * s + 1] * hi16(a.bs[s]);
     const int mainAcc = sum - 32 * bsumTerm;
-    return fmul(fmul(d, q8s), i2f(mainAcc));
+    return fmul(fmul(d, a.s), i2f(mainAcc));
 }
 
 // Q8_0 x Q8_0 over one 32-block (Runtime/Q8DotKernel.cs:99-140).
-__device__ __forceinline__ float q80_unit(const uint8_t *wq, float ws, const uint8_t *act) {
+__device__ __forceinline__ float q80_block(const uint8_t *wq, float ws, const Q8Act &a) {
     const uint4 w0 = *reinterpret_cast<const uint4 *>(wq);
     const uint4 w1 = *reinterpret_cast<const uint4 *>(wq + 16);
-    const uint4 a0 = *reinterpret_cast<const uint4 *>(act);
-    const uint4 a1 = *reinterpret_cast<const uint4 *>(act + 16);
-    const float xs = *reinterpret_cast<const float *>(act + 32);
     int dot = 0;
-    dot = dp4a((int)w0.x, (int)a0.x, dot);
-    dot = dp4a((int)w0.y, (int)a0.y, dot);
-    dot = dp4a((int)w0.z, (int)a0.z, dot);
-    dot = dp4a((int)w0.w, (int)a0.w, dot);
-    dot = dp4a((int)w1.x, (int)a1.x, dot);
-    dot = dp4a((int)w1.y, (int)a1.y, dot);
-    dot = dp4a((int)w1.z, (int)a1.z, dot);
-    dot = dp4a((int)w1.w, (int)a1.w, dot);
-    return fmul(fmul(ws, xs), i2f(dot));
+    dot = dp4a((int)w0.x, (int)a.q[0], dot);
+    dot = dp4a((int)w0.y, (int)a.q[1], dot);
+    dot = dp4a((int)w0.z, (int)a.q[2], dot);
+    dot = dp4a((int)w0.w, (int)a.q[3], dot);
+    dot = dp4a((int)w1.x, (int)a.q[4], dot);
+    dot = dp4a((int)w1.y, (int)a.q[5], dot);
+    dot = dp4a((int)w1.z, (int)a.q[6], dot);
+    dot = dp4a((int)w1.w, (int)a.q[7], dot);
+    return fmul(fmul(ws, a.s), i2f(dot));
 }
 
 // --------------------------------------------------------- activation prep
@@ -505,321 +517,310 @@ __device__ __forceinline__ bool slot_row(const GemvParams &p, const GroupRef &g,
     return slot < g.nr;
 }
 
-// Copies bytes [off, off+len) of `src` (total `total` bytes) so that they sit
-// at dst + (off & 15): the bulk engine moves whole 16-byte units, the lane
-// itself the bytes past the buffer's last 16-byte boundary.  Returns the bulk
-// bytes (for the stage's transaction count); `issue` false only counts.
+// Stages bytes [off, off+len) of `src` (a buffer of `total` bytes) at
+// dst + (off & 15).  The bulk engine moves the whole 16-byte units from the
+// boundary at or below `off`; the bytes past the buffer's last 16-byte
+// boundary (only a segment's final tile can have them) are stored by the
+// thread itself.  `bulk` false: store those tail bytes and return the bulk
+// byte count; `bulk` true: issue the bulk copy.
 __device__ __forceinline__ uint32_t copy_span(uint8_t *dst, const uint8_t *src, size_t off, size_t len, size_t total,
-                                              uint64_t *bar, uint64_t pol, bool issue) {
+                                              uint64_t *bar, uint64_t pol, bool bulk) {
     const size_t a = off & ~size_t(15);
     const size_t e = min(align_up(off + len, 16), total);
     const size_t be = e & ~size_t(15);
-    const uint32_t bulk = be > a ? (uint32_t)(be - a) : 0u;
-    if (issue) {
-        if (bulk) bulk_g2s(dst, src + a, bulk, bar, pol);
+    const uint32_t n = be > a ? (uint32_t)(be - a) : 0u;
+    if (!bulk) {
         for (size_t i = max(a, be); i < e; ++i) dst[i - a] = src[i];
+    } else if (n) {
+        bulk_g2s(dst, src + a, n, bar, pol);
     }
-    return bulk;
+    return n;
 }
 
-// Issued by warp 0: chunk `c` of every row of tile `g`, one copy per row
-// (two for Q8_0: quants and scales), lane i copying row slot i.
-__device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L, const GroupRef &g, int c,
-                                            uint8_t *stage, uint64_t *bar, uint64_t pol, int lane) {
-    if (p.chunk == L.nb) {
-        // Whole rows: lane `part` copies the tile's rows of its matrix.
-        const int parts = p.pair ? 2 : 1;
-        const GemvSeg &sg = p.seg[p.pair ? min(lane, 1) : g.seg];
-        uint32_t bytes = 0;
-        const bool mine = lane < parts && g.nr > 0;
-        for (int pass = 0; pass < 2; ++pass) {
-            const bool issue = pass == 1;
-            if (issue) {
-                const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, bytes);
-                if (lane == 0) mbar_arrive_expect_tx(bar, total);
-                __syncwarp();
-            }
-            if (!mine) continue;
-            if (is_kquant(sg.type)) {
-                // The part is cut into `split` copies issued by consecutive
-                // lanes: more copies in flight keep more DRAM requests open.
-                const size_t rb = (size_t)L.nb * kq_block_bytes(sg.type);
-                const size_t off = (size_t)g.r0 * rb, len = (size_t)g.nr * rb;
-                const size_t a0 = off & ~size_t(15);
-                const size_t piece = align_up((len + (off - a0) + p.copy_split - 1) / p.copy_split, 16);
-                bytes = 0;
-                for (int q = 0; q < p.copy_split; ++q) {
-                    const size_t ps = a0 + q * piece;
-                    if (ps >= off + len) break;
-                    const size_t s0 = q == 0 ? off : ps;
-                    const size_t e0 = min(off + len, ps + piece);
-                    bytes += copy_span(stage + lane * L.part_bytes + (s0 - a0) - (s0 & 15), sg.w, s0, e0 - s0,
-                                       (size_t)sg.rows * rb, bar, pol, issue);
-                }
-            } else {
-                const size_t K = p.K;
-                const uint32_t b1 = copy_span(stage + lane * L.part_bytes, sg.w, (size_t)g.r0 * K, (size_t)g.nr * K,
-                                              (size_t)sg.rows * K, bar, pol, issue);
-                const uint32_t b2 = copy_span(stage + L.s_region + lane * L.s_part,
-                                              reinterpret_cast<const uint8_t *>(sg.ws), (size_t)g.r0 * (K / 8),
-                                              (size_t)g.nr * (K / 8), (size_t)sg.rows * (K / 8), bar, pol, issue);
-                bytes = b1 + b2;
-            }
-        }
-        return;
-    }
-    const int slot = lane;
-    int seg = 0, row = 0;
-    const bool mine = slot < p.rows_per_group && slot_row(p, g, slot, &seg, &row);
+// Fills one stage with tile `g`; run by the producer thread alone.  Pass 0
+// stores the tail bytes and counts the bulk bytes, the arrive (which
+// releases those stores) announces the transaction count, pass 1 issues the
+// copies.
+__device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L, const GroupRef &g, uint8_t *stage,
+                                            uint64_t *bar, uint64_t pol) {
+    const int parts = p.pair ? 2 : 1;
     uint32_t bytes = 0;
-    const GemvSeg &sg = p.seg[seg];
-    const int type = sg.type;
-    const int nbk = is_kquant(type) ? p.K / 256 : p.K / 32;
-    const int cc = min(p.chunk, nbk - c * p.chunk);  // the last chunk may be short
     for (int pass = 0; pass < 2; ++pass) {
-        const bool issue = pass == 1;
-        if (issue) {
-            const uint32_t total = __reduce_add_sync(0xFFFFFFFFu, bytes);
-            if (lane == 0) mbar_arrive_expect_tx(bar, total);
-            __syncwarp();
+        const bool bulk = pass == 1;
+        for (int part = 0; part < parts && g.nr > 0; ++part) {
+            const GemvSeg &sg = p.seg[p.pair ? part : g.seg];
+            const size_t rb = (size_t)row_bytes(sg.type, p.K);
+            bytes += copy_span(stage + part * L.part_bytes, sg.w, (size_t)g.r0 * rb, (size_t)g.nr * rb,
+                               (size_t)sg.rows * rb, bar, pol, bulk);
+            if (!is_kquant(sg.type)) {
+                const size_t sb = (size_t)(p.K / 8);
+                bytes += copy_span(stage + L.s_region + part * L.s_part, reinterpret_cast<const uint8_t *>(sg.ws),
+                                   (size_t)g.r0 * sb, (size_t)g.nr * sb, (size_t)sg.rows * sb, bar, pol, bulk);
+            }
         }
-        if (!mine) continue;
-        if (is_kquant(type)) {
-            const int bb = kq_block_bytes(type);
-            const size_t rb = (size_t)nbk * bb;
-            const size_t off = (size_t)row * rb + (size_t)c * p.chunk * bb;
-            bytes = copy_span(stage + slot * L.q_stride, sg.w, off, (size_t)cc * bb, (size_t)sg.rows * rb, bar, pol,
-                              issue);
-        } else {
-            const size_t K = p.K;
-            const size_t offq = (size_t)row * K + (size_t)c * p.chunk * 32;
-            const size_t offs = (size_t)row * (K / 8) + (size_t)c * p.chunk * 4;
-            const uint32_t b1 = copy_span(stage + slot * L.q_stride, sg.w, offq, (size_t)cc * 32, (size_t)sg.rows * K,
-                                          bar, pol, issue);
-            const uint32_t b2 =
-                copy_span(stage + L.s_region + slot * L.s_stride, reinterpret_cast<const uint8_t *>(sg.ws), offs,
-                          (size_t)cc * 4, (size_t)sg.rows * (K / 8), bar, pol, issue);
-            bytes = b1 + b2;
-        }
+        if (!bulk) mbar_arrive_expect_tx(bar, bytes);
     }
 }
 
 // ------------------------------------------------------------------ kernel
-// A CTA owns T-row tiles (persistent, tile = blockIdx.x + i*gridDim.x) and
-// streams each through a ring of `stages` shared-memory buffers, C blocks of
-// every row per stage.  Warp specialisation: the last warp issues the bulk
-// copies and keeps the ordered row sums; the other (compute) warps contract
-// each stage (thread -> row slot and block, so the lanes of a warp read at
-// most two activation blocks) into the stage's [T][C] term buffer and
-// arrive on the stage's `done` mbarrier.  The row warp then adds row r's
-// terms in ascending block order (lane r), refills the stage and, after a
-// row's last chunk, runs the epilogue.  No CTA-wide barrier sits in the loop.
-static constexpr int kComputeWarps = 8;
+// A CTA owns T-row tiles (persistent: tile = blockIdx.x + i * gridDim.x) and
+// streams each through a ring of `stages` shared-memory buffers.  Three
+// warp roles run decoupled, linked only by mbarriers:
+//   producer (last warp, one lane): waits for a free stage, issues its bulk
+//     copies, nothing else — the copy engine is never starved by arithmetic;
+//   compute warps: contract a stage into a [T][nb] term buffer (one thread
+//     per (row, block)), release the stage and hand the terms on;
+//   sum warp: lane r adds row slot r's terms in ascending block order — the
+//     reference's sequential fp32 loop — and runs the epilogue, while the
+//     compute warps already work on the next tiles (kTermBufs buffers).
+static constexpr int kComputeWarps = 6;
+static constexpr int kComputeThreads = kComputeWarps * 32;
+static constexpr int kSumWarp = kComputeWarps;
+static constexpr int kProducerWarp = kComputeWarps + 1;
+static constexpr int kThreads = (kComputeWarps + 2) * 32;
 
-__global__ void __launch_bounds__((kComputeWarps + 1) * 32, 1) gemv_kernel(const GemvParams p) {
+struct Bars {
+    uint64_t *full, *empty, *tready, *tfree;
+    volatile int *abort_flag;
+};
+
+__device__ __forceinline__ Bars bars_of(uint8_t *smem, int stages) {
+    Bars b;
+    b.full = reinterpret_cast<uint64_t *>(smem);
+    b.empty = b.full + stages;
+    b.tready = b.empty + stages;
+    b.tfree = b.tready + kTermBufs;
+    b.abort_flag = reinterpret_cast<volatile int *>(b.tfree + kTermBufs);
+    return b;
+}
+
+// Bounded wait that gives up for good once any wait of the CTA has failed.
+__device__ __forceinline__ void wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (*abort_flag) return;
+    if (!mbar_wait_bounded(bar, parity)) *abort_flag = 1;
+}
+
+template <bool KQ, int BPS>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const Layout L = make_layout(p);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *done = full + p.stages;
+    const Bars B = bars_of(smem, p.stages);
     uint8_t *ring = smem + L.stage_off;
     float *tbuf = reinterpret_cast<float *>(smem + L.terms_off);
-    const int T = p.rows_per_group, C = p.chunk, nb = L.nb;
-    const int my_tiles = blockIdx.x < p.total_groups ? (p.total_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    const int items = my_tiles * p.nchunks;
-    const uint64_t pol = l2_evict_first_policy();
-    const bool row_warp = warp == kComputeWarps;
+    const int T = p.rows_per_group, nb = L.nb;
+    const int items = blockIdx.x < p.total_groups ? (p.total_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&done[s], kComputeWarps);
+            mbar_init(&B.full[s], 1);
+            mbar_init(&B.empty[s], kComputeWarps);
         }
+        for (int j = 0; j < kTermBufs; ++j) {
+            mbar_init(&B.tready[j], kComputeWarps);
+            mbar_init(&B.tfree[j], 1);
+        }
+        *B.abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
+    uint64_t pol = 0;
     // Weights do not depend on the previous kernel: start streaming now.
-    if (row_warp)
-        for (int it = 0; it < p.stages && it < items; ++it) {
-            const GroupRef g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
-            issue_stage(p, L, g, it % p.nchunks, ring + (size_t)it * L.stage_bytes, &full[it], pol, lane);
-        }
+    if (warp == kProducerWarp && lane == 0) {
+        pol = l2_evict_first_policy();
+        for (int it = 0; it < p.stages && it < items; ++it)
+            issue_stage(p, L, locate(p, blockIdx.x + it * gridDim.x), ring + (size_t)it * L.stage_bytes, &B.full[it],
+                        pol);
+    }
 
     pdl_wait();
-    if (is_kquant(p.seg[0].type)) prep_q8k(p, L, smem);
+    if (KQ) prep_q8k(p, L, smem);
     else prep_q80(p, L, smem);
     __syncthreads();
     pdl_launch_dependents();
 
-    const bool kq = is_kquant(p.seg[0].type);
-    if (!row_warp) {
-        // ------------------------------------------------ compute warps
-        const int ct = warp * 32 + lane, nct = kComputeWarps * 32;
-        const int rs = ct % T, m0 = ct / T, mstep = nct / T;
-        GroupRef g{0, 0, 0};
-        for (int it = 0; it < items; ++it) {
+    if (warp == kProducerWarp) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        for (int it = p.stages; it < items; ++it) {
             const int s = it % p.stages;
-            const int c = it % p.nchunks;
-            if (c == 0) g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
-            if (!mbar_wait_bounded(&full[s], (uint32_t)((it / p.stages) & 1))) break;
-            const uint8_t *stage = ring + (size_t)s * L.stage_bytes;
-            float *tb = tbuf + (size_t)s * T * C;
-            int seg = 0, row = 0;
-            const bool valid = slot_row(p, g, rs, &seg, &row);
-            const int type = p.seg[seg].type;
-            const int cc = min(C, nb - c * C);
-            if (C == nb) {
-                // Whole rows: unit u -> (row slot u / nb, block u % nb); the
-                // lanes of a warp walk consecutive blocks of one or two rows.
-                if (!p.skip_compute) {
-                    const int half = p.pair ? T / 2 : T;
-                    for (int u = ct; u < T * nb; u += nct) {
-                        const int us = u / nb, m = u - us * nb;
-                        int useg = 0, urow = 0;
-                        if (!slot_row(p, g, us, &useg, &urow)) continue;
-                        const int part = us / half, i = us - part * half;
-                        const int utype = p.seg[useg].type;
-                        float t;
-                        if (kq) {
-                            const int bb = kq_block_bytes(utype);
-                            const size_t off0 = (size_t)g.r0 * nb * bb;
-                            const uint8_t *blk = stage + part * L.part_bytes + (off0 & 15) + (size_t)i * L.q_stride +
-                                                 (size_t)m * bb;
-                            t = utype == OVF_TYPE_Q4_K
-                                    ? q4k_unit(blk, smem + L.act_q_off + m * kQ8kActStride,
-                                               smem + L.act_meta_off + m * kQ8kMetaStride)
-                                    : q6k_unit(blk, smem + L.act_q_off + m * kQ8kActStride,
-                                               smem + L.act_meta_off + m * kQ8kMetaStride);
-                        } else {
-                            const size_t offq0 = (size_t)g.r0 * p.K, offs0 = (size_t)g.r0 * (p.K / 8);
-                            const uint8_t *wq = stage + part * L.part_bytes + (offq0 & 15) + (size_t)i * p.K + 32 * m;
-                            const float ws = *reinterpret_cast<const float *>(
-                                stage + L.s_region + part * L.s_part + (offs0 & 15) + (size_t)i * (p.K / 8) + 4 * m);
-                            t = q80_unit(wq, ws, smem + L.act_q_off + m * kQ80ActStride);
-                        }
-                        tb[us * C + m] = t;
-                    }
-                }
-            } else if (valid && !p.skip_compute) {
-                for (int m = m0; m < cc; m += mstep) {
-                    const int j = c * C + m;
-                    float t;
-                    if (kq) {
-                        const int bb = kq_block_bytes(type);
-                        const size_t off = (size_t)row * nb * bb + (size_t)c * C * bb;
-                        const uint8_t *blk = stage + rs * L.q_stride + (off & 15) + (size_t)m * bb;
-                        const uint8_t *aq = smem + L.act_q_off + j * kQ8kActStride;
-                        const uint8_t *am = smem + L.act_meta_off + j * kQ8kMetaStride;
-                        t = type == OVF_TYPE_Q4_K ? q4k_unit(blk, aq, am) : q6k_unit(blk, aq, am);
-                    } else {
-                        const size_t offq = (size_t)row * p.K + (size_t)c * C * 32;
-                        const size_t offs = (size_t)row * (p.K / 8) + (size_t)c * C * 4;
-                        const uint8_t *wq = stage + rs * L.q_stride + (offq & 15) + 32 * m;
-                        const float ws = *reinterpret_cast<const float *>(stage + L.s_region + rs * L.s_stride +
-                                                                          (offs & 15) + 4 * m);
-                        t = q80_unit(wq, ws, smem + L.act_q_off + j * kQ80ActStride);
-                    }
-                    tb[rs * C + m] = t;
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&done[s]);
+            wait_or_abort(&B.empty[s], (uint32_t)(((it / p.stages) - 1) & 1), B.abort_flag);
+            if (*B.abort_flag) break;
+            fence_proxy_async_smem();
+            issue_stage(p, L, locate(p, blockIdx.x + it * gridDim.x), ring + (size_t)s * L.stage_bytes, &B.full[s],
+                        pol);
         }
         return;
     }
 
-    // ------------------------------------------------------ row warp
-    const int G = kq ? nb : p.q8_group;
-    const bool grouped = G < nb;
-    unsigned long long best = 0ull;
-    float sum = 0.0f, grp = 0.0f, acc = 0.0f;  // lane r: running sums of row slot r
-    int gpos = 0;
-    GroupRef g{0, 0, 0};
-    for (int it = 0; it < items; ++it) {
-        const int s = it % p.stages;
-        const int c = it % p.nchunks;
-        if (c == 0) g = locate(p, blockIdx.x + (it / p.nchunks) * gridDim.x);
-        if (!mbar_wait_bounded(&done[s], (uint32_t)((it / p.stages) & 1))) break;
-        int seg = 0, row = 0;
-        const bool valid = lane < T && slot_row(p, g, lane, &seg, &row);
-        const int cc = min(C, nb - c * C);
-        const float *tb = tbuf + (size_t)s * T * C;
-        if (lane < T) {
-            if (c == 0) {
-                sum = 0.0f;
-                grp = 0.0f;
-                gpos = 0;
-                acc = (valid && p.seg[seg].bias) ? p.seg[seg].bias[row] : 0.0f;
-            }
-            const float *tr = tb + lane * C;
-            for (int m = 0; m < cc; ++m) {
-                const float v = tr[m];
-                if (grouped) {
-                    grp = gpos == 0 ? fadd(0.0f, v) : fadd(grp, v);
-                    if (++gpos == G) {
-                        acc = fadd(acc, grp);
-                        gpos = 0;
+    const int half = p.pair ? T / 2 : T;
+    if (warp == kSumWarp) {
+        // ------------------------------------------------------- sum warp
+        const int G = KQ ? nb : p.q8_group;
+        const bool grouped = G < nb;
+        const int nslots = half;  // pair mode: slot r sums gate row r and up row r
+        unsigned long long best = 0ull;
+        for (int it = 0; it < items; ++it) {
+            const int j = it % kTermBufs;
+            const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
+            for (int slot = lane; slot < ((nslots + 31) & ~31); slot += 32) {
+                int seg = 0, row = 0;
+                const bool valid = slot < nslots && slot_row(p, g, slot, &seg, &row);
+                // epilogue operands first: their latency overlaps the wait
+                const bool hb0 = valid && p.seg[seg].bias != nullptr;
+                const float b0 = hb0 ? p.seg[seg].bias[row] : 0.0f;
+                const bool hb1 = valid && p.pair && p.seg[1].bias != nullptr;
+                const float b1 = hb1 ? p.seg[1].bias[row] : 0.0f;
+                const float res = valid && p.epi == EPI_RESIDUAL ? p.resid[row] : 0.0f;
+                if (slot == lane) wait_or_abort(&B.tready[j], (uint32_t)((it / kTermBufs) & 1), B.abort_flag);
+                __syncwarp();
+                if (!valid) continue;
+                const float *tb = tbuf + (size_t)j * T * nb;
+                float y[2] = {0.0f, 0.0f};
+                for (int k = 0; k < (p.pair ? 2 : 1); ++k) {
+                    const float *tr = tb + (size_t)(slot + k * half) * nb;
+                    const bool hb = k == 0 ? hb0 : hb1;
+                    const float bv = k == 0 ? b0 : b1;
+                    if (grouped) {
+                        float acc = hb ? bv : 0.0f;
+                        for (int m0 = 0; m0 < nb; m0 += G) {
+                            float grp = fadd(0.0f, tr[m0]);
+                            for (int m = 1; m < G; ++m) grp = fadd(grp, tr[m0 + m]);
+                            acc = fadd(acc, grp);
+                        }
+                        y[k] = acc;
+                    } else {
+                        float sum = 0.0f;
+                        int m = 0;
+                        for (; m + 8 <= nb; m += 8) {
+                            float v[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) v[q] = tr[m + q];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) sum = fadd(sum, v[q]);
+                        }
+                        for (; m < nb; ++m) sum = fadd(sum, tr[m]);
+                        y[k] = hb ? fadd(bv, sum) : sum;
                     }
-                } else {
-                    sum = fadd(sum, v);
                 }
+                if (p.epi == EPI_SILU_PAIR) {
+                    const float sg = fdiv(1.0f, fadd(1.0f, expf(-y[0])));
+                    p.seg[0].out[row] = fmul(fmul(y[0], sg), y[1]);
+                } else {
+                    float *out = p.seg[seg].out;
+                    if (p.epi == EPI_RESIDUAL) out[row] = fadd(res, y[0]);
+                    else out[row] = y[0];
+                    if (p.epi == EPI_LOGITS_ARGMAX) {
+                        const unsigned long long kk = argmax_key(y[0], row);
+                        best = kk > best ? kk : best;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.tfree[j]);
+        }
+        if (p.epi == EPI_LOGITS_ARGMAX) {
+            // warp max -> one global atomic per CTA; the last CTA to finish
+            // turns the winning key into the next token.
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+                best = other > best ? other : best;
+            }
+            if (lane == 0) {
+                if (best) atomicMax(&p.step->argmax_key, best);
+                __threadfence();
+                const int ticket = atomicAdd(&p.step->done_ctas, 1);
+                if (ticket == (int)gridDim.x - 1) {
+                    __threadfence();
+                    const unsigned long long k = atomicAdd(&p.step->argmax_key, 0ull);
+                    const int idx = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+                    p.step->token = idx;
+                    if (p.tokens_out) p.tokens_out[p.step->n_generated] = idx;
+                    p.step->n_generated += 1;
+                    p.step->argmax_key = 0ull;
+                    p.step->done_ctas = 0;
+                    __threadfence();
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------- compute warps
+    // Thread -> (block slot, row subset): one thread per block (K-quant
+    // super-block or Q8_0 32-block).  With fewer blocks than threads the
+    // threads split the tile's rows into RS subsets; with more (Q8_0 only),
+    // a thread takes BPS blocks.
+    constexpr int NS = kComputeThreads;
+    int RS = 1, subset = 0;
+    bool slot_ok = true;
+    int mblk[BPS];
+    bool mval[BPS];
+    if (BPS == 1) {
+        RS = max(1, NS / nb);
+        subset = tid / nb;
+        slot_ok = tid < RS * nb;
+        mblk[0] = slot_ok ? tid % nb : 0;
+        mval[0] = slot_ok;
+    } else {
+#pragma unroll
+        for (int b = 0; b < BPS; ++b) {
+            const int m = tid + b * NS;
+            mval[b] = m < nb;
+            mblk[b] = mval[b] ? m : 0;
+        }
+    }
+    const int rps = (T + RS - 1) / RS;
+    KqAct kact[KQ ? BPS : 1];
+    Q8Act qact[KQ ? 1 : BPS];
+#pragma unroll
+    for (int b = 0; b < BPS; ++b) {
+        if (KQ)
+            load_kq_act(smem + L.act_q_off + mblk[b] * kQ8kActStride, smem + L.act_meta_off + mblk[b] * kQ8kMetaStride,
+                        kact[KQ ? b : 0]);
+        else
+            load_q8_act(smem + L.act_q_off + mblk[b] * kQ80ActStride, qact[KQ ? 0 : b]);
+    }
+    const size_t sb = (size_t)(p.K / 8);
+    for (int it = 0; it < items; ++it) {
+        const int s = it % p.stages, j = it % kTermBufs;
+        const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
+        const int ttype = p.seg[p.pair ? 0 : g.seg].type;  // a tile never mixes types
+        const size_t rb = (size_t)row_bytes(ttype, p.K);
+        const uint8_t *stage = ring + (size_t)s * L.stage_bytes;
+        const uint8_t *qbase = stage + (((size_t)g.r0 * rb) & 15);
+        const uint8_t *sbase = stage + L.s_region + (((size_t)g.r0 * sb) & 15);
+        float *tb = tbuf + (size_t)j * T * nb;
+        if (it >= kTermBufs) wait_or_abort(&B.tfree[j], (uint32_t)(((it / kTermBufs) - 1) & 1), B.abort_flag);
+        wait_or_abort(&B.full[s], (uint32_t)((it / p.stages) & 1), B.abort_flag);
+        for (int rr = 0; rr < rps; ++rr) {
+            const int r = subset + rr * RS;
+            int useg = 0, urow = 0;
+            const bool rv = slot_ok && r < T && slot_row(p, g, r, &useg, &urow);
+            if (!rv) continue;
+            const int part = r / half, i = r - part * half;
+            const uint8_t *rp = qbase + part * L.part_bytes + (size_t)i * rb;
+#pragma unroll
+            for (int b = 0; b < BPS; ++b) {
+                if (!mval[b]) continue;
+                float t;
+                if (KQ) {
+                    const KqAct &a = kact[KQ ? b : 0];
+                    t = ttype == OVF_TYPE_Q4_K ? q4k_block(rp + (size_t)mblk[b] * 144, a)
+                                               : q6k_block(rp + (size_t)mblk[b] * 210, a);
+                } else {
+                    const uint8_t *sp = sbase + part * L.s_part + (size_t)i * sb;
+                    t = q80_block(rp + 32 * mblk[b], *reinterpret_cast<const float *>(sp + 4 * mblk[b]),
+                                  qact[KQ ? 0 : b]);
+                }
+                tb[r * nb + mblk[b]] = t;
             }
         }
         __syncwarp();
-        // The stage and its terms are consumed: refill with item it + stages.
-        const int nx = it + p.stages;
-        if (nx < items) {
-            if (lane == 0) fence_proxy_async_smem();
-            __syncwarp();
-            const GroupRef gn = locate(p, blockIdx.x + (nx / p.nchunks) * gridDim.x);
-            issue_stage(p, L, gn, nx % p.nchunks, ring + (size_t)s * L.stage_bytes, &full[s], pol, lane);
-        }
-        if (c == p.nchunks - 1) {
-            float y;
-            if (grouped) y = acc;
-            else y = (valid && p.seg[seg].bias) ? fadd(p.seg[seg].bias[row], sum) : sum;
-            if (p.epi == EPI_SILU_PAIR) {
-                const int half = T / 2;
-                const float u = __shfl_down_sync(0xFFFFFFFFu, y, half);
-                if (lane < half && valid) {
-                    const float sg = fdiv(1.0f, fadd(1.0f, expf(-y)));
-                    p.seg[0].out[row] = fmul(fmul(y, sg), u);
-                }
-            } else if (valid) {
-                float *out = p.seg[seg].out;
-                if (p.epi == EPI_RESIDUAL) out[row] = fadd(p.resid[row], y);
-                else out[row] = y;
-                if (p.epi == EPI_LOGITS_ARGMAX) {
-                    const unsigned long long kk = argmax_key(y, row);
-                    best = kk > best ? kk : best;
-                }
-            }
-        }
-    }
-
-    if (p.epi == EPI_LOGITS_ARGMAX) {
-        // the row warp holds the CTA's rows: warp max -> one global atomic per
-        // CTA; the last CTA to finish turns the winning key into the next token.
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-            best = other > best ? other : best;
-        }
         if (lane == 0) {
-            atomicMax(&p.step->argmax_key, best);
-            __threadfence();
-            const int ticket = atomicAdd(&p.step->done_ctas, 1);
-            if (ticket == (int)gridDim.x - 1) {
-                __threadfence();
-                const unsigned long long k = atomicAdd(&p.step->argmax_key, 0ull);
-                const int idx = (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
-                p.step->token = idx;
-                if (p.tokens_out) p.tokens_out[p.step->n_generated] = idx;
-                p.step->n_generated += 1;
-                p.step->argmax_key = 0ull;
-                p.step->done_ctas = 0;
-                __threadfence();
-            }
+            mbar_arrive(&B.empty[s]);   // the stage may be refilled
+            mbar_arrive(&B.tready[j]);  // the terms may be summed (release)
         }
     }
 }
@@ -880,25 +881,37 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     const int nb = kq ? p.K / 256 : p.K / 32;
     if (!kq && p.q8_group <= 0) p.q8_group = nb;
     OVF_CHECK_ARG(kq || nb % p.q8_group == 0, "gemv: Q8_0 group must divide the block count");
-    // Whole-row tiles of T rows (~40 KB of weights, up to 16 rows; pair
-    // launches take T/2 gate + T/2 up rows): one bulk copy per matrix per
-    // stage.  OVF_GEMV_C selects the per-row chunked mode instead.
-    int T = 16, C = nb;
-    int rb = 0;
-    for (int s = 0; s < p.nseg; ++s) rb = std::max(rb, kq ? nb * kq_block_bytes(p.seg[s].type) : p.K + p.K / 8);
-    T = (int)std::max<int64_t>(1, std::min<int64_t>(16, (40 * 1024) / rb));
-    if (p.pair) T = std::max(2, T & ~1);
-    if (const char *e = getenv("OVF_GEMV_T")) T = std::max(1, std::min(32, atoi(e)));
-    if (const char *e = getenv("OVF_GEMV_C")) if (atoi(e) > 0) C = std::max(1, std::min(nb, atoi(e)));
-    p.copy_split = 1;
-    if (const char *e = getenv("OVF_GEMV_SPLIT")) p.copy_split = std::max(1, std::min(16, atoi(e)));
-    OVF_CHECK_ARG(T * C <= 32 * 128, "gemv: tile too large");
+    int rb = 0;  // bytes streamed per weight row (Q8_0: quants + fp32 scales)
+    for (int s = 0; s < p.nseg; ++s) rb = std::max(rb, row_bytes(p.seg[s].type, p.K) + (kq ? 0 : p.K / 8));
+    const int parts = p.pair ? 2 : 1;
+
+    // Tile size: T rows (T/2 gate + T/2 up rows in pair launches), at most
+    // ~40 KB of weights per stage.  Among those, take the T that minimises
+    // the busiest CTA's streamed bytes plus a fixed per-tile cost (~2 KB
+    // equivalent): balanced tile counts matter for the small matrices.
+    const int budget = smem_optin(device) - 1024;
+    const int t_cap = std::max(1, std::min(64, (40 * 1024) / (rb * parts))) * parts;
+    int best_T = parts;
+    double best_cost = 1e300;
+    for (int T = parts; T <= t_cap; T += parts) {
+        const int rows_per = T / parts;
+        int tiles = 0;
+        if (p.pair) tiles = (p.seg[0].rows + rows_per - 1) / rows_per;
+        else
+            for (int s = 0; s < p.nseg; ++s) tiles += (p.seg[s].rows + rows_per - 1) / rows_per;
+        if (tiles == 0) break;
+        const int grid = std::min(nsm, tiles);
+        const double cost = (double)((tiles + grid - 1) / grid) * ((double)T * rb + 2048.0);
+        if (cost < best_cost * 0.999) {
+            best_cost = cost;
+            best_T = T;
+        }
+    }
+    int T = best_T;
+    if (const char *e = getenv("OVF_GEMV_T")) T = std::max(parts, std::min(64, atoi(e) / parts * parts));
+    OVF_CHECK_ARG(T * nb <= 16384, "gemv: K=%d is too long for one tile row", p.K);
     p.rows_per_group = T;
-    p.chunk = C;
-    p.nchunks = (nb + C - 1) / C;
-    p.lanes_per_row = 1;
-    p.units_per_lane = 1;
-    const int rows_per = p.pair ? T / 2 : T;
+    const int rows_per = T / parts;
     int total = 0;
     for (int s = 0; s < p.nseg; ++s) {
         p.seg[s].groups = (p.seg[s].rows + rows_per - 1) / rows_per;
@@ -908,14 +921,12 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     p.total_groups = total;
     if (total == 0) return OVF_OK;
 
-    const int budget = smem_optin(device) - 1024;
     const int grid = std::min(nsm, total);
-    const int warps = kComputeWarps + 1;
+    const int warps = kThreads / 32;
     int stages = 0;
     size_t smem = 0;
-    int s_hi = 6, s_lo = 2;
+    int s_hi = 8, s_lo = 2;
     if (const char *e = getenv("OVF_GEMV_S")) s_hi = s_lo = std::max(2, std::min(8, atoi(e)));
-    if (const char *e = getenv("OVF_GEMV_SKIP")) p.skip_compute = atoi(e);
     for (int S = s_hi; S >= s_lo; --S) {
         p.stages = S;
         const Layout L = make_layout(p);
@@ -927,14 +938,19 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     }
     OVF_CHECK_ARG(stages >= 2, "gemv: K=%d does not fit shared memory", p.K);
     p.stages = stages;
-    static bool attr_done[64] = {false};
-    if (device < 64 && !attr_done[device]) {
-        OVF_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          smem_optin(device)));
-        attr_done[device] = true;
+    // Blocks per compute slot: the activation slices live in registers.
+    const int bps = (nb + kComputeThreads - 1) / kComputeThreads;
+    OVF_CHECK_ARG(bps <= (kq ? 1 : 2), "gemv: K=%d is too long (at most %d)", p.K,
+                  kq ? kComputeThreads * 256 : 2 * kComputeThreads * 32);
+    void (*kern)(GemvParams) = kq ? gemv_kernel<true, 1> : (bps == 1 ? gemv_kernel<false, 1> : gemv_kernel<false, 2>);
+    const int ki = (kq ? 0 : 1) + (bps - 1);
+    static bool attr_done[64][4] = {};
+    if (device < 64 && !attr_done[device][ki]) {
+        OVF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin(device)));
+        attr_done[device][ki] = true;
     }
-    if (plan_out) *plan_out = GemvPlan{T, p.chunk, stages, warps, grid, smem};
-    cudaError_t e = launch_pdl(gemv_kernel, dim3(grid), dim3(warps * 32), smem, stream, pdl, p);
+    if (plan_out) *plan_out = GemvPlan{T, stages, warps, grid, smem};
+    cudaError_t e = launch_pdl(kern, dim3(grid), dim3(warps * 32), smem, stream, pdl, p);
     if (e != cudaSuccess) return cuda_status(e, "gemv_kernel launch");
     return OVF_OK;
 }

@@ -1,7 +1,7 @@
 // ovf_gemv.cuh — the quantized decode GEMV (launch parameters and host API).
 //
 // One kernel streams Q4_K (144 B), Q6_K (210 B) and Q8_0 (int8 + fp32 scale)
-// weight rows from HBM with 1-D bulk copies (the TMA engine) into per-warp
+// weight rows from HBM with 1-D bulk copies (the TMA engine) into a ring of
 // shared-memory stages, contracts them with a Q8_K / Q8_0 activation held in
 // shared memory using dp4a, and sums each row's super-block terms in
 // ascending order so the result is bit-identical to the reference's
@@ -45,26 +45,20 @@ struct GemvSeg {
     float *out;
     int type;
     int rows;
-    int groups;          // row groups (one warp's rows) in this segment
+    int groups;          // row tiles in this segment
 };
 
 struct GemvParams {
     GemvSeg seg[3];
     int nseg;
     int K;
-    int lanes_per_row;   // L: lanes sharing one weight row (1, 2 or 4)
-    int units_per_lane;  // u: blocks a lane contracts per chunk
-    int chunk;           // C = L*u blocks of a row streamed per stage
-    int nchunks;         // blocks per row / C
-    int rows_per_group;  // rows one warp owns (32/L; 16 per matrix in pair mode)
+    int rows_per_group;  // T: rows per tile (T/2 gate + T/2 up rows in pair mode)
     int stages;
     int q8_group;        // Q8_0 blocks per summation group (== K/32 when ungrouped)
     int act_mode;
     int epi;
     int pair;            // EPI_SILU_PAIR: seg0 = gate, seg1 = up, same row groups
-    int total_groups;
-    int skip_compute;    // experiments only: stream the weights, contract nothing
-    int copy_split;      // bulk copies per matrix part of a whole-row stage
+    int total_groups;    // row tiles over all segments
     const float *x;
     const float *gamma;
     float eps;
@@ -80,7 +74,7 @@ struct GemvParams {
 };
 
 struct GemvPlan {
-    int lanes_per_row, chunk, stages, warps, grid;
+    int rows_per_tile, stages, warps, grid;
     size_t smem;
 };
 
