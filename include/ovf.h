@@ -132,13 +132,22 @@ ovf_status ovf_rmsnorm(const float *x, const float *gamma, float *y, int64_t d, 
 ovf_status ovf_rope_apply(float *v, int32_t n_vec, int32_t head_dim, const float *cos_row,
                           const float *sin_row, int32_t split_half, void *stream);
 /* Runtime/CachedAttentionKernel.cs:36 ComputeSingleHead for every query head
- * (GQA: head h reads KV head h/(n_heads/n_kv_heads), CachedMultiHeadAttention.cs:897),
- * split along the sequence (flash-decode) and merged with log-sum-exp.
+ * (GQA: head h reads KV head h/(n_heads/n_kv_heads), CachedMultiHeadAttention.cs:897)
+ * over fp16 caches (no reference counterpart), split along the sequence
+ * (flash-decode) and merged with log-sum-exp: within tolerance of the
+ * reference, not bit-identical.
  * q [n_heads x hd] fp32; k_cache/v_cache fp16 [n_kv_heads x max_ctx x hd];
  * positions [0, seq_len) are attended.  scratch must hold
  * ovf_attention_scratch_bytes(n_heads, n_kv_heads, hd) bytes and
  * counters n_kv_heads int32 zeros (they are left zero on return). */
 int64_t ovf_attention_scratch_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t head_dim);
+/* Runtime/CachedAttentionKernel.cs:36 ComputeSingleHead for every query head
+ * over F32 caches k_cache/v_cache [n_kv_heads x max_ctx x hd], positions
+ * [0, seq_len): the reference's operation order, bit-identical results.
+ * head_dim 32, 64, 128 or 256.  No scratch. */
+ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const float *v_cache, float *out,
+                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
+                                     int32_t seq_len, float scale, void *stream);
 ovf_status ovf_attention_decode(const float *q, const void *k_cache, const void *v_cache, float *out,
                                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                 int32_t max_ctx, int32_t seq_len, float scale, void *scratch,
@@ -198,8 +207,20 @@ ovf_status ovf_model_destroy(ovf_model *m);
 /* Device bytes of resident weights (for bandwidth accounting). */
 int64_t ovf_model_weight_bytes(const ovf_model *m);
 
-/* ISlmInferenceEngine.CreateSession (Contracts/ISlmInferenceEngine.cs:9). */
+/* KV-cache element types (Runtime/KvCacheDType.cs:15).  OVF_KV_F32 is the
+ * reference's default: attention then runs in the reference's exact
+ * operation order (CachedAttentionKernel.ComputeSingleHead).  OVF_KV_F16 has
+ * no reference counterpart: half the KV traffic, flash-decode attention with
+ * a log-sum-exp merge, results within tolerance of the F32 path only. */
+#define OVF_KV_F32 0
+#define OVF_KV_F16 2
+
+/* ISlmInferenceEngine.CreateSession (Contracts/ISlmInferenceEngine.cs:9):
+ * F32 KV cache. */
 ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out);
+/* CachedLlamaInferenceEngine.CreateSession(maxContextLength, kvCacheDType)
+ * (Runtime/CachedLlamaInferenceEngine.cs:360). */
+ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype, ovf_session **out);
 ovf_status ovf_session_destroy(ovf_session *s);
 /* ISlmSession.Reset (Contracts/ISlmSession.cs:8). */
 ovf_status ovf_session_reset(ovf_session *s);

@@ -71,10 +71,12 @@ SIGNATURES = {
     "ovf_attention_scratch_bytes": (I64, [I32, I32, I32]),
     "ovf_attention_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P, P, P]),
     "ovf_attention_decode_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
+    "ovf_attention_single_head": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_model_create": (I32, [I32, P, P, I32, P]),
     "ovf_model_destroy": (I32, [P]),
     "ovf_model_weight_bytes": (I64, [P]),
     "ovf_session_create": (I32, [P, I32, P]),
+    "ovf_session_create_kv": (I32, [P, I32, I32, P]),
     "ovf_session_destroy": (I32, [P]),
     "ovf_session_reset": (I32, [P]),
     "ovf_session_position": (I32, [P]),

@@ -273,4 +273,23 @@ ovf_status ovf_attention_decode(const float *q, const void *k_cache, const void 
     return launch_attention(p, S(stream), false);
 }
 
+ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const float *v_cache, float *out,
+                                     int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
+                                     int32_t seq_len, float scale, void *stream) {
+    OVF_CHECK_ARG(q && k_cache && v_cache && out, "ComputeSingleHead: null buffer");
+    OVF_CHECK_ARG(seq_len >= 1 && seq_len <= max_ctx, "ComputeSingleHead: seq_len must be in [1, max_ctx]");
+    AttnParams p{};
+    p.q = q;
+    p.kc = (__half *)k_cache;
+    p.vc = (__half *)v_cache;
+    p.out = out;
+    p.H = n_heads;
+    p.KVH = n_kv_heads;
+    p.hd = head_dim;
+    p.max_ctx = max_ctx;
+    p.seq_len_host = seq_len;
+    p.scale = scale;
+    return launch_attention_exact(p, seq_len, S(stream), false);
+}
+
 }  // extern "C"

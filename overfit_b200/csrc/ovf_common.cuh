@@ -96,6 +96,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or `ns` nanoseconds pass, instead of spinning on issue slots
+// that the CTA's other warps need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Sleeping bounded wait: gives up after 2^20 suspensions of at most 2 us
+// (about two seconds), raises the device error word and returns false.
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 20); ++i)
+        if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+    raise_dev_error(DEVERR_MBAR_TIMEOUT);
+    return false;
+}
+
 // Bounded wait: gives up after ~2^26 polls (each try_wait itself suspends
 // for a while), raises the device error word and returns false.  A correct
 // program never gets near the limit.
@@ -132,6 +154,40 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
+
+// Running fp32 sum of squares over x[0..n) in index order — the
+// reference's sequential RMSNorm loop (Runtime/CachedTransformerBlock.cs:
+// 532-536), bit for bit — computed by one warp: lanes square 32 elements at
+// a time (the next 32 are loaded meanwhile) and the running sum takes them
+// in order through shuffles.  Every lane returns the same sum.
+__device__ __forceinline__ float warp_seq_sumsq(const float *x, int n, float acc) {
+    const int lane = threadIdx.x & 31;
+    float nxt = lane < n ? __ldcg(x + lane) : 0.0f;
+    for (int b = 0; b < n; b += 32) {
+        const float sq = fmul(nxt, nxt);
+        const int m = min(32, n - b);
+        nxt = b + 32 + lane < n ? __ldcg(x + b + 32 + lane) : 0.0f;
+        if (m == 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+        } else {
+            for (int j = 0; j < m; ++j) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+        }
+    }
+    return acc;
+}
+
+// RMSNorm scale from the sum of squares: 1 / sqrt(sumSq / d + eps).
+__device__ __forceinline__ float rms_scale(float sumsq, int d, float eps) {
+    return fdiv(1.0f, sqrtf(fadd(fdiv(sumsq, (float)d), eps)));
+}
+
+// e^x for a float argument, rounded once from the double-precision exp: the
+// correctly rounded result but for rare near-ties.  The reference's
+// MathF.Exp is the host C library's expf, which returns the correctly
+// rounded value for all but a small fraction of inputs, so this agrees with
+// it far more often than the single-precision expf.
+__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp((double)x)); }
 
 // Q8_K / Q8_0 element quantizer: clamp(round_half_even(x * inv), -127, 127).
 __device__ __forceinline__ int quant_elem(float x, float inv) {

@@ -267,6 +267,127 @@ __device__ __forceinline__ float q80_block(const uint8_t *wq, float ws, const Q8
     return fmul(fmul(ws, a.s), i2f(dot));
 }
 
+// Shared-memory-activation forms of the block dots (the activation block is
+// read from shared memory for every row).
+// Q4_K x Q8_K over one super-block (Runtime/Q4KDotKernel.cs:216-256).
+__device__ __forceinline__ float q4k_unit(const uint8_t *blk, const uint8_t *q8, const uint8_t *meta) {
+    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+    const float d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
+    const float dmin = h2f_bits((uint16_t)(h.x >> 16));
+    // 6-bit scales and mins (Loading/GgmlDequant.cs:49-77), four per word
+    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
+    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    int mainAcc = 0, mainAccH = 0;  // mainAccH: exact multiple of 16
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+        const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
+        const uint4 l0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p);
+        const uint4 l1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 16);
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 32);
+        const uint4 h1 = *reinterpret_cast<const uint4 *>(q8 + 64 * p + 48);
+        const uint32_t M = 0x0F0F0F0Fu, HM = 0xF0F0F0F0u;
+        // High nibbles stay in place (16 * nibble as the unsigned operand):
+        // that sum is 16x the nibble dot and is divided out exactly below.
+        int lo = dp4a((int)(qa.x & M), (int)l0.x, 0);
+        int lo2 = dp4a((int)(qb.x & M), (int)l1.x, 0);
+        int hi = dp4a_us(qa.x & HM, (int)h0.x, 0);
+        int hi2 = dp4a_us(qb.x & HM, (int)h1.x, 0);
+        lo = dp4a((int)(qa.y & M), (int)l0.y, lo);
+        lo2 = dp4a((int)(qb.y & M), (int)l1.y, lo2);
+        hi = dp4a_us(qa.y & HM, (int)h0.y, hi);
+        hi2 = dp4a_us(qb.y & HM, (int)h1.y, hi2);
+        lo = dp4a((int)(qa.z & M), (int)l0.z, lo);
+        lo2 = dp4a((int)(qb.z & M), (int)l1.z, lo2);
+        hi = dp4a_us(qa.z & HM, (int)h0.z, hi);
+        hi2 = dp4a_us(qb.z & HM, (int)h1.z, hi2);
+        lo = dp4a((int)(qa.w & M), (int)l0.w, lo);
+        lo2 = dp4a((int)(qb.w & M), (int)l1.w, lo2);
+        hi = dp4a_us(qa.w & HM, (int)h0.w, hi);
+        hi2 = dp4a_us(qb.w & HM, (int)h1.w, hi2);
+        const uint32_t scw = p < 2 ? sc03 : sc47;
+        mainAcc += (int)byte_of(scw, (2 * p) & 3) * (lo + lo2);
+        mainAccH += (int)byte_of(scw, (2 * p + 1) & 3) * (hi + hi2);
+    }
+    mainAcc += mainAccH >> 4;
+    // min correction: sum_s m[s] * (bsum[2s] + bsum[2s+1]) as four dp2a
+    const uint4 ps = *reinterpret_cast<const uint4 *>(meta + 48);
+    const float q8s = *reinterpret_cast<const float *>(meta + 32);
+    int minAcc = __dp2a_lo((int)ps.x, (int)mn03, 0);
+    minAcc = __dp2a_hi((int)ps.y, (int)mn03, minAcc);
+    minAcc = __dp2a_lo((int)ps.z, (int)mn47, minAcc);
+    minAcc = __dp2a_hi((int)ps.w, (int)mn47, minAcc);
+    return fmul(q8s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
+}
+
+// Q6_K x Q8_K over one super-block (Runtime/Q6KDotKernel.cs:77-121 with the
+// unsigned dot :186-215).
+__device__ __forceinline__ float q6k_unit(const uint8_t *blk, const uint8_t *q8, const uint8_t *meta) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+    const uint32_t *base = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const int sh = (int)(a & 3u) * 8;
+    int sc[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t w = ldw_shifted(base, 48 + i, sh);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[4 * i + j] = (int)(int8_t)byte_of(w, j);
+    }
+    const float d = h2f_bits((uint16_t)(ldw_shifted(base, 52, sh) & 0xFFFFu));
+    const uint32_t *q8w = reinterpret_cast<const uint32_t *>(q8);
+    int sum = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int lw = 0; lw < 8; ++lw) {
+            const uint32_t qla = ldw_shifted(base, 16 * h + lw, sh);
+            const uint32_t qlb = ldw_shifted(base, 16 * h + 8 + lw, sh);
+            const uint32_t qhw = ldw_shifted(base, 32 + 8 * h + lw, sh);
+            const uint32_t M = 0x0F0F0F0Fu, H = 0x30303030u;
+            const int q1 = (int)((qla & M) | ((qhw << 4) & H));
+            const int q2 = (int)((qlb & M) | ((qhw << 2) & H));
+            const int q3 = (int)(((qla >> 4) & M) | (qhw & H));
+            const int q4 = (int)(((qlb >> 4) & M) | ((qhw >> 2) & H));
+            const int is = lw >> 2;
+            const int base8 = 32 * h + lw;
+            sum += sc[8 * h + is] * dp4a(q1, (int)q8w[base8], 0) + sc[8 * h + is + 2] * dp4a(q2, (int)q8w[base8 + 8], 0) +
+                   sc[8 * h + is + 4] * dp4a(q3, (int)q8w[base8 + 16], 0) +
+                   sc[8 * h + is + 6] * dp4a(q4, (int)q8w[base8 + 24], 0);
+        }
+    }
+    const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
+    const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
+    const float q8s = *reinterpret_cast<const float *>(meta + 32);
+    const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    int bsumTerm = 0;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+        bsumTerm += sc[2 * s] * (int)(int16_t)(bw[s] & 0xFFFFu) + sc[2 * s + 1] * (int)(int16_t)(bw[s] >> 16);
+    }
+    const int mainAcc = sum - 32 * bsumTerm;
+    return fmul(fmul(d, q8s), i2f(mainAcc));
+}
+
+// Q8_0 x Q8_0 over one 32-block (Runtime/Q8DotKernel.cs:99-140).
+__device__ __forceinline__ float q80_unit(const uint8_t *wq, float ws, const uint8_t *act) {
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(wq);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(wq + 16);
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(act);
+    const uint4 a1 = *reinterpret_cast<const uint4 *>(act + 16);
+    const float xs = *reinterpret_cast<const float *>(act + 32);
+    int dot = 0;
+    dot = dp4a((int)w0.x, (int)a0.x, dot);
+    dot = dp4a((int)w0.y, (int)a0.y, dot);
+    dot = dp4a((int)w0.z, (int)a0.z, dot);
+    dot = dp4a((int)w0.w, (int)a0.w, dot);
+    dot = dp4a((int)w1.x, (int)a1.x, dot);
+    dot = dp4a((int)w1.y, (int)a1.y, dot);
+    dot = dp4a((int)w1.z, (int)a1.z, dot);
+    dot = dp4a((int)w1.w, (int)a1.w, dot);
+    return fmul(fmul(ws, xs), i2f(dot));
+}
+
 // --------------------------------------------------------- activation prep
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -279,46 +400,11 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// RMSNorm scale s = 1/sqrt(sum(x^2)/K + eps) with a fixed-order block
-// reduction (Runtime/CachedTransformerBlock.cs:525-552; the reference's sum
-// is sequential, so this one agrees to rounding, not bit for bit).
-__device__ float block_rms_scale(const float *x, int K, float eps, float *red) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    float s = 0.0f;
-    for (int i = tid; i < K; i += blockDim.x) s = fadd(s, fmul(x[i], x[i]));
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    if (warp == 0) {
-        float v = lane < nw ? red[lane] : 0.0f;
-        v = warp_sum(v);
-        if (lane == 0) red[32] = fdiv(1.0f, sqrtf(fadd(fdiv(v, (float)K), eps)));
-    }
-    __syncthreads();
-    return red[32];
-}
-
-// Block-wide sum of one value per thread (fixed order), broadcast to all.
-__device__ __forceinline__ float block_sum(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        float t = lane < nw ? red[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) red[32] = t;
-    }
-    __syncthreads();
-    return red[32];
-}
-
 // Activation prologue, Q8_K form.  Every lane first issues the loads of all
-// its elements (independent 16-byte loads, one memory round trip), then the
-// CTA reduces the RMSNorm sum of squares (Runtime/CachedTransformerBlock.cs:
-// 525-552; fixed-order tree, so equal to the reference's sequential sum up to
-// rounding) and quantizes per 256 (Runtime/Q4KDotKernel.cs:71-136).
+// its elements (independent 16-byte loads, one memory round trip), applies
+// RMSNorm as (x * scale) * gamma with the scale its producer computed in the
+// reference's order (Runtime/CachedTransformerBlock.cs:525-552), and
+// quantizes per 256 (Runtime/Q4KDotKernel.cs:71-136).
 __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint8_t *aq = smem + L.act_q_off;
@@ -336,36 +422,10 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
         }
         return;
     }
-    float *red = reinterpret_cast<float *>(smem + L.red_off);
     const bool norm = p.act_mode == ACT_F32_RMSNORM;
     const bool write_out = blockIdx.x == 0 && p.aq_out != nullptr;
     constexpr int MB = 4;  // blocks per warp held in registers per batch
-    float s = 1.0f;
-    if (norm) {
-        float ss = 0.0f;
-        for (int b0 = warp; b0 < nsb; b0 += nw * MB) {
-            float4 x0[MB], x1[MB];
-#pragma unroll
-            for (int i = 0; i < MB; ++i) {
-                const int b = b0 + i * nw;
-                if (b < nsb) {
-                    x0[i] = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane);
-                    x1[i] = *reinterpret_cast<const float4 *>(p.x + b * 256 + 8 * lane + 4);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < MB; ++i) {
-                if (b0 + i * nw < nsb) {
-                    ss = fadd(ss, fmul(x0[i].x, x0[i].x)); ss = fadd(ss, fmul(x0[i].y, x0[i].y));
-                    ss = fadd(ss, fmul(x0[i].z, x0[i].z)); ss = fadd(ss, fmul(x0[i].w, x0[i].w));
-                    ss = fadd(ss, fmul(x1[i].x, x1[i].x)); ss = fadd(ss, fmul(x1[i].y, x1[i].y));
-                    ss = fadd(ss, fmul(x1[i].z, x1[i].z)); ss = fadd(ss, fmul(x1[i].w, x1[i].w));
-                }
-            }
-        }
-        const float tot = block_sum(ss, red);
-        s = fdiv(1.0f, sqrtf(fadd(fdiv(tot, (float)p.K), p.eps)));
-    }
+    const float s = norm ? *p.norm_scale : 1.0f;
     for (int b0 = warp; b0 < nsb; b0 += nw * MB) {
         float v[MB][8];
         float gm[MB][8];
@@ -428,24 +488,11 @@ __device__ void prep_q8k(const GemvParams &p, const Layout &L, uint8_t *smem) {
 __device__ void prep_q80(const GemvParams &p, const Layout &L, uint8_t *smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint8_t *act = smem + L.act_q_off;
-    float *red = reinterpret_cast<float *>(smem + L.red_off);
     const bool norm = p.act_mode == ACT_F32_RMSNORM;
     const bool write_out = blockIdx.x == 0 && p.aq_out != nullptr;
     constexpr int MB = 16;
     const int nb = L.nb;
-    float s = 1.0f;
-    if (norm) {
-        float ss = 0.0f;
-        for (int b0 = warp; b0 < nb; b0 += nw * MB) {
-            float xv[MB];
-#pragma unroll
-            for (int i = 0; i < MB; ++i) xv[i] = (b0 + i * nw < nb) ? p.x[(b0 + i * nw) * 32 + lane] : 0.0f;
-#pragma unroll
-            for (int i = 0; i < MB; ++i) ss = fadd(ss, fmul(xv[i], xv[i]));
-        }
-        const float tot = block_sum(ss, red);
-        s = fdiv(1.0f, sqrtf(fadd(fdiv(tot, (float)p.K), p.eps)));
-    }
+    const float s = norm ? *p.norm_scale : 1.0f;
     for (int b0 = warp; b0 < nb; b0 += nw * MB) {
         float xv[MB], gv[MB];
 #pragma unroll
@@ -573,7 +620,21 @@ __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L
 //   sum warp: lane r adds row slot r's terms in ascending block order — the
 //     reference's sequential fp32 loop — and runs the epilogue, while the
 //     compute warps already work on the next tiles (kTermBufs buffers).
-static constexpr int kComputeWarps = 6;
+#ifndef OVF_GEMV_CW
+#define OVF_GEMV_CW 4
+#endif
+#ifndef OVF_GEMV_ACTREG
+#define OVF_GEMV_ACTREG 0
+#endif
+static constexpr int kComputeWarps = OVF_GEMV_CW;
+static constexpr bool kActRegs = OVF_GEMV_ACTREG;
+#ifndef OVF_GEMV_CTAS
+#define OVF_GEMV_CTAS 3
+#endif
+static constexpr int kCtasPerSm = OVF_GEMV_CTAS;
+#ifndef OVF_GEMV_TILE_KB
+#define OVF_GEMV_TILE_KB 16
+#endif
 static constexpr int kComputeThreads = kComputeWarps * 32;
 static constexpr int kSumWarp = kComputeWarps;
 static constexpr int kProducerWarp = kComputeWarps + 1;
@@ -597,11 +658,53 @@ __device__ __forceinline__ Bars bars_of(uint8_t *smem, int stages) {
 // Bounded wait that gives up for good once any wait of the CTA has failed.
 __device__ __forceinline__ void wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (*abort_flag) return;
-    if (!mbar_wait_bounded(bar, parity)) *abort_flag = 1;
+    if (!mbar_wait_sleep_bounded(bar, parity)) *abort_flag = 1;
+}
+
+// RMSNorm of a residual output (EPI_RESIDUAL with norm_out): the sum warp of
+// CTA 0 walks the output rows in index order as their tiles complete
+// (per-tile flags, set by each tile's sum warp after its stores) and keeps
+// the reference's sequential fp32 sum of squares; the scale it leaves in
+// norm_out spares every CTA of the consuming kernel a reduction, and
+// reproduces the reference's RmsNormalize bit for bit.  CTA 0 resets each
+// flag it consumes, so the flags are zero again for the next launch.
+struct NormChain {
+    int tile = 0;     // next tile to add
+    float acc = 0.0f;
+    bool ok = true;
+};
+
+__device__ __noinline__ void chain_norm(const GemvParams &p, NormChain &c, bool block) {
+    const int lane = threadIdx.x & 31;
+    while (c.ok && c.tile < p.total_groups) {
+        int f = 0;
+        if (lane == 0) {
+            volatile int *fl = p.tile_flags + c.tile;
+            f = *fl;
+            for (uint32_t i = 0; !f && block && i < (1u << 22); ++i) {
+                __nanosleep(64);
+                f = *fl;
+            }
+        }
+        f = __shfl_sync(0xFFFFFFFFu, f, 0);
+        if (!f) {
+            if (block) {
+                c.ok = false;
+                if (lane == 0) raise_dev_error(DEVERR_COUNTER);
+            }
+            return;
+        }
+        __threadfence();
+        const GroupRef g = locate(p, c.tile);
+        c.acc = warp_seq_sumsq(p.seg[0].out + g.r0, g.nr, c.acc);
+        __syncwarp();
+        if (lane == 0) p.tile_flags[c.tile] = 0;
+        ++c.tile;
+    }
 }
 
 template <bool KQ, int BPS>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const Layout L = make_layout(p);
@@ -647,8 +750,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             wait_or_abort(&B.empty[s], (uint32_t)(((it / p.stages) - 1) & 1), B.abort_flag);
             if (*B.abort_flag) break;
             fence_proxy_async_smem();
+#ifdef OVF_GEMV_NOCOPY
+            mbar_arrive(&B.full[s]);
+#else
             issue_stage(p, L, locate(p, blockIdx.x + it * gridDim.x), ring + (size_t)s * L.stage_bytes, &B.full[s],
                         pol);
+#endif
         }
         return;
     }
@@ -660,6 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         const bool grouped = G < nb;
         const int nslots = half;  // pair mode: slot r sums gate row r and up row r
         unsigned long long best = 0ull;
+        NormChain chain;
         for (int it = 0; it < items; ++it) {
             const int j = it % kTermBufs;
             const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
@@ -704,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                     }
                 }
                 if (p.epi == EPI_SILU_PAIR) {
-                    const float sg = fdiv(1.0f, fadd(1.0f, expf(-y[0])));
+                    const float sg = fdiv(1.0f, fadd(1.0f, exp_rn(-y[0])));
                     p.seg[0].out[row] = fmul(fmul(y[0], sg), y[1]);
                 } else {
                     float *out = p.seg[seg].out;
@@ -718,6 +826,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&B.tfree[j]);
+            if (p.norm_out) {
+                // publish the tile's outputs for the RMSNorm chain of CTA 0
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicExch(&p.tile_flags[blockIdx.x + it * gridDim.x], 1);
+                if (blockIdx.x == 0) chain_norm(p, chain, false);
+            }
+        }
+        if (p.norm_out && blockIdx.x == 0) {
+            chain_norm(p, chain, true);
+            if (lane == 0) *p.norm_out = chain.ok ? rms_scale(chain.acc, p.seg[0].rows, p.eps) : __int_as_float(0x7FC00000);
         }
         if (p.epi == EPI_LOGITS_ARGMAX) {
             // warp max -> one global atomic per CTA; the last CTA to finish
@@ -772,18 +891,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         }
     }
     const int rps = (T + RS - 1) / RS;
-    KqAct kact[KQ ? BPS : 1];
+    KqAct kact[(KQ && kActRegs) ? BPS : 1];
     Q8Act qact[KQ ? 1 : BPS];
 #pragma unroll
     for (int b = 0; b < BPS; ++b) {
+        if (KQ && !kActRegs) continue;
         if (KQ)
             load_kq_act(smem + L.act_q_off + mblk[b] * kQ8kActStride, smem + L.act_meta_off + mblk[b] * kQ8kMetaStride,
-                        kact[KQ ? b : 0]);
+                        kact[(KQ && kActRegs) ? b : 0]);
         else
             load_q8_act(smem + L.act_q_off + mblk[b] * kQ80ActStride, qact[KQ ? 0 : b]);
     }
     const size_t sb = (size_t)(p.K / 8);
+#ifdef OVF_GEMV_TIMING
+    long long t_tf = 0, t_full = 0, t_comp = 0, t_rest = 0, t0 = clock64(), t1;
+#define TMARK(v) t1 = clock64(); v += t1 - t0; t0 = t1;
+#else
+#define TMARK(v)
+#endif
     for (int it = 0; it < items; ++it) {
+        TMARK(t_rest)
         const int s = it % p.stages, j = it % kTermBufs;
         const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
         const int ttype = p.seg[p.pair ? 0 : g.seg].type;  // a tile never mixes types
@@ -792,9 +919,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         const uint8_t *qbase = stage + (((size_t)g.r0 * rb) & 15);
         const uint8_t *sbase = stage + L.s_region + (((size_t)g.r0 * sb) & 15);
         float *tb = tbuf + (size_t)j * T * nb;
+        TMARK(t_rest)
         if (it >= kTermBufs) wait_or_abort(&B.tfree[j], (uint32_t)(((it / kTermBufs) - 1) & 1), B.abort_flag);
+        TMARK(t_tf)
         wait_or_abort(&B.full[s], (uint32_t)((it / p.stages) & 1), B.abort_flag);
+        TMARK(t_full)
+#ifdef OVF_GEMV_NOCOMP
+        for (int rr = 0; rr < 0; ++rr) {
+#else
         for (int rr = 0; rr < rps; ++rr) {
+#endif
             const int r = subset + rr * RS;
             int useg = 0, urow = 0;
             const bool rv = slot_ok && r < T && slot_row(p, g, r, &useg, &urow);
@@ -805,10 +939,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             for (int b = 0; b < BPS; ++b) {
                 if (!mval[b]) continue;
                 float t;
-                if (KQ) {
-                    const KqAct &a = kact[KQ ? b : 0];
+                if (KQ && kActRegs) {
+                    const KqAct &a = kact[(KQ && kActRegs) ? b : 0];
                     t = ttype == OVF_TYPE_Q4_K ? q4k_block(rp + (size_t)mblk[b] * 144, a)
                                                : q6k_block(rp + (size_t)mblk[b] * 210, a);
+                } else if (KQ) {
+                    const uint8_t *aq = smem + L.act_q_off + mblk[b] * kQ8kActStride;
+                    const uint8_t *am = smem + L.act_meta_off + mblk[b] * kQ8kMetaStride;
+                    t = ttype == OVF_TYPE_Q4_K ? q4k_unit(rp + (size_t)mblk[b] * 144, aq, am)
+                                               : q6k_unit(rp + (size_t)mblk[b] * 210, aq, am);
                 } else {
                     const uint8_t *sp = sbase + part * L.s_part + (size_t)i * sb;
                     t = q80_block(rp + 32 * mblk[b], *reinterpret_cast<const float *>(sp + 4 * mblk[b]),
@@ -818,11 +957,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             }
         }
         __syncwarp();
+        TMARK(t_comp)
         if (lane == 0) {
             mbar_arrive(&B.empty[s]);   // the stage may be refilled
             mbar_arrive(&B.tready[j]);  // the terms may be summed (release)
         }
     }
+#ifdef OVF_GEMV_TIMING
+    if (lane == 0 && blockIdx.x == 0)
+        printf("cw %d items %d rps %d T %d S %d tfree %lld full %lld comp %lld rest %lld\n", warp, items, rps, T,
+               p.stages, t_tf, t_full, t_comp, t_rest);
+#endif
 }
 
 // ---------------------------------------------------------------- host side
@@ -873,6 +1018,10 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
                           p.epi == EPI_SILU_PAIR,
                       "gemv: pair mode needs 2 segments of equal shape and type");
     if (p.epi == EPI_RESIDUAL) OVF_CHECK_ARG(p.resid != nullptr, "gemv: residual epilogue without residual");
+    if (p.norm_out)
+        OVF_CHECK_ARG(p.epi == EPI_RESIDUAL && p.nseg == 1 && p.tile_flags != nullptr,
+                      "gemv: an output RMSNorm needs a single-segment residual launch and tile flags");
+    if (p.act_mode == ACT_F32_RMSNORM) OVF_CHECK_ARG(p.norm_scale != nullptr, "gemv: RMSNorm input without its scale");
     if (p.epi == EPI_LOGITS_ARGMAX) OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
 
     int device = 0;
@@ -889,8 +1038,8 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     // ~40 KB of weights per stage.  Among those, take the T that minimises
     // the busiest CTA's streamed bytes plus a fixed per-tile cost (~2 KB
     // equivalent): balanced tile counts matter for the small matrices.
-    const int budget = smem_optin(device) - 1024;
-    const int t_cap = std::max(1, std::min(64, (40 * 1024) / (rb * parts))) * parts;
+    const int budget = (smem_optin(device) + 1024) / kCtasPerSm - 2048;
+    const int t_cap = std::max(1, std::min(64, (OVF_GEMV_TILE_KB * 1024) / (rb * parts))) * parts;
     int best_T = parts;
     double best_cost = 1e300;
     for (int T = parts; T <= t_cap; T += parts) {
@@ -900,7 +1049,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
         else
             for (int s = 0; s < p.nseg; ++s) tiles += (p.seg[s].rows + rows_per - 1) / rows_per;
         if (tiles == 0) break;
-        const int grid = std::min(nsm, tiles);
+        const int grid = std::min(nsm * kCtasPerSm, tiles);
         const double cost = (double)((tiles + grid - 1) / grid) * ((double)T * rb + 2048.0);
         if (cost < best_cost * 0.999) {
             best_cost = cost;
@@ -921,7 +1070,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     p.total_groups = total;
     if (total == 0) return OVF_OK;
 
-    const int grid = std::min(nsm, total);
+    const int grid = std::min(nsm * kCtasPerSm, total);
     const int warps = kThreads / 32;
     int stages = 0;
     size_t smem = 0;
@@ -939,11 +1088,14 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     OVF_CHECK_ARG(stages >= 2, "gemv: K=%d does not fit shared memory", p.K);
     p.stages = stages;
     // Blocks per compute slot: the activation slices live in registers.
-    const int bps = (nb + kComputeThreads - 1) / kComputeThreads;
-    OVF_CHECK_ARG(bps <= (kq ? 1 : 2), "gemv: K=%d is too long (at most %d)", p.K,
-                  kq ? kComputeThreads * 256 : 2 * kComputeThreads * 32);
-    void (*kern)(GemvParams) = kq ? gemv_kernel<true, 1> : (bps == 1 ? gemv_kernel<false, 1> : gemv_kernel<false, 2>);
-    const int ki = (kq ? 0 : 1) + (bps - 1);
+    int bps = (nb + kComputeThreads - 1) / kComputeThreads;
+    OVF_CHECK_ARG(bps <= (kq ? 1 : 4), "gemv: K=%d is too long (at most %d)", p.K,
+                  kq ? kComputeThreads * 256 : 4 * kComputeThreads * 32);
+    if (!kq && bps == 3) bps = 4;
+    void (*kern)(GemvParams) = kq ? gemv_kernel<true, 1>
+                               : (bps == 1 ? gemv_kernel<false, 1>
+                                           : (bps == 2 ? gemv_kernel<false, 2> : gemv_kernel<false, 4>));
+    const int ki = kq ? 0 : (bps == 1 ? 1 : (bps == 2 ? 2 : 3));
     static bool attr_done[64][4] = {};
     if (device < 64 && !attr_done[device][ki]) {
         OVF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin(device)));

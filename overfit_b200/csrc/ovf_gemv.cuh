@@ -17,7 +17,7 @@ namespace ovf {
 enum ActMode : int {
     ACT_PREQ_Q8K = 0,  // Q8_K activation given in global memory (ProjectPreQuantized)
     ACT_F32 = 1,       // fp32 x, quantized inside every CTA (ProjectParallel)
-    ACT_F32_RMSNORM = 2,  // fp32 x -> RMSNorm(gamma, eps) -> quantized
+    ACT_F32_RMSNORM = 2,  // fp32 x -> (x * norm_scale) * gamma -> quantized
 };
 
 enum EpiMode : int {
@@ -68,7 +68,10 @@ struct GemvParams {
     int8_t *aq_out;      // optional copy of the quantized activation (CTA 0)
     float *as_out;
     int16_t *ab_out;
+    const float *norm_scale;  // ACT_F32_RMSNORM: RMSNorm scale of x, computed by its producer
     const float *resid;
+    float *norm_out;     // EPI_RESIDUAL: also produce the RMSNorm scale of the output (eps)
+    int *tile_flags;     // norm_out: per-tile completion flags, zero between launches
     DevStep *step;       // EPI_LOGITS_ARGMAX
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
 };

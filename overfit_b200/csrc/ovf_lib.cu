@@ -6,5 +6,6 @@
 #include "ovf_gemv.cu"
 #include "ovf_ops.cu"
 #include "ovf_attn_cluster.cu"
+#include "ovf_attn_exact.cu"
 #include "ovf_model.cu"
 #include "ovf_noalloc.cu"

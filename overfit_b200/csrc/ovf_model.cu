@@ -59,11 +59,15 @@ struct ovf_session {
     int pos = 0;           // host mirror of DevStep::next_pos
     int n_logits = 0;      // host mirror of DevStep::n_generated
     cudaStream_t stream = nullptr;
-    __half *kc = nullptr, *vc = nullptr;
+    int kv_dtype = OVF_KV_F32;
+    void *kc = nullptr, *vc = nullptr;  // [layers][KVH][max_ctx][hd], fp32 or fp16
     float *hidden = nullptr, *after = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *h = nullptr,
           *gtmp = nullptr, *utmp = nullptr, *logits = nullptr, *rope_cos = nullptr, *rope_sin = nullptr,
           *partial = nullptr;
     int *counters = nullptr, *tokens_log = nullptr;
+    float *norm_s = nullptr;  // [0]: RMSNorm scale of hidden, [1]: of after
+    int *tile_flags = nullptr;
+    int n_tile_flags = 0;
     DevStep *step = nullptr;
     int32_t *pinned_tok = nullptr;  // host staging
     int pinned_cap = 0;
@@ -226,7 +230,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     const ovf_model_config &c = m->cfg;
     const cudaStream_t st = s->stream;
     const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim;
-    ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step, st, true);
+    ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step,
+                                &s->norm_s[0], c.eps, st, true);
     prof_mark(st, "embed");
     if (r) return r;
     for (int l = 0; l < c.n_layers; ++l) {
@@ -244,6 +249,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.act_mode = ACT_F32_RMSNORM;
             p.x = s->hidden;
             p.gamma = L.attn_norm;
+            p.norm_scale = &s->norm_s[0];
             p.eps = c.eps;
             p.epi = EPI_STORE;
             if ((r = gemv_launch(p, st, true))) return r;
@@ -260,6 +266,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.act_mode = ACT_F32_RMSNORM;
                 p.x = s->hidden;
                 p.gamma = L.attn_norm;
+                p.norm_scale = &s->norm_s[0];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
                 if ((r = gemv_launch(p, st, true))) return r;
@@ -270,8 +277,9 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         a.q = s->q;
         a.k_new = s->k;
         a.v_new = s->v;
-        a.kc = s->kc + (size_t)l * KVH * s->max_ctx * hd;
-        a.vc = s->vc + (size_t)l * KVH * s->max_ctx * hd;
+        const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : 2;
+        a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
+        a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
         a.out = s->attn;
         a.rope_cos = s->rope_cos;
         a.rope_sin = s->rope_sin;
@@ -284,7 +292,9 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         a.hd = hd;
         a.max_ctx = s->max_ctx;
         a.scale = 1.0f / sqrtf((float)hd);
-        if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
+        if (s->kv_dtype == OVF_KV_F32) {
+            if ((r = launch_attention_exact(a, s->max_ctx, st, true))) return r;
+        } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
             if ((r = launch_attention_cluster(a, st, true))) return r;
         } else if ((r = launch_attention(a, st, true))) {
             return r;
@@ -302,6 +312,9 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.x = s->attn;
             p.epi = EPI_RESIDUAL;
             p.resid = s->hidden;
+            p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
+            p.tile_flags = s->tile_flags;
+            p.eps = c.eps;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "wo");
         }
@@ -315,6 +328,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.act_mode = ACT_F32_RMSNORM;
             p.x = s->after;
             p.gamma = L.ffn_norm;
+            p.norm_scale = &s->norm_s[1];
             p.eps = c.eps;
             p.epi = EPI_SILU_PAIR;
             if ((r = gemv_launch(p, st, true))) return r;
@@ -330,6 +344,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.act_mode = ACT_F32_RMSNORM;
                 p.x = s->after;
                 p.gamma = L.ffn_norm;
+                p.norm_scale = &s->norm_s[1];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
                 if ((r = gemv_launch(p, st, true))) return r;
@@ -347,6 +362,9 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.x = s->h;
             p.epi = EPI_RESIDUAL;
             p.resid = s->after;
+            p.norm_out = &s->norm_s[0];  // RMSNorm scale of the new hidden: next layer / final norm
+            p.tile_flags = s->tile_flags;
+            p.eps = c.eps;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "down");
         }
@@ -359,6 +377,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         p.act_mode = ACT_F32_RMSNORM;
         p.x = s->hidden;
         p.gamma = m->final_norm;
+        p.norm_scale = &s->norm_s[0];
         p.eps = c.eps;
         p.epi = EPI_LOGITS_ARGMAX;
         p.step = s->step;
@@ -531,12 +550,24 @@ ovf_status ovf_model_destroy(ovf_model *m) {
 int64_t ovf_model_weight_bytes(const ovf_model *m) { return m ? m->weight_bytes : 0; }
 
 ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out) {
+    return ovf_session_create_kv(m, max_ctx, OVF_KV_F32, out);
+}
+
+ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype, ovf_session **out) {
     OVF_CHECK_ARG(m && out, "ovf_session_create: null argument");
     OVF_CHECK_ARG(max_ctx > 0 && max_ctx <= (1 << 20), "ovf_session_create: bad max_ctx");
+    OVF_CHECK_ARG(kv_dtype == OVF_KV_F32 || kv_dtype == OVF_KV_F16, "ovf_session_create: unknown KV dtype %d",
+                  kv_dtype);
+    if (kv_dtype == OVF_KV_F32) {
+        OVF_CHECK_ARG(attn_exact_supported(m->cfg.head_dim), "ovf_session_create: head_dim %d unsupported",
+                      m->cfg.head_dim);
+        OVF_CHECK_ARG(max_ctx <= attn_exact_max_seq(m->cfg.head_dim), "ovf_session_create: max_ctx too large");
+    }
     DeviceGuard guard(m->device);
     ovf_session *s = new ovf_session();
     s->m = m;
     s->max_ctx = max_ctx;
+    s->kv_dtype = kv_dtype;
     const ovf_model_config &c = m->cfg;
     const size_t D = c.d_model, QD = (size_t)c.n_heads * c.head_dim, KD = (size_t)c.n_kv_heads * c.head_dim;
     const size_t kv = (size_t)c.n_layers * KD * max_ctx;
@@ -544,8 +575,9 @@ ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out) 
     auto A = [&](void **p, size_t bytes) {
         if (!st) st = dalloc(s->allocs, p, bytes);
     };
-    A((void **)&s->kc, kv * 2);
-    A((void **)&s->vc, kv * 2);
+    const size_t esz = kv_dtype == OVF_KV_F32 ? 4 : 2;
+    A((void **)&s->kc, kv * esz);
+    A((void **)&s->vc, kv * esz);
     A((void **)&s->hidden, D * 4);
     A((void **)&s->after, D * 4);
     A((void **)&s->q, QD * 4);
@@ -560,13 +592,17 @@ ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out) 
     A((void **)&s->rope_sin, (size_t)max_ctx * c.head_dim / 2 * 4);
     A((void **)&s->partial, (size_t)attn_scratch_bytes(c.n_heads, c.n_kv_heads, c.head_dim));
     A((void **)&s->counters, (size_t)c.n_kv_heads * 4);
+    A((void **)&s->norm_s, 2 * 4);
+    s->n_tile_flags = (int)D;  // a residual launch has at most one tile per output row
+    A((void **)&s->tile_flags, (size_t)s->n_tile_flags * 4);
     A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
     A((void **)&s->step, sizeof(DevStep));
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
     if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->tile_flags, 0, (size_t)s->n_tile_flags * 4), "memset");
     if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
-    if (!st) st = cuda_status(cudaMemset(s->kc, 0, kv * 2), "memset");
-    if (!st) st = cuda_status(cudaMemset(s->vc, 0, kv * 2), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->kc, 0, kv * esz), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->vc, 0, kv * esz), "memset");
     if (!st) st = fill_rope_tables(s);
     if (!st) {
         s->pinned_cap = max_ctx + 1;

@@ -325,25 +325,19 @@ ovf_status launch_attention(const AttnParams &p0, cudaStream_t st, bool pdl) {
 }
 
 // ------------------------------------------------------------------ RMSNorm
+// Runtime/CachedTransformerBlock.cs:525-552 (RmsNormalize): warp 0 runs
+// the sequential sum of squares, then every thread scales its elements as
+// (x * scale) * gamma.  Bit-identical to the reference.
 __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gm, float *__restrict__ y,
                                int64_t d, float eps) {
-    __shared__ float red[33];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    float s = 0.0f;
-    for (int64_t i = tid; i < d; i += blockDim.x) s = fadd(s, fmul(x[i], x[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s = fadd(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    if (warp == 0) {
-        float v = lane < nw ? red[lane] : 0.0f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-        if (lane == 0) red[32] = fdiv(1.0f, sqrtf(fadd(fdiv(v, (float)d), eps)));
+    __shared__ float sc;
+    if (threadIdx.x < 32) {
+        const float ss = warp_seq_sumsq(x, (int)d, 0.0f);
+        if (threadIdx.x == 0) sc = rms_scale(ss, (int)d, eps);
     }
     __syncthreads();
-    const float sc = red[32];
-    for (int64_t i = tid; i < d; i += blockDim.x) y[i] = gm ? fmul(fmul(x[i], sc), gm[i]) : fmul(x[i], sc);
+    const float scale = sc;
+    for (int64_t i = threadIdx.x; i < d; i += blockDim.x) y[i] = gm ? fmul(fmul(x[i], scale), gm[i]) : fmul(x[i], scale);
 }
 
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st) {
@@ -366,32 +360,37 @@ ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float 
 // ------------------------------------------------------------ embedding row
 // CachedLlamaSession.EmbedAndAdvance (:851-868): decode row `token` of the
 // embedding (DecodeWeight.DequantizeRow) into hidden and advance the
-// position.  Block 0 / thread 0 owns the position update.
+// position; then warp 0 runs the first layer's RMSNorm sum of squares in
+// the reference's order and leaves the scale in norm_out (one CTA).
 __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict__ w, const float *__restrict__ q8s,
-                             int d, float *__restrict__ hidden) {
+                             int d, float *__restrict__ hidden, float *norm_out, float eps) {
     pdl_wait();
     const int token = step->token;
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < d) {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
         float v;
-        if (type == OVF_TYPE_Q4_K) v = q4k_elem(w + ((int64_t)token * (d / 256) + i / 256) * 144, (int)(i % 256));
-        else if (type == OVF_TYPE_Q6_K) v = q6k_elem(w + ((int64_t)token * (d / 256) + i / 256) * 210, (int)(i % 256));
+        if (type == OVF_TYPE_Q4_K) v = q4k_elem(w + ((int64_t)token * (d / 256) + i / 256) * 144, i % 256);
+        else if (type == OVF_TYPE_Q6_K) v = q6k_elem(w + ((int64_t)token * (d / 256) + i / 256) * 210, i % 256);
         else if (type == OVF_TYPE_Q8_0)
             v = fmul(q8s[(int64_t)token * (d / 32) + i / 32], (float)reinterpret_cast<const int8_t *>(w)[(int64_t)token * d + i]);
         else v = reinterpret_cast<const float *>(w)[(int64_t)token * d + i];
         hidden[i] = v;
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
         step->cur_pos = step->next_pos;
         step->next_pos += 1;
+    }
+    if (threadIdx.x < 32 && norm_out) {
+        const float ss = warp_seq_sumsq(hidden, d, 0.0f);
+        if (threadIdx.x == 0) *norm_out = rms_scale(ss, d, eps);
     }
     pdl_launch_dependents();
 }
 
 ovf_status launch_embed(const DevStep *, int type, const void *w, const float *q8s, int d, float *hidden,
-                        DevStep *step, cudaStream_t st, bool pdl) {
-    cudaError_t e = launch_pdl(embed_kernel, dim3((d + 255) / 256), dim3(256), 0, st, pdl, step, type,
-                               (const uint8_t *)w, q8s, d, hidden);
+                        DevStep *step, float *norm_out, float eps, cudaStream_t st, bool pdl) {
+    cudaError_t e = launch_pdl(embed_kernel, dim3(1), dim3(1024), 0, st, pdl, step, type, (const uint8_t *)w, q8s, d,
+                               hidden, norm_out, eps);
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "embed");
 }
 
@@ -403,7 +402,7 @@ __global__ void silu_mul_kernel(const float *g, const float *u, float *h, int64_
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
         const float x = g[i];
-        const float sg = fdiv(1.0f, fadd(1.0f, expf(-x)));
+        const float sg = fdiv(1.0f, fadd(1.0f, exp_rn(-x)));
         h[i] = fmul(fmul(x, sg), u[i]);
     }
     pdl_launch_dependents();

@@ -99,8 +99,10 @@ class CudaLlamaInferenceEngine:
     def vocabulary_size(self) -> int:
         return self.cfg["vocab"]
 
-    def create_session(self, max_context: int) -> "CudaLlamaSession":
-        return CudaLlamaSession(self, max_context)
+    def create_session(self, max_context: int, kv_cache_dtype: str = "f32") -> "CudaLlamaSession":
+        """CreateSession(maxContextLength, kvCacheDType): "f32" (the reference's
+        default, bit-exact attention) or "f16" (no reference counterpart)."""
+        return CudaLlamaSession(self, max_context, kv_cache_dtype)
 
     def close(self):
         if self._h:
@@ -118,11 +120,17 @@ class CudaLlamaSession:
     """ISlmSession over the device-resident decode loop (greedy sampling on
     the device; logits are copied out only when asked for)."""
 
-    def __init__(self, engine: CudaLlamaInferenceEngine, max_context: int):
+    KV_DTYPES = {"f32": 0, "f16": 2}
+
+    def __init__(self, engine: CudaLlamaInferenceEngine, max_context: int, kv_cache_dtype: str = "f32"):
         self.engine = engine
         self.max_context_length = max_context
+        if kv_cache_dtype not in self.KV_DTYPES:
+            raise ValueError(f"kv_cache_dtype must be one of {sorted(self.KV_DTYPES)}")
+        self.kv_cache_dtype = kv_cache_dtype
         h = C.c_void_p()
-        check(_lib.load().ovf_session_create(engine._h, max_context, C.byref(h)), "ovf_session_create")
+        check(_lib.load().ovf_session_create_kv(engine._h, max_context, self.KV_DTYPES[kv_cache_dtype], C.byref(h)),
+              "ovf_session_create")
         self._h = h
         self._logits = np.zeros(engine.cfg["vocab"], np.float32)
         self._have_logits = False

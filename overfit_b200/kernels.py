@@ -334,6 +334,17 @@ class CachedAttentionKernel:
         return int(_lib.load().ovf_attention_scratch_bytes(n_heads, n_kv_heads, head_dim))
 
     @staticmethod
+    def compute_single_head_all(query, k_cache, v_cache, output, n_heads, n_kv_heads, head_dim, seq_len,
+                                scale) -> None:
+        """ComputeSingleHead (Runtime/CachedAttentionKernel.cs:36-128) for every
+        query head, over F32 caches [n_kv_heads, max_ctx, hd], in the
+        reference's operation order (bit-identical)."""
+        max_ctx = k_cache.shape[1]
+        check(_lib.load().ovf_attention_single_head(_ptr(query), _ptr(k_cache), _ptr(v_cache), _ptr(output),
+                                                    n_heads, n_kv_heads, head_dim, max_ctx, seq_len, float(scale),
+                                                    _stream()), "ComputeSingleHead")
+
+    @staticmethod
     def compute_all_heads(query, k_cache, v_cache, output, n_heads, n_kv_heads, head_dim, seq_len, scale,
                           scratch, counters) -> None:
         """ComputeSingleHead (Runtime/CachedAttentionKernel.cs:36-128) for every
