@@ -157,24 +157,90 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 
 // Running fp32 sum of squares over x[0..n) in index order — the
 // reference's sequential RMSNorm loop (Runtime/CachedTransformerBlock.cs:
-// 532-536), bit for bit — computed by one warp: lanes square 32 elements at
-// a time (the next 32 are loaded meanwhile) and the running sum takes them
-// in order through shuffles.  Every lane returns the same sum.
+// 532-536), bit for bit — computed by one warp.  The lanes hold 512
+// elements at a time in registers (the next 512 are loaded meanwhile, so
+// the loads hide behind the chain), square them, and the running sum takes
+// them in order through shuffles: about one dependent add per element.
+// Every lane returns the same sum.
 __device__ __forceinline__ float warp_seq_sumsq(const float *x, int n, float acc) {
+    constexpr int V = 16;  // elements per lane per batch
     const int lane = threadIdx.x & 31;
-    float nxt = lane < n ? __ldcg(x + lane) : 0.0f;
-    for (int b = 0; b < n; b += 32) {
-        const float sq = fmul(nxt, nxt);
-        const int m = min(32, n - b);
-        nxt = b + 32 + lane < n ? __ldcg(x + b + 32 + lane) : 0.0f;
-        if (m == 32) {
+    float cur[V], nxt[V];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
-        } else {
-            for (int j = 0; j < m; ++j) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, j));
+    for (int j = 0; j < V; ++j) cur[j] = 32 * j + lane < n ? __ldcg(x + 32 * j + lane) : 0.0f;
+    for (int b = 0; b < n; b += 32 * V) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int i = b + 32 * V + 32 * j + lane;
+            nxt[j] = i < n ? __ldcg(x + i) : 0.0f;
         }
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int m = min(32, n - (b + 32 * j));
+            if (m <= 0) break;
+            const float sq = fmul(cur[j], cur[j]);
+            if (m == 32) {
+#pragma unroll
+                for (int l = 0; l < 32; ++l) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, l));
+            } else {
+                for (int l = 0; l < m; ++l) acc = fadd(acc, __shfl_sync(0xFFFFFFFFu, sq, l));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < V; ++j) cur[j] = nxt[j];
     }
     return acc;
+}
+
+// The same running sum formed by a whole CTA: the threads square 1024
+// elements at a time into shared memory (`stage`, 2 x 1024 floats, double
+// buffered) while thread 0 adds the previous 1024 in order, four per
+// shared-memory load — one dependent add per element.  Called by every
+// thread of the CTA; every thread returns the sum.
+__device__ __forceinline__ float cta_seq_sumsq(const float *x, int n, float acc, float *stage) {
+    __shared__ float s_acc;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) s_acc = acc;
+    for (int i = tid; i < 1024 && i < n; i += nt) stage[i] = fmul(__ldcg(x + i), __ldcg(x + i));
+    __syncthreads();
+    for (int b = 0, buf = 0; b < n; b += 1024, buf ^= 1) {
+        const int m = min(1024, n - b);
+        if (tid == 0) {
+            const float4 *sv = reinterpret_cast<const float4 *>(stage + buf * 1024);
+            float a = s_acc;
+            const int m32 = m & ~31;
+            // 32 elements in registers ahead of the chain
+            float4 cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = m32 ? sv[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < m32; i += 32) {
+                float4 nxt[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = i + 32 < m32 ? sv[(i + 32) / 4 + j] : cur[j];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    a = fadd(a, cur[j].x);
+                    a = fadd(a, cur[j].y);
+                    a = fadd(a, cur[j].z);
+                    a = fadd(a, cur[j].w);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            }
+            for (int i = m32; i < m; ++i) a = fadd(a, stage[buf * 1024 + i]);
+            s_acc = a;
+        } else {
+            float *nx = stage + (buf ^ 1) * 1024;
+            for (int i = tid - 1; i < 1024 && b + 1024 + i < n; i += nt - 1) {
+                const float v = __ldcg(x + b + 1024 + i);
+                nx[i] = fmul(v, v);
+            }
+        }
+        __syncthreads();
+    }
+    const float r = s_acc;
+    __syncthreads();
+    return r;
 }
 
 // RMSNorm scale from the sum of squares: 1 / sqrt(sumSq / d + eps).

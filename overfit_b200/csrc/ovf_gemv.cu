@@ -661,46 +661,43 @@ __device__ __forceinline__ void wait_or_abort(uint64_t *bar, uint32_t parity, vo
     if (!mbar_wait_sleep_bounded(bar, parity)) *abort_flag = 1;
 }
 
-// RMSNorm of a residual output (EPI_RESIDUAL with norm_out): the sum warp of
-// CTA 0 walks the output rows in index order as their tiles complete
-// (per-tile flags, set by each tile's sum warp after its stores) and keeps
-// the reference's sequential fp32 sum of squares; the scale it leaves in
-// norm_out spares every CTA of the consuming kernel a reduction, and
-// reproduces the reference's RmsNormalize bit for bit.  CTA 0 resets each
-// flag it consumes, so the flags are zero again for the next launch.
-struct NormChain {
-    int tile = 0;     // next tile to add
+// RMSNorm of a residual output (EPI_RESIDUAL with norm_out): CTA 0 takes no
+// tiles; it walks the output rows in index order and keeps the reference's
+// sequential fp32 sum of squares, and the scale it leaves in norm_out spares
+// every CTA of the consuming kernel a reduction and reproduces the
+// reference's RmsNormalize bit for bit.  Tiles finish in waves (wave k =
+// tiles [k*tgrid, (k+1)*tgrid), whose rows are contiguous): each tile's sum
+// warp bumps its wave's counter after its stores, and the chain takes a
+// wave once its counter is full, so it trails the GEMV by about one wave.
+// The counters are reset as they are consumed (zero for the next launch).
+__device__ __noinline__ void norm_cta(const GemvParams &p, int tgrid, float *stage) {
+    __shared__ int s_n;
+    const int nwaves = (p.total_groups + tgrid - 1) / tgrid;
     float acc = 0.0f;
     bool ok = true;
-};
-
-__device__ __noinline__ void chain_norm(const GemvParams &p, NormChain &c, bool block) {
-    const int lane = threadIdx.x & 31;
-    while (c.ok && c.tile < p.total_groups) {
-        int f = 0;
-        if (lane == 0) {
-            volatile int *fl = p.tile_flags + c.tile;
-            f = *fl;
-            for (uint32_t i = 0; !f && block && i < (1u << 22); ++i) {
-                __nanosleep(64);
-                f = *fl;
+    for (int w = 0; w < nwaves && ok; ++w) {
+        const int first = w * tgrid, ntiles = min(tgrid, p.total_groups - first);
+        if (threadIdx.x == 0) {
+            volatile int *cnt = p.tile_flags + w;
+            int n = *cnt;
+            for (uint32_t i = 0; n < ntiles && i < (1u << 22); ++i) {
+                __nanosleep(32);
+                n = *cnt;
             }
+            s_n = n;
+            if (n >= ntiles) *cnt = 0;
         }
-        f = __shfl_sync(0xFFFFFFFFu, f, 0);
-        if (!f) {
-            if (block) {
-                c.ok = false;
-                if (lane == 0) raise_dev_error(DEVERR_COUNTER);
-            }
-            return;
+        __syncthreads();
+        if (s_n < ntiles) {
+            ok = false;
+            if (threadIdx.x == 0) raise_dev_error(DEVERR_COUNTER);
+            break;
         }
         __threadfence();
-        const GroupRef g = locate(p, c.tile);
-        c.acc = warp_seq_sumsq(p.seg[0].out + g.r0, g.nr, c.acc);
-        __syncwarp();
-        if (lane == 0) p.tile_flags[c.tile] = 0;
-        ++c.tile;
+        const GroupRef g0 = locate(p, first), g1 = locate(p, first + ntiles - 1);
+        acc = cta_seq_sumsq(p.seg[0].out + g0.r0, g1.r0 + g1.nr - g0.r0, acc, stage);
     }
+    if (threadIdx.x == 0) *p.norm_out = ok ? rms_scale(acc, p.seg[0].rows, p.eps) : __int_as_float(0x7FC00000);
 }
 
 template <bool KQ, int BPS>
@@ -712,7 +709,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     uint8_t *ring = smem + L.stage_off;
     float *tbuf = reinterpret_cast<float *>(smem + L.terms_off);
     const int T = p.rows_per_group, nb = L.nb;
-    const int items = blockIdx.x < p.total_groups ? (p.total_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    // With an output RMSNorm, CTA 0 only runs the norm chain and the others
+    // take the tiles: tile = tcta + i * tgrid.
+    const int nfirst = p.norm_out ? 1 : 0;
+    const int tgrid = (int)gridDim.x - nfirst, tcta = (int)blockIdx.x - nfirst;
+    const int items = tcta >= 0 && tcta < p.total_groups ? (p.total_groups - tcta + tgrid - 1) / tgrid : 0;
 
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
@@ -732,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     if (warp == kProducerWarp && lane == 0) {
         pol = l2_evict_first_policy();
         for (int it = 0; it < p.stages && it < items; ++it)
-            issue_stage(p, L, locate(p, blockIdx.x + it * gridDim.x), ring + (size_t)it * L.stage_bytes, &B.full[it],
+            issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)it * L.stage_bytes, &B.full[it],
                         pol);
     }
 
@@ -740,7 +741,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     if (KQ) prep_q8k(p, L, smem);
     else prep_q80(p, L, smem);
     __syncthreads();
-    pdl_launch_dependents();
+    // A launch that forms an output RMSNorm lets its dependent start only as
+    // its CTAs finish (completion is the trigger): dependent CTAs scheduled
+    // early could otherwise take the SM slots of this grid's not-yet-resident
+    // CTAs, whose tiles the norm chain of CTA 0 waits for.
+    if (!p.norm_out) pdl_launch_dependents();
+    if (p.norm_out && blockIdx.x == 0) {
+        norm_cta(p, tgrid, reinterpret_cast<float *>(ring));
+        return;
+    }
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------- producer
@@ -753,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
 #ifdef OVF_GEMV_NOCOPY
             mbar_arrive(&B.full[s]);
 #else
-            issue_stage(p, L, locate(p, blockIdx.x + it * gridDim.x), ring + (size_t)s * L.stage_bytes, &B.full[s],
+            issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)s * L.stage_bytes, &B.full[s],
                         pol);
 #endif
         }
@@ -767,10 +776,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
         const bool grouped = G < nb;
         const int nslots = half;  // pair mode: slot r sums gate row r and up row r
         unsigned long long best = 0ull;
-        NormChain chain;
         for (int it = 0; it < items; ++it) {
             const int j = it % kTermBufs;
-            const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
+            const GroupRef g = locate(p, tcta + it * tgrid);
             for (int slot = lane; slot < ((nslots + 31) & ~31); slot += 32) {
                 int seg = 0, row = 0;
                 const bool valid = slot < nslots && slot_row(p, g, slot, &seg, &row);
@@ -827,16 +835,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             __syncwarp();
             if (lane == 0) mbar_arrive(&B.tfree[j]);
             if (p.norm_out) {
-                // publish the tile's outputs for the RMSNorm chain of CTA 0
+                // publish the tile's outputs to the norm chain of CTA 0
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) atomicExch(&p.tile_flags[blockIdx.x + it * gridDim.x], 1);
-                if (blockIdx.x == 0) chain_norm(p, chain, false);
+                if (lane == 0) atomicAdd(&p.tile_flags[it], 1);  // wave `it`
             }
-        }
-        if (p.norm_out && blockIdx.x == 0) {
-            chain_norm(p, chain, true);
-            if (lane == 0) *p.norm_out = chain.ok ? rms_scale(chain.acc, p.seg[0].rows, p.eps) : __int_as_float(0x7FC00000);
         }
         if (p.epi == EPI_LOGITS_ARGMAX) {
             // warp max -> one global atomic per CTA; the last CTA to finish
@@ -912,7 +915,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     for (int it = 0; it < items; ++it) {
         TMARK(t_rest)
         const int s = it % p.stages, j = it % kTermBufs;
-        const GroupRef g = locate(p, blockIdx.x + it * gridDim.x);
+        const GroupRef g = locate(p, tcta + it * tgrid);
         const int ttype = p.seg[p.pair ? 0 : g.seg].type;  // a tile never mixes types
         const size_t rb = (size_t)row_bytes(ttype, p.K);
         const uint8_t *stage = ring + (size_t)s * L.stage_bytes;
@@ -1038,7 +1041,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     // ~40 KB of weights per stage.  Among those, take the T that minimises
     // the busiest CTA's streamed bytes plus a fixed per-tile cost (~2 KB
     // equivalent): balanced tile counts matter for the small matrices.
-    const int budget = (smem_optin(device) + 1024) / kCtasPerSm - 2048;
+    const int budget = (smem_optin(device) + 1024) / kCtasPerSm - 2048;  // leaves room for static smem
     const int t_cap = std::max(1, std::min(64, (OVF_GEMV_TILE_KB * 1024) / (rb * parts))) * parts;
     int best_T = parts;
     double best_cost = 1e300;
@@ -1070,7 +1073,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     p.total_groups = total;
     if (total == 0) return OVF_OK;
 
-    const int grid = std::min(nsm * kCtasPerSm, total);
+    const int grid = std::min(nsm * kCtasPerSm, total + (p.norm_out ? 1 : 0));
     const int warps = kThreads / 32;
     int stages = 0;
     size_t smem = 0;
@@ -1098,7 +1101,10 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     const int ki = kq ? 0 : (bps == 1 ? 1 : (bps == 2 ? 2 : 3));
     static bool attr_done[64][4] = {};
     if (device < 64 && !attr_done[device][ki]) {
-        OVF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin(device)));
+        cudaFuncAttributes fa{};
+        OVF_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+        OVF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          smem_optin(device) - (int)fa.sharedSizeBytes));
         attr_done[device][ki] = true;
     }
     if (plan_out) *plan_out = GemvPlan{T, stages, warps, grid, smem};

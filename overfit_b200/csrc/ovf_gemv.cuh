@@ -71,7 +71,7 @@ struct GemvParams {
     const float *norm_scale;  // ACT_F32_RMSNORM: RMSNorm scale of x, computed by its producer
     const float *resid;
     float *norm_out;     // EPI_RESIDUAL: also produce the RMSNorm scale of the output (eps)
-    int *tile_flags;     // norm_out: per-tile completion flags, zero between launches
+    int *tile_flags;     // norm_out: per-wave tile counters (>= tiles / grid), zero between launches
     DevStep *step;       // EPI_LOGITS_ARGMAX
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
 };

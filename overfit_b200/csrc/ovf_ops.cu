@@ -330,13 +330,8 @@ ovf_status launch_attention(const AttnParams &p0, cudaStream_t st, bool pdl) {
 // (x * scale) * gamma.  Bit-identical to the reference.
 __global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ gm, float *__restrict__ y,
                                int64_t d, float eps) {
-    __shared__ float sc;
-    if (threadIdx.x < 32) {
-        const float ss = warp_seq_sumsq(x, (int)d, 0.0f);
-        if (threadIdx.x == 0) sc = rms_scale(ss, (int)d, eps);
-    }
-    __syncthreads();
-    const float scale = sc;
+    __shared__ __align__(16) float stage[2048];
+    const float scale = rms_scale(cta_seq_sumsq(x, (int)d, 0.0f, stage), (int)d, eps);
     for (int64_t i = threadIdx.x; i < d; i += blockDim.x) y[i] = gm ? fmul(fmul(x[i], scale), gm[i]) : fmul(x[i], scale);
 }
 
@@ -380,8 +375,9 @@ __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict_
         step->cur_pos = step->next_pos;
         step->next_pos += 1;
     }
-    if (threadIdx.x < 32 && norm_out) {
-        const float ss = warp_seq_sumsq(hidden, d, 0.0f);
+    if (norm_out) {
+        __shared__ __align__(16) float stage[2048];
+        const float ss = cta_seq_sumsq(hidden, d, 0.0f, stage);
         if (threadIdx.x == 0) *norm_out = rms_scale(ss, d, eps);
     }
     pdl_launch_dependents();
