@@ -211,9 +211,23 @@ def gemv_roofline(torch, eng_cfg, model_file, device, peaks) -> dict:
     peak = peaks.get("hbm_gbs", 6650.0)
     del gates, ups
     return {"bound": "hbm", "kernel": "gemv_kernel (Q4_K gate+up pair, 2x14336x4096)", "achieved": achieved,
-            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": profiled_traffic(),
             "launch_us": dt * 1e6, "algorithmic_bytes": alg,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback 6650"}
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the gate/up GEMV from the committed ncu
+    summary (profiles/gemv_q4k_gateup.md, line `traffic_bytes_per_launch:`),
+    or None when no capture has been summarised."""
+    p = os.path.join(ROOT, "profiles", "gemv_q4k_gateup.md")
+    try:
+        for ln in open(p):
+            if ln.strip().startswith("traffic_bytes_per_launch:"):
+                return float(ln.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
 
 
 def run_ours(args):
@@ -286,7 +300,8 @@ def run_ours(args):
     e2e = world * e2e_steps / e2e_dt
 
     weight_bytes = eng.weight_bytes
-    kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * 2 * (args.prompt + args.warmup +
+    # F32 KV cache (the reference's default): K and V read once per step
+    kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * 4 * (args.prompt + args.warmup +
                                                                                 args.steps // 2)
     roof = gemv_roofline(torch, cfg, mf, device, peaks) if rank == 0 else None
     sess.close()

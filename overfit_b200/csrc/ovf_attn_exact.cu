@@ -33,16 +33,16 @@ namespace cg = cooperative_groups;
 
 static constexpr int kExactCluster = 8;     // CTAs per query head
 static constexpr int kExactThreads = 128;
+static constexpr int kExactMaxSeq = 32768;  // the whole probability vector sits in each CTA's shared memory
+static constexpr int kVBlock = 256;         // positions per staged value block
 
 int64_t attn_exact_smem_bytes(int hd, int seq_len) {
     const int chunk = (seq_len + kExactCluster - 1) / kExactCluster;
-    return (int64_t)(3 * hd + chunk + 8) * 4;
+    const int dpc = hd / kExactCluster;
+    return (int64_t)(3 * hd + 8 + chunk + ((seq_len + 3) & ~3) + 2 * kVBlock * dpc) * 4 + 16;
 }
 
-int attn_exact_max_seq(int hd) {
-    // the per-CTA score slice lives in shared memory (up to ~200 KB)
-    return (int)((200 * 1024 / 4 - 3 * hd - 8) * kExactCluster);
-}
+int attn_exact_max_seq(int) { return kExactMaxSeq; }
 
 template <int HD>
 __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactThreads)
@@ -94,24 +94,26 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
 #pragma unroll
     for (int i = 0; i < HD / 16; ++i) qreg[i] = qs[16 * i + c];
     float lmax = -INFINITY;
-    constexpr int KPI = 2 * (kExactThreads / 32);  // keys per pass of the CTA
-    for (int tb = t0; tb < t1; tb += 2 * KPI) {
-        float acc[2];
+    constexpr int KPI = 2 * (kExactThreads / 32);  // keys per step of the CTA (a half-warp each)
+    constexpr int U = HD <= 128 ? 8 : 4;            // keys per half-warp in flight
+    for (int tb = t0; tb < t1; tb += U * KPI) {
+        float kv[U][HD / 16];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < U; ++u) {
             const int t = tb + u * KPI + 2 * warp + hw;
             const bool ok = t < t1;
             const float *kr = (has_new && t == pos) ? kn : kf + (size_t)(ok ? t : t0) * HD;
-            float a = 0.0f;
 #pragma unroll
-            for (int i = 0; i < HD / 16; ++i) a = fadd(a, fmul(qreg[i], kr[16 * i + c]));
-            acc[u] = a;
+            for (int i = 0; i < HD / 16; ++i) kv[u][i] = kr[16 * i + c];
         }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
+        for (int u = 0; u < U; ++u) {
             const int t = tb + u * KPI + 2 * warp + hw;
+            float a = 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD / 16; ++i) a = fadd(a, fmul(qreg[i], kv[u][i]));
             // v[j] = acc0[j] + acc1[j], then ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7))
-            float v = fadd(acc[u], __shfl_xor_sync(0xFFFFFFFFu, acc[u], 8));
+            float v = fadd(a, __shfl_xor_sync(0xFFFFFFFFu, a, 8));
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
@@ -138,22 +140,71 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     for (int t = t0 + tid; t < t1; t += kExactThreads) ex[t - t0] = exp_rn(fsub(ex[t - t0], gmax));
     cluster.sync();
 
-    // 3. sumExp over t in order (every CTA forms the same chain)
+    // 3. every CTA gathers all probabilities' numerators into its own shared
+    //    memory, then thread 0 forms sumExp over t in order (the same chain,
+    //    so the same value, in every CTA)
+    float *eall = ex + chunk;  // [seq], 16-byte aligned below
+    eall = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(eall) + 15) & ~uintptr_t(15));
+    {
+        // all slices at once: eight remote loads in flight per thread
+        constexpr int GU = 8;
+        for (int base = 0; base < seq; base += GU * kExactThreads) {
+            float tmp[GU];
+#pragma unroll
+            for (int j = 0; j < GU; ++j) {
+                const int t = base + j * kExactThreads + tid;
+                const int r = t < seq ? t / chunk : 0;
+                tmp[j] = t < seq ? cluster.map_shared_rank(ex, r)[t - r * chunk] : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < GU; ++j) {
+                const int t = base + j * kExactThreads + tid;
+                if (t < seq) eall[t] = tmp[j];
+            }
+        }
+    }
+    constexpr int DPC = HD / kExactCluster;
+    float *vbuf = eall + ((seq + 3) & ~3);  // [2][kVBlock][DPC] staged values of this CTA's dimensions
+    const int d0 = rank * DPC;
+    // float4 pieces of a block: kVBlock rows x DPC/4, eight in flight per thread
+    constexpr int Q4 = DPC / 4, NQ = kVBlock * Q4 / kExactThreads;
+    auto stage_values = [&](int blk) {
+        float4 *dst = reinterpret_cast<float4 *>(vbuf + (blk & 1) * kVBlock * DPC);
+        const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+        float4 tmp[NQ];
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) {
+            const int i = tid + j * kExactThreads, t = i / Q4, q4 = i % Q4;
+            tmp[j] = t < n ? *reinterpret_cast<const float4 *>(vf + (size_t)(tb + t) * HD + d0 + 4 * q4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);  // the row at `pos` is replaced from vn below
+        }
+#pragma unroll
+        for (int j = 0; j < NQ; ++j) dst[tid + j * kExactThreads] = tmp[j];
+    };
+    stage_values(0);
+    __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
-        for (int r = 0; r < kExactCluster; ++r) {
-            const int a = min(seq, r * chunk), b = min(seq, a + chunk);
-            const float *e = cluster.map_shared_rank(ex, r);
-            int t = 0;
-            for (; t + 8 <= b - a; t += 8) {
-                float v[8];
+        const int s32 = seq & ~31;
+        const float4 *e4 = reinterpret_cast<const float4 *>(eall);
+        float4 cur[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = e[t + j];
+        for (int j = 0; j < 8; ++j) cur[j] = s32 ? e4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < s32; i += 32) {
+            float4 nxt[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sum = fadd(sum, v[j]);
+            for (int j = 0; j < 8; ++j) nxt[j] = i + 32 < s32 ? e4[(i + 32) / 4 + j] : cur[j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                sum = fadd(sum, cur[j].x);
+                sum = fadd(sum, cur[j].y);
+                sum = fadd(sum, cur[j].z);
+                sum = fadd(sum, cur[j].w);
             }
-            for (; t < b - a; ++t) sum = fadd(sum, e[t]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
         }
+        for (int t = s32; t < seq; ++t) sum = fadd(sum, eall[t]);
         red[5] = sum;
     }
     __syncthreads();
@@ -161,35 +212,37 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const bool bad = !(sumExp > 0.0f) || isinf(sumExp);
     const float invSum = bad ? 0.0f : fdiv(1.0f, sumExp);
 
-    // 4. out[d] for this CTA's dimensions, over t in order
-    constexpr int DPC = HD / kExactCluster;
-    if (tid < DPC) {
-        const int d = rank * DPC + tid;
-        float acc = 0.0f;
-        if (!bad) {
-            for (int r = 0; r < kExactCluster; ++r) {
-                const int a = min(seq, r * chunk), b = min(seq, a + chunk);
-                const float *e = cluster.map_shared_rank(ex, r);
-                int t = a;
-                for (; t + 4 <= b; t += 4) {
-                    float ev[4], vv[4];
+    // 4. out[d] for this CTA's dimensions over t in order; the values are
+    //    staged block by block in shared memory by all threads while the
+    //    DPC chain threads consume the previous block
+    float acc = 0.0f;
+    const int nblk = (seq + kVBlock - 1) / kVBlock;
+    const float vnew_d = tid < DPC && has_new ? vn[d0 + tid] : 0.0f;
+    for (int blk = 0; blk < nblk; ++blk) {
+        if (blk + 1 < nblk) stage_values(blk + 1);
+        if (tid < DPC && !bad) {
+            const float *vb = vbuf + (blk & 1) * kVBlock * DPC + tid;
+            const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+            int i = 0;
+            for (; i + 8 <= n; i += 8) {
+                float ev[8], vv[8];
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        ev[j] = e[t + j - a];
-                        vv[j] = (has_new && t + j == pos) ? vn[d] : vf[(size_t)(t + j) * HD + d];
-                    }
+                for (int j = 0; j < 8; ++j) {
+                    ev[j] = eall[tb + i + j];
+                    vv[j] = (has_new && tb + i + j == pos) ? vnew_d : vb[(i + j) * DPC];
+                }
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) acc = fadd(acc, fmul(fmul(ev[j], invSum), vv[j]));
-                }
-                for (; t < b; ++t) {
-                    const float vv = (has_new && t == pos) ? vn[d] : vf[(size_t)t * HD + d];
-                    acc = fadd(acc, fmul(fmul(e[t - a], invSum), vv));
-                }
+                for (int j = 0; j < 8; ++j) acc = fadd(acc, fmul(fmul(ev[j], invSum), vv[j]));
+            }
+            for (; i < n; ++i) {
+                const float vv = (has_new && tb + i == pos) ? vnew_d : vb[i * DPC];
+                acc = fadd(acc, fmul(fmul(eall[tb + i], invSum), vv));
             }
         }
-        p.out[(size_t)h * HD + d] = acc;
+        __syncthreads();
     }
-    cluster.sync();  // no CTA leaves while another still reads its shared memory
+    if (tid < DPC) p.out[(size_t)h * HD + d0 + tid] = acc;
+    cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }

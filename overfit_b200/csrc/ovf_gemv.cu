@@ -671,33 +671,79 @@ __device__ __forceinline__ void wait_or_abort(uint64_t *bar, uint32_t parity, vo
 // wave once its counter is full, so it trails the GEMV by about one wave.
 // The counters are reset as they are consumed (zero for the next launch).
 __device__ __noinline__ void norm_cta(const GemvParams &p, int tgrid, float *stage) {
-    __shared__ int s_n;
+    __shared__ int s_fail;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int rows = p.seg[0].rows, T = p.rows_per_group;
     const int nwaves = (p.total_groups + tgrid - 1) / tgrid;
-    float acc = 0.0f;
-    bool ok = true;
-    for (int w = 0; w < nwaves && ok; ++w) {
-        const int first = w * tgrid, ntiles = min(tgrid, p.total_groups - first);
-        if (threadIdx.x == 0) {
-            volatile int *cnt = p.tile_flags + w;
-            int n = *cnt;
-            for (uint32_t i = 0; n < ntiles && i < (1u << 22); ++i) {
-                __nanosleep(32);
-                n = *cnt;
+    const int nchunks = (rows + 1023) / 1024;
+    int waves_done = 0;  // thread 32's view
+    if (tid == 0) s_fail = 0;
+    __syncthreads();
+    // warps 1..: wait until the tiles covering chunk c have finished, then
+    // stage the chunk's squares in stage[buf]
+    auto stage_chunk = [&](int c, int buf) {
+        const int r0 = 1024 * c, r1 = min(rows, r0 + 1024);
+        if (tid == 32) {
+            const int need = min(nwaves - 1, ((r1 - 1) / T) / tgrid);
+            while (waves_done <= need && !s_fail) {
+                const int ntiles = min(tgrid, p.total_groups - waves_done * tgrid);
+                volatile int *cnt = p.tile_flags + waves_done;
+                int n = *cnt;
+                for (uint32_t i = 0; n < ntiles && i < (1u << 22); ++i) {
+                    __nanosleep(32);
+                    n = *cnt;
+                }
+                if (n < ntiles) {
+                    s_fail = 1;
+                    raise_dev_error(DEVERR_COUNTER);
+                    break;
+                }
+                *cnt = 0;
+                ++waves_done;
             }
-            s_n = n;
-            if (n >= ntiles) *cnt = 0;
+            __threadfence();
+        }
+        asm volatile("bar.sync 2, %0;" ::"r"(nt - 32) : "memory");
+        float *dst = stage + buf * 1024;
+        for (int i = tid - 32; i < r1 - r0; i += nt - 32) {
+            const float v = __ldcg(p.seg[0].out + r0 + i);
+            dst[i] = fmul(v, v);
+        }
+    };
+    if (tid >= 32) stage_chunk(0, 0);
+    __syncthreads();
+    float acc = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+        if (tid == 0) {
+            // the reference's sequential sum over this chunk, 32 squares in
+            // registers ahead of the dependent adds
+            const int m = min(1024, rows - 1024 * c), m32 = m & ~31;
+            const float *sv = stage + (c & 1) * 1024;
+            const float4 *s4 = reinterpret_cast<const float4 *>(sv);
+            float4 cur[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = m32 ? s4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int i = 0; i < m32; i += 32) {
+                float4 nxt[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) nxt[j] = i + 32 < m32 ? s4[(i + 32) / 4 + j] : cur[j];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    acc = fadd(acc, cur[j].x);
+                    acc = fadd(acc, cur[j].y);
+                    acc = fadd(acc, cur[j].z);
+                    acc = fadd(acc, cur[j].w);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            }
+            for (int i = m32; i < m; ++i) acc = fadd(acc, sv[i]);
+        } else if (tid >= 32 && c + 1 < nchunks) {
+            stage_chunk(c + 1, (c + 1) & 1);
         }
         __syncthreads();
-        if (s_n < ntiles) {
-            ok = false;
-            if (threadIdx.x == 0) raise_dev_error(DEVERR_COUNTER);
-            break;
-        }
-        __threadfence();
-        const GroupRef g0 = locate(p, first), g1 = locate(p, first + ntiles - 1);
-        acc = cta_seq_sumsq(p.seg[0].out + g0.r0, g1.r0 + g1.nr - g0.r0, acc, stage);
     }
-    if (threadIdx.x == 0) *p.norm_out = ok ? rms_scale(acc, p.seg[0].rows, p.eps) : __int_as_float(0x7FC00000);
+    if (tid == 0) *p.norm_out = s_fail ? __int_as_float(0x7FC00000) : rms_scale(acc, rows, p.eps);
 }
 
 template <bool KQ, int BPS>
