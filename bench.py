@@ -1,6 +1,6 @@
 """Benchmark: Llama-3-8B-shaped Q4_K_M batch-1 greedy decode on B200.
 
-Metric (BASELINE.json): decode tok/s, Llama-3-8B shape, Q4_K_M random-init
+Metric: decode tok/s, Llama-3-8B shape, Q4_K_M random-init
 weights (synthetic), 1 session, greedy, after a 2048-token prompt; plus the
 Q4_K GEMV's achieved HBM GB/s as the roofline of the dominant kernel.
 
@@ -14,7 +14,7 @@ Arms:
   python bench.py [--gpus N --steps K --warmup W]         this implementation
   python bench.py --impl reference [...]                  the reference CPU path
       (the C restatement in oracle/, all host threads; the reference is C#/.NET
-      with no runtime in this image, see DESIGN.md)
+      with no runtime in this image)
 Multi-GPU (torchrun, N > 1): independent replicas, one per GPU ("replicas
 only" until tensor parallelism lands); value = sum over ranks with the
 max-over-ranks time.

@@ -105,7 +105,8 @@ ovf_status ovf_q8_0_project_batched(const float *x, int64_t rows, const int8_t *
 /* Loading/GgmlQuant.cs:141 QuantizeQ4_K: fp32 [rows x k] -> Q4_K bytes. */
 ovf_status ovf_quantize_q4k(const float *w, int64_t rows, int64_t k, void *out, void *stream);
 /* Q6_K encoder for the decoder at Loading/GgmlDequant.cs:159 (the reference
- * has no Q6_K encoder; symmetric absmax scheme). */
+ * has no Q6_K encoder): per 16 weights an int8 scale, per 256 an fp16 d,
+ * 6-bit values q - 32 from a symmetric absmax fit. */
 ovf_status ovf_quantize_q6k(const float *w, int64_t rows, int64_t k, void *out, void *stream);
 /* GGUF Q8_0 encoder (fp16 scale + 32 int8) using Runtime/Q8DotKernel.cs:42 quants. */
 ovf_status ovf_quantize_q8_0_gguf(const float *w, int64_t n, void *out, void *stream);

@@ -25,14 +25,14 @@ from ._lib import (TENSORS_PER_LAYER, TYPE_F32, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_0,
 
 LAYER_KEYS = ("attn_norm", "wq", "wk", "wv", "wo", "bq", "bk", "bv", "bo", "ffn_norm", "gate", "up", "down", "router")
 
-# BASELINE model shapes (random-init, synthetic).  eps follows the reference,
+# Benchmark model shapes (random-init, synthetic).  eps follows the reference,
 # which uses 1e-6 for every GGUF model (Runtime/CachedLlamaInferenceEngine.cs:139).
 LLAMA3_8B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, d_ff=14336, vocab=128256,
                  theta=500000.0, eps=1e-6, rope_split_half=0, tied=False, qkv_bias=False, scheme="q4_k_m")
 QWEN2_05B = dict(n_layers=24, d_model=896, n_heads=14, n_kv_heads=2, head_dim=64, d_ff=4864, vocab=151936,
                  theta=1000000.0, eps=1e-6, rope_split_half=1, tied=True, qkv_bias=True, scheme="q8_0")
 
-# Q4_K_M tensor map (our choice for synthetic files, documented in DESIGN.md):
+# Q4_K_M tensor map used for synthetic files (our choice: Q4_K for q/k/o/gate/up/embedding, Q6_K for v/down/output):
 # Q6_K for attn_v, ffn_down and the output head, Q4_K elsewhere.
 _Q4KM = dict(wq=TYPE_Q4_K, wk=TYPE_Q4_K, wv=TYPE_Q6_K, wo=TYPE_Q4_K, gate=TYPE_Q4_K, up=TYPE_Q4_K,
              down=TYPE_Q6_K, embed=TYPE_Q4_K, lm_head=TYPE_Q6_K)

@@ -2,7 +2,7 @@
 the C ABI) against the CPU restatement of CachedLlamaSession on the same
 seeded synthetic weights.
 
-Bar (BASELINE north_star): logits within 1e-2 relative L2 at every step and
+Bar: logits within 1e-2 relative L2 at every step and
 identical greedy tokens for 32 decode steps.  The GPU keeps an fp16 KV cache
 and reduces RMSNorm / attention sums in a different order, so logits are not
 bit-identical; every projection inside is.
