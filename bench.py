@@ -230,6 +230,27 @@ def profiled_traffic():
     return None
 
 
+def max_over_ranks(value: float, device=None) -> float:
+    """The job's time for a weak-scaling replica run: the max of every
+    rank's device-timed interval (all-reduce MAX over the process group; the
+    NCCL group on GPUs, gloo on CPU)."""
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64,
+                     device=f"cuda:{device}" if device is not None else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def replica_value(steps_per_rank: int, world: int, seconds: float) -> float:
+    """Whole-job throughput: every rank decodes steps_per_rank tokens of its
+    own session; the job is done when the slowest rank is."""
+    return world * steps_per_rank / seconds
+
+
 def run_ours(args):
     import torch
 
@@ -276,12 +297,8 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize(device)
     clk = clocks.stop()
-    dt = e0.elapsed_time(e1) / 1e3
-    if world > 1:
-        t = torch.tensor([dt], device=f"cuda:{device}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        dt = float(t.item())
-    value = world * args.steps / dt
+    dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
+    value = replica_value(args.steps, world, dt)
 
     # e2e: the session call with host buffers (token in, argmax out).
     e2e_steps = min(args.steps, 64)
@@ -292,12 +309,8 @@ def run_ours(args):
         tok = sess.decode(tok, want_logits=False)
     e1.record(stream)
     torch.cuda.synchronize(device)
-    e2e_dt = e0.elapsed_time(e1) / 1e3
-    if world > 1:
-        t = torch.tensor([e2e_dt], device=f"cuda:{device}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_dt = float(t.item())
-    e2e = world * e2e_steps / e2e_dt
+    e2e_dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
+    e2e = replica_value(e2e_steps, world, e2e_dt)
 
     weight_bytes = eng.weight_bytes
     # F32 KV cache (the reference's default): K and V read once per step

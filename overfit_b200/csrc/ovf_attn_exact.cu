@@ -33,14 +33,24 @@ namespace cg = cooperative_groups;
 
 static constexpr int kExactCluster = 8;     // CTAs per query head
 static constexpr int kExactThreads = 128;
-static constexpr int kExactMaxSeq = 32768;  // the whole probability vector sits in each CTA's shared memory
+static constexpr int kExactMaxSeq = 16384;  // the whole probability vector sits in each CTA's shared memory
 static constexpr int kVBlock = 256;         // positions per staged value block
+static constexpr int kVBufs = 3;            // value blocks in flight
 
+// shared memory: q, k_new, v_new [hd each] | 8 scalars | value blocks
+// [kVBufs][kVBlock][hd/CL] | own score slice [chunk] | all probabilities [seq]
 int64_t attn_exact_smem_bytes(int hd, int seq_len) {
     const int chunk = (seq_len + kExactCluster - 1) / kExactCluster;
     const int dpc = hd / kExactCluster;
-    return (int64_t)(3 * hd + 8 + chunk + ((seq_len + 3) & ~3) + 2 * kVBlock * dpc) * 4 + 16;
+    return (int64_t)(3 * hd + 8 + kVBufs * kVBlock * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
 }
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 int attn_exact_max_seq(int) { return kExactMaxSeq; }
 
@@ -53,7 +63,10 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const int h = blockIdx.x / kExactCluster;
     const int G = p.H / p.KVH, g = h / G;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float *qs = esm, *kn = esm + HD, *vn = esm + 2 * HD, *red = esm + 3 * HD, *ex = esm + 3 * HD + 8;
+    constexpr int DPC = HD / kExactCluster;
+    float *qs = esm, *kn = esm + HD, *vn = esm + 2 * HD, *red = esm + 3 * HD;
+    float *vbuf = esm + 3 * HD + 8;                     // [kVBufs][kVBlock][DPC]
+    float *ex = vbuf + kVBufs * kVBlock * DPC;          // own slice of scores / exponentials
     const float *kf = reinterpret_cast<const float *>(p.kc) + (size_t)g * p.max_ctx * HD;
     const float *vf = reinterpret_cast<const float *>(p.vc) + (size_t)g * p.max_ctx * HD;
 
@@ -63,6 +76,25 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const int chunk = (seq + kExactCluster - 1) / kExactCluster;
     const int t0 = min(seq, rank * chunk), t1 = min(seq, t0 + chunk);
     const bool has_new = p.k_new != nullptr;
+    const int d0 = rank * DPC;
+    const int nblk = (seq + kVBlock - 1) / kVBlock;
+    // value block b -> vbuf[b % kVBufs] with 16-byte asynchronous copies
+    // (the row at `pos` is replaced from v_new when it is used)
+    constexpr int Q4 = DPC / 4, NQ = kVBlock * Q4 / kExactThreads;
+    auto stage_values = [&](int blk) {
+        if (blk < nblk) {
+            float *dst = vbuf + (blk % kVBufs) * kVBlock * DPC;
+            const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+#pragma unroll
+            for (int j = 0; j < NQ; ++j) {
+                const int i = tid + j * kExactThreads, t = i / Q4, q4 = i % Q4;
+                if (t < n) cp_async16(dst + 4 * i, vf + (size_t)(tb + t) * HD + d0 + 4 * q4);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int b = 0; b < kVBufs; ++b) stage_values(b);
 
     for (int i = tid; i < HD; i += kExactThreads) {
         qs[i] = p.q[(size_t)h * HD + i];
@@ -163,25 +195,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             }
         }
     }
-    constexpr int DPC = HD / kExactCluster;
-    float *vbuf = eall + ((seq + 3) & ~3);  // [2][kVBlock][DPC] staged values of this CTA's dimensions
-    const int d0 = rank * DPC;
-    // float4 pieces of a block: kVBlock rows x DPC/4, eight in flight per thread
-    constexpr int Q4 = DPC / 4, NQ = kVBlock * Q4 / kExactThreads;
-    auto stage_values = [&](int blk) {
-        float4 *dst = reinterpret_cast<float4 *>(vbuf + (blk & 1) * kVBlock * DPC);
-        const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
-        float4 tmp[NQ];
-#pragma unroll
-        for (int j = 0; j < NQ; ++j) {
-            const int i = tid + j * kExactThreads, t = i / Q4, q4 = i % Q4;
-            tmp[j] = t < n ? *reinterpret_cast<const float4 *>(vf + (size_t)(tb + t) * HD + d0 + 4 * q4)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);  // the row at `pos` is replaced from vn below
-        }
-#pragma unroll
-        for (int j = 0; j < NQ; ++j) dst[tid + j * kExactThreads] = tmp[j];
-    };
-    stage_values(0);
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
@@ -216,12 +229,12 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     //    staged block by block in shared memory by all threads while the
     //    DPC chain threads consume the previous block
     float acc = 0.0f;
-    const int nblk = (seq + kVBlock - 1) / kVBlock;
     const float vnew_d = tid < DPC && has_new ? vn[d0 + tid] : 0.0f;
     for (int blk = 0; blk < nblk; ++blk) {
-        if (blk + 1 < nblk) stage_values(blk + 1);
+        cp_async_wait<kVBufs - 1>();  // block blk has landed (this thread's part)
+        __syncthreads();
         if (tid < DPC && !bad) {
-            const float *vb = vbuf + (blk & 1) * kVBlock * DPC + tid;
+            const float *vb = vbuf + (blk % kVBufs) * kVBlock * DPC + tid;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
             int i = 0;
             for (; i + 8 <= n; i += 8) {
@@ -240,7 +253,9 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             }
         }
         __syncthreads();
+        stage_values(blk + kVBufs);  // into the buffer just consumed
     }
+    cp_async_wait<0>();
     if (tid < DPC) p.out[(size_t)h * HD + d0 + tid] = acc;
     cluster.sync();  // no CTA leaves while another may still read its shared memory
 }

@@ -787,11 +787,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     if (KQ) prep_q8k(p, L, smem);
     else prep_q80(p, L, smem);
     __syncthreads();
-    // A launch that forms an output RMSNorm lets its dependent start only as
-    // its CTAs finish (completion is the trigger): dependent CTAs scheduled
-    // early could otherwise take the SM slots of this grid's not-yet-resident
-    // CTAs, whose tiles the norm chain of CTA 0 waits for.
-    if (!p.norm_out) pdl_launch_dependents();
+    // The dependent grid may launch once every CTA of this one has passed
+    // this point, i.e. once all of them are resident: its CTAs then take
+    // only the slots that finished CTAs free, stream their first weight
+    // stages and wait at griddepcontrol.wait for this grid (and its norm
+    // chain) to complete.
+    pdl_launch_dependents();
     if (p.norm_out && blockIdx.x == 0) {
         norm_cta(p, tgrid, reinterpret_cast<float *>(ring));
         return;
@@ -844,11 +845,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                     const bool hb = k == 0 ? hb0 : hb1;
                     const float bv = k == 0 ? b0 : b1;
                     if (grouped) {
-                        float acc = hb ? bv : 0.0f;
-                        for (int m0 = 0; m0 < nb; m0 += G) {
-                            float grp = fadd(0.0f, tr[m0]);
-                            for (int m = 1; m < G; ++m) grp = fadd(grp, tr[m0 + m]);
-                            acc = fadd(acc, grp);
+                        // head-ordered sum: each group of G blocks summed in
+                        // order, the group sums added in order on the bias
+                        float acc = hb ? bv : 0.0f, grp = 0.0f;
+                        int gp = 0;
+                        int m = 0;
+                        for (; m + 8 <= nb; m += 8) {
+                            float v[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) v[q] = tr[m + q];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                grp = gp == 0 ? fadd(0.0f, v[q]) : fadd(grp, v[q]);
+                                if (++gp == G) {
+                                    acc = fadd(acc, grp);
+                                    gp = 0;
+                                }
+                            }
+                        }
+                        for (; m < nb; ++m) {
+                            grp = gp == 0 ? fadd(0.0f, tr[m]) : fadd(grp, tr[m]);
+                            if (++gp == G) {
+                                acc = fadd(acc, grp);
+                                gp = 0;
+                            }
                         }
                         y[k] = acc;
                     } else {
