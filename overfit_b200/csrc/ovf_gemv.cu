@@ -665,48 +665,31 @@ __device__ __forceinline__ void wait_or_abort(uint64_t *bar, uint32_t parity, vo
 // tiles; it walks the output rows in index order and keeps the reference's
 // sequential fp32 sum of squares, and the scale it leaves in norm_out spares
 // every CTA of the consuming kernel a reduction and reproduces the
-// reference's RmsNormalize bit for bit.  Tiles finish in waves (wave k =
-// tiles [k*tgrid, (k+1)*tgrid), whose rows are contiguous): each tile's sum
-// warp bumps its wave's counter after its stores, and the chain takes a
-// wave once its counter is full, so it trails the GEMV by about one wave.
-// The counters are reset as they are consumed (zero for the next launch).
-__device__ __noinline__ void norm_cta(const GemvParams &p, int tgrid, float *stage) {
+// reference's RmsNormalize bit for bit.  The output buffer holds the
+// kNormSentinel pattern before this launch (an earlier kernel of the step
+// fills it), so the norm CTA knows a row has been written when its value is
+// no longer the sentinel: the tile CTAs publish nothing and pay no fences.
+// The norm CTA stages 1024 squares at a time (warps 1..) while thread 0 adds
+// the previous 1024 in order, so the chain trails the GEMV closely.
+__device__ __noinline__ void norm_cta(const GemvParams &p, float *stage) {
     __shared__ int s_fail;
     const int tid = threadIdx.x, nt = blockDim.x;
-    const int rows = p.seg[0].rows, T = p.rows_per_group;
-    const int nwaves = (p.total_groups + tgrid - 1) / tgrid;
+    const int rows = p.seg[0].rows;
     const int nchunks = (rows + 1023) / 1024;
-    int waves_done = 0;  // thread 32's view
+    const float *out = p.seg[0].out;
     if (tid == 0) s_fail = 0;
     __syncthreads();
-    // warps 1..: wait until the tiles covering chunk c have finished, then
-    // stage the chunk's squares in stage[buf]
+    // warps 1..: load chunk c once every row of it has been written
     auto stage_chunk = [&](int c, int buf) {
-        const int r0 = 1024 * c, r1 = min(rows, r0 + 1024);
-        if (tid == 32) {
-            const int need = min(nwaves - 1, ((r1 - 1) / T) / tgrid);
-            while (waves_done <= need && !s_fail) {
-                const int ntiles = min(tgrid, p.total_groups - waves_done * tgrid);
-                volatile int *cnt = p.tile_flags + waves_done;
-                int n = *cnt;
-                for (uint32_t i = 0; n < ntiles && i < (1u << 22); ++i) {
-                    __nanosleep(32);
-                    n = *cnt;
-                }
-                if (n < ntiles) {
-                    s_fail = 1;
-                    raise_dev_error(DEVERR_COUNTER);
-                    break;
-                }
-                *cnt = 0;
-                ++waves_done;
-            }
-            __threadfence();
-        }
-        asm volatile("bar.sync 2, %0;" ::"r"(nt - 32) : "memory");
+        const int r0 = 1024 * c, n = min(1024, rows - r0);
         float *dst = stage + buf * 1024;
-        for (int i = tid - 32; i < r1 - r0; i += nt - 32) {
-            const float v = __ldcg(p.seg[0].out + r0 + i);
+        for (int i = tid - 32; i < n; i += nt - 32) {
+            float v = __ldcg(out + r0 + i);
+            for (uint32_t k = 0; __float_as_uint(v) == kNormSentinel && k < (1u << 22); ++k) {
+                __nanosleep(64);
+                v = __ldcg(out + r0 + i);
+            }
+            if (__float_as_uint(v) == kNormSentinel) s_fail = 1;
             dst[i] = fmul(v, v);
         }
     };
@@ -743,7 +726,10 @@ __device__ __noinline__ void norm_cta(const GemvParams &p, int tgrid, float *sta
         }
         __syncthreads();
     }
-    if (tid == 0) *p.norm_out = s_fail ? __int_as_float(0x7FC00000) : rms_scale(acc, rows, p.eps);
+    if (tid == 0) {
+        if (s_fail) raise_dev_error(DEVERR_COUNTER);
+        *p.norm_out = s_fail ? __int_as_float(0x7FC00000) : rms_scale(acc, rows, p.eps);
+    }
 }
 
 template <bool KQ, int BPS>
@@ -784,6 +770,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     }
 
     pdl_wait();
+    if (p.fill_sentinel) {
+        // mark the buffer a later residual launch of this step will write
+        // (its norm CTA waits for the marks to be overwritten)
+        for (int i = blockIdx.x * blockDim.x + tid; i < p.fill_n; i += gridDim.x * blockDim.x)
+            p.fill_sentinel[i] = __uint_as_float(kNormSentinel);
+    }
     if (KQ) prep_q8k(p, L, smem);
     else prep_q80(p, L, smem);
     __syncthreads();
@@ -794,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     // chain) to complete.
     pdl_launch_dependents();
     if (p.norm_out && blockIdx.x == 0) {
-        norm_cta(p, tgrid, reinterpret_cast<float *>(ring));
+        norm_cta(p, reinterpret_cast<float *>(ring));
         return;
     }
 
@@ -900,12 +892,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&B.tfree[j]);
-            if (p.norm_out) {
-                // publish the tile's outputs to the norm chain of CTA 0
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(&p.tile_flags[it], 1);  // wave `it`
-            }
         }
         if (p.epi == EPI_LOGITS_ARGMAX) {
             // warp max -> one global atomic per CTA; the last CTA to finish
@@ -1088,8 +1074,8 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
                       "gemv: pair mode needs 2 segments of equal shape and type");
     if (p.epi == EPI_RESIDUAL) OVF_CHECK_ARG(p.resid != nullptr, "gemv: residual epilogue without residual");
     if (p.norm_out)
-        OVF_CHECK_ARG(p.epi == EPI_RESIDUAL && p.nseg == 1 && p.tile_flags != nullptr,
-                      "gemv: an output RMSNorm needs a single-segment residual launch and tile flags");
+        OVF_CHECK_ARG(p.epi == EPI_RESIDUAL && p.nseg == 1,
+                      "gemv: an output RMSNorm needs a single-segment residual launch");
     if (p.act_mode == ACT_F32_RMSNORM) OVF_CHECK_ARG(p.norm_scale != nullptr, "gemv: RMSNorm input without its scale");
     if (p.epi == EPI_LOGITS_ARGMAX) OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
 

@@ -38,6 +38,11 @@ struct DevStep {
     int pad[3];
 };
 
+// Bit pattern of "not written yet" in a residual output whose RMSNorm is
+// formed on the fly (a NaN payload that no arithmetic on finite values
+// produces).
+static constexpr uint32_t kNormSentinel = 0x7FBADBADu;
+
 struct GemvSeg {
     const uint8_t *w;    // K-quant blocks, or Q8_0 int8 quants
     const float *ws;     // Q8_0 fp32 scales [rows x K/32]
@@ -70,8 +75,10 @@ struct GemvParams {
     int16_t *ab_out;
     const float *norm_scale;  // ACT_F32_RMSNORM: RMSNorm scale of x, computed by its producer
     const float *resid;
-    float *norm_out;     // EPI_RESIDUAL: also produce the RMSNorm scale of the output (eps)
-    int *tile_flags;     // norm_out: per-wave tile counters (>= tiles / grid), zero between launches
+    float *norm_out;     // EPI_RESIDUAL: also produce the RMSNorm scale of the output (eps); the
+                         // output must hold kNormSentinel when the launch starts
+    float *fill_sentinel;  // optional: buffer to fill with kNormSentinel (for a later launch)
+    int fill_n;
     DevStep *step;       // EPI_LOGITS_ARGMAX
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
 };

@@ -66,8 +66,6 @@ struct ovf_session {
           *partial = nullptr;
     int *counters = nullptr, *tokens_log = nullptr;
     float *norm_s = nullptr;  // [0]: RMSNorm scale of hidden, [1]: of after
-    int *tile_flags = nullptr;
-    int n_tile_flags = 0;
     DevStep *step = nullptr;
     int32_t *pinned_tok = nullptr;  // host staging
     int pinned_cap = 0;
@@ -252,6 +250,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.norm_scale = &s->norm_s[0];
             p.eps = c.eps;
             p.epi = EPI_STORE;
+            p.fill_sentinel = s->after;  // Wo's norm CTA watches `after` being written
+            p.fill_n = D;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "qkv");
         } else {
@@ -269,6 +269,10 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.norm_scale = &s->norm_s[0];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
+                if (i == 0) {
+                    p.fill_sentinel = s->after;
+                    p.fill_n = D;
+                }
                 if ((r = gemv_launch(p, st, true))) return r;
                 prof_mark(st, "qkv");
             }
@@ -313,7 +317,6 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_RESIDUAL;
             p.resid = s->hidden;
             p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
-            p.tile_flags = s->tile_flags;
             p.eps = c.eps;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "wo");
@@ -331,6 +334,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.norm_scale = &s->norm_s[1];
             p.eps = c.eps;
             p.epi = EPI_SILU_PAIR;
+            p.fill_sentinel = s->hidden;  // the down projection's norm CTA watches `hidden`
+            p.fill_n = D;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "gateup");
         } else {
@@ -347,6 +352,10 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.norm_scale = &s->norm_s[1];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
+                if (i == 0) {
+                    p.fill_sentinel = s->hidden;
+                    p.fill_n = D;
+                }
                 if ((r = gemv_launch(p, st, true))) return r;
                 prof_mark(st, "gateup");
             }
@@ -363,7 +372,6 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_RESIDUAL;
             p.resid = s->after;
             p.norm_out = &s->norm_s[0];  // RMSNorm scale of the new hidden: next layer / final norm
-            p.tile_flags = s->tile_flags;
             p.eps = c.eps;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "down");
@@ -593,13 +601,10 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     A((void **)&s->partial, (size_t)attn_scratch_bytes(c.n_heads, c.n_kv_heads, c.head_dim));
     A((void **)&s->counters, (size_t)c.n_kv_heads * 4);
     A((void **)&s->norm_s, 2 * 4);
-    s->n_tile_flags = (int)D;  // a residual launch has at most one tile per output row
-    A((void **)&s->tile_flags, (size_t)s->n_tile_flags * 4);
     A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
     A((void **)&s->step, sizeof(DevStep));
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
     if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
-    if (!st) st = cuda_status(cudaMemset(s->tile_flags, 0, (size_t)s->n_tile_flags * 4), "memset");
     if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
     if (!st) st = cuda_status(cudaMemset(s->kc, 0, kv * esz), "memset");
     if (!st) st = cuda_status(cudaMemset(s->vc, 0, kv * esz), "memset");
