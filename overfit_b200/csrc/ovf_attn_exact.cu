@@ -70,6 +70,9 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const float *kf = reinterpret_cast<const float *>(p.kc) + (size_t)g * p.max_ctx * HD;
     const float *vf = reinterpret_cast<const float *>(p.vc) + (size_t)g * p.max_ctx * HD;
 
+    // the next projections' weights do not depend on this kernel: pull them
+    // into L2 while the (latency-bound) attention runs
+    if (tid == 0 && p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
     pdl_wait();
     const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
     const int seq = pos + 1;

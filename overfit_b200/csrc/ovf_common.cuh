@@ -284,6 +284,31 @@ cudaError_t launch_pdl(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStre
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Upcoming weights to pull into L2 while a kernel runs: the next
+// projection's bytes during a latency-bound phase (attention chains, a
+// GEMV's drain and norm tail), so the next launch streams from L2.
+struct L2Prefetch {
+    const void *ptr[4];
+    int64_t bytes[4];
+    int n;
+};
+
+// CTA `cta` of `ncta` issues its slice of every range (bulk L2 prefetches of
+// at most 64 KB, 16-byte granules; no shared memory, no completion wait).
+__device__ __forceinline__ void prefetch_l2_slice(const L2Prefetch &pf, int cta, int ncta) {
+    for (int r = 0; r < pf.n; ++r) {
+        const int64_t per = ((pf.bytes[r] + ncta - 1) / ncta + 15) & ~int64_t(15);
+        const int64_t a = per * cta, e = pf.bytes[r] < a + per ? pf.bytes[r] : a + per;
+        const char *base = static_cast<const char *>(pf.ptr[r]);
+        for (int64_t o = a; o < e; o += 65536) {
+            const int64_t left = e - o;
+            const uint32_t n = (uint32_t)(left < 65536 ? left : 65536) & ~15u;
+            if (!n) break;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + o), "r"(n) : "memory");
+        }
+    }
+}
+
 int sm_count(int device);
 
 }  // namespace ovf

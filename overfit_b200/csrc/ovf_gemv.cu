@@ -798,13 +798,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             wait_or_abort(&B.empty[s], (uint32_t)(((it / p.stages) - 1) & 1), B.abort_flag);
             if (*B.abort_flag) break;
             fence_proxy_async_smem();
-#ifdef OVF_GEMV_NOCOPY
-            mbar_arrive(&B.full[s]);
-#else
             issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)s * L.stage_bytes, &B.full[s],
                         pol);
-#endif
         }
+        if (p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
         return;
     }
 
@@ -979,11 +976,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
         TMARK(t_tf)
         wait_or_abort(&B.full[s], (uint32_t)((it / p.stages) & 1), B.abort_flag);
         TMARK(t_full)
-#ifdef OVF_GEMV_NOCOMP
-        for (int rr = 0; rr < 0; ++rr) {
-#else
         for (int rr = 0; rr < rps; ++rr) {
-#endif
             const int r = subset + rr * RS;
             int useg = 0, urow = 0;
             const bool rv = slot_ok && r < T && slot_row(p, g, r, &useg, &urow);

@@ -66,6 +66,7 @@ struct AttnParams {
     int *counters;            // [KVH], zero on entry and on exit
     int split_half, H, KVH, hd, max_ctx, seq_len_host, n_splits, chunk_max, sc_floats;
     float scale;
+    L2Prefetch pf;            // weights of later launches to pull into L2 during the chains
 };
 int attn_splits(int n_kv_heads);
 int64_t attn_scratch_bytes(int H, int KVH, int hd);

@@ -168,6 +168,41 @@ ovf_status fill_rope_tables(ovf_session *s) {
     return OVF_OK;
 }
 
+// OVF_EAGER=1 launches the step's kernels directly instead of replaying a
+// CUDA graph (profiling and debugging); OVF_NO_PDL=1 drops programmatic
+// dependent launch; OVF_NO_L2_PREFETCH=1 drops the L2 prefetch of upcoming
+// weights.
+bool env_flag(const char *name) {
+    const char *v = getenv(name);
+    return v && v[0] == '1';
+}
+
+int l2_prefetch_mode() {
+    static const int mode = [] {
+        const char *v = getenv("OVF_L2_PF");
+        return v ? atoi(v) : 0;
+    }();
+    return mode;
+}
+
+// Adds a resident weight's bytes (quants, then Q8_0 scales) to an L2
+// prefetch list.
+void add_prefetch(L2Prefetch &pf, const DevWeight &w) {
+    if (!w.data) return;
+    int64_t qb = 0;
+    if (w.type == OVF_TYPE_Q4_K) qb = w.rows * w.cols / 256 * 144;
+    else if (w.type == OVF_TYPE_Q6_K) qb = w.rows * w.cols / 256 * 210;
+    else if (w.type == OVF_TYPE_Q8_0) qb = w.rows * w.cols;
+    if (qb > 0 && pf.n < 4) {
+        pf.ptr[pf.n] = w.data;
+        pf.bytes[pf.n++] = qb;
+    }
+    if (w.type == OVF_TYPE_Q8_0 && w.scales && pf.n < 4) {
+        pf.ptr[pf.n] = w.scales;
+        pf.bytes[pf.n++] = w.rows * w.cols / 32 * 4;
+    }
+}
+
 GemvSeg seg_of(const DevWeight &w, const float *bias, float *out) {
     return GemvSeg{w.data, w.scales, bias, out, w.type, (int)w.rows, 0};
 }
@@ -296,6 +331,11 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         a.hd = hd;
         a.max_ctx = s->max_ctx;
         a.scale = 1.0f / sqrtf((float)hd);
+        if (l2_prefetch_mode() & 1) add_prefetch(a.pf, L.wo);
+        if (l2_prefetch_mode() & 2) {
+            add_prefetch(a.pf, L.gate);
+            add_prefetch(a.pf, L.up);
+        }
         if (s->kv_dtype == OVF_KV_F32) {
             if ((r = launch_attention_exact(a, s->max_ctx, st, true))) return r;
         } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
@@ -317,6 +357,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_RESIDUAL;
             p.resid = s->hidden;
             p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
+            if (l2_prefetch_mode() & 4) add_prefetch(p.pf, L.down);
             p.eps = c.eps;
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "wo");
@@ -336,6 +377,12 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_SILU_PAIR;
             p.fill_sentinel = s->hidden;  // the down projection's norm CTA watches `hidden`
             p.fill_n = D;
+            if ((l2_prefetch_mode() & 8) && l + 1 < c.n_layers) {
+                const DevLayer &N = m->layers[l + 1];
+                add_prefetch(p.pf, N.wq);
+                add_prefetch(p.pf, N.wk);
+                add_prefetch(p.pf, N.wv);
+            }
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "gateup");
         } else {
@@ -411,13 +458,6 @@ ovf_status capture(ovf_session *s, bool with_logits, cudaGraphExec_t *out) {
     return cuda_status(e, "cudaGraphInstantiate");
 }
 
-// OVF_EAGER=1 launches the step's kernels directly instead of replaying a
-// CUDA graph (profiling and debugging); OVF_NO_PDL=1 drops programmatic
-// dependent launch.
-static bool env_flag(const char *name) {
-    const char *v = getenv(name);
-    return v && v[0] == '1';
-}
 
 ovf_status run_step(ovf_session *s, bool with_logits) {
     cudaGraphExec_t *gx = with_logits ? &s->graph_logits : &s->graph_nologits;
