@@ -47,6 +47,10 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer layers (invalid as a bench number)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv", default="f16", choices=["f16", "f32"],
+                    help="KV cache of the timed session: f16 (the benchmark config) or f32 (the reference's default, "
+                         "bit-exact attention)")
+    ap.add_argument("--no-f32-line", action="store_true", help="skip the extra F32-KV (exact) measurement")
     return ap.parse_args()
 
 
@@ -277,8 +281,29 @@ def run_ours(args):
     eng = engine.CudaLlamaInferenceEngine(cfg, mf, device=device)
     gen_s = time.time() - t0
     max_ctx = args.prompt + args.warmup + args.steps + 64
-    sess = eng.create_session(max_ctx)
     prompt = np.random.default_rng(1234 + rank).integers(0, cfg["vocab"], args.prompt).astype(np.int32)
+
+    # The reference's default F32 KV cache (exact attention order), timed on
+    # a shorter run and reported beside the benchmark config's fp16 cache.
+    exact = None
+    if args.kv == "f16" and not args.no_f32_line:
+        sx = eng.create_session(max_ctx, "f32")
+        sx.prefill(prompt)
+        sx.generate_greedy(args.warmup)
+        stx = torch.cuda.ExternalStream(sx.stream_handle, device=device)
+        ex0, ex1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nx = min(args.steps, 64)
+        torch.cuda.synchronize(device)
+        ex0.record(stx)
+        sx.generate_greedy(nx)
+        ex1.record(stx)
+        torch.cuda.synchronize(device)
+        dtx = max_over_ranks(ex0.elapsed_time(ex1) / 1e3, device)
+        exact = {"kv_cache": "f32", "value": replica_value(nx, world, dtx), "unit": "tok/s", "steps": nx,
+                 "ms_per_step": dtx / nx * 1e3}
+        sx.close()
+
+    sess = eng.create_session(max_ctx, args.kv)
     t0 = time.time()
     sess.prefill(prompt)
     prefill_s = time.time() - t0
@@ -313,9 +338,10 @@ def run_ours(args):
     e2e = replica_value(e2e_steps, world, e2e_dt)
 
     weight_bytes = eng.weight_bytes
-    # F32 KV cache (the reference's default): K and V read once per step
-    kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * 4 * (args.prompt + args.warmup +
-                                                                                args.steps // 2)
+    # K and V of every layer read once per step, at the run's mean context
+    kv_elem = 2 if args.kv == "f16" else 4
+    kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * kv_elem * (args.prompt + args.warmup +
+                                                                                      args.steps // 2)
     roof = gemv_roofline(torch, cfg, mf, device, peaks) if rank == 0 else None
     sess.close()
     eng.close()
@@ -335,7 +361,9 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (Q4_K/Q6_K/Q8_0 x Q8_K/Q8_0), fp32 accum",
                 "data": "synthetic (random-init N(0,0.02), quantized on device)",
-                "config": {"workload": "llama3-8b-q4_k_m greedy decode batch 1, prompt %d" % args.prompt,
+                "config": {"workload": "llama3-8b-q4_k_m greedy decode batch 1, prompt %d, %s KV cache"
+                                       % (args.prompt, args.kv),
+                           "kv_cache": args.kv,
                            "model": "Llama-3-8B shape" + ("" if not args.layers else f" ({args.layers} layers)"),
                            "global_batch": world, "seq_len": args.prompt, "parallelism": f"replicas x{world}",
                            "l2": "inputs larger than L2 (%.2f GB of weights per step)" % (weight_bytes / 1e9)},
@@ -345,6 +373,7 @@ def run_ours(args):
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
                 "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
                 "gpu_launches": launches_per_step * args.steps,
+                "f32_kv_exact": exact,
                 "setup_s": {"model_gen_upload": gen_s, "prefill": prefill_s}}
         print(json.dumps(line), flush=True)
     if world > 1:

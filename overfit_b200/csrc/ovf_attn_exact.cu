@@ -32,21 +32,30 @@ namespace ovf {
 namespace cg = cooperative_groups;
 
 static constexpr int kExactCluster = 8;     // CTAs per query head
-static constexpr int kExactThreads = 128;
+static constexpr int kExactThreads = 256;
 static constexpr int kExactMaxSeq = 16384;  // the whole probability vector sits in each CTA's shared memory
-static constexpr int kVBlock = 256;         // positions per staged value block
-static constexpr int kVBufs = 3;            // value blocks in flight
+static constexpr int kVBlock = 128;         // positions per staged value block
+static constexpr int kVRow = kVBlock + 4;   // one dimension's values of a block, padded (16-byte rows)
+static constexpr int kVBufs = 8;            // value blocks in flight (hd <= 128; 4 for hd 256)
+template <int HD>
+struct VStage {
+    static constexpr int bufs = HD <= 128 ? kVBufs : kVBufs / 2;
+};
 
-// shared memory: q, k_new, v_new [hd each] | 8 scalars | value blocks
+// shared memory: q, k_new, v_new [hd each] | 16 scalars | value blocks
 // [kVBufs][kVBlock][hd/CL] | own score slice [chunk] | all probabilities [seq]
 int64_t attn_exact_smem_bytes(int hd, int seq_len) {
     const int chunk = (seq_len + kExactCluster - 1) / kExactCluster;
     const int dpc = hd / kExactCluster;
-    return (int64_t)(3 * hd + 8 + kVBufs * kVBlock * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
+    const int bufs = hd <= 128 ? kVBufs : kVBufs / 2;
+    return (int64_t)(3 * hd + 16 + bufs * kVRow * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
 }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -65,15 +74,43 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int DPC = HD / kExactCluster;
     float *qs = esm, *kn = esm + HD, *vn = esm + 2 * HD, *red = esm + 3 * HD;
-    float *vbuf = esm + 3 * HD + 8;                     // [kVBufs][kVBlock][DPC]
-    float *ex = vbuf + kVBufs * kVBlock * DPC;          // own slice of scores / exponentials
+    float *vbuf = esm + 3 * HD + 16;                    // [kVBufs][kVBlock][DPC]
+    constexpr int NBUF = VStage<HD>::bufs;
+    float *ex = vbuf + NBUF * kVRow * DPC;              // own slice of scores / exponentials
     const float *kf = reinterpret_cast<const float *>(p.kc) + (size_t)g * p.max_ctx * HD;
     const float *vf = reinterpret_cast<const float *>(p.vc) + (size_t)g * p.max_ctx * HD;
 
     // the next projections' weights do not depend on this kernel: pull them
     // into L2 while the (latency-bound) attention runs
+    if (tid == 0) trace_mark(p.trace, TR_START);
     if (tid == 0 && p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
+    if (tid == 0 && p.pos_dev && !p.no_kv_prefetch) {
+        // The cache rows before this token do not depend on the previous
+        // kernel: pull this CTA's key slice and a slice of the value rows
+        // into L2 now.  The position read here may still be the previous
+        // step's (the bound only matters for the hint); the real one is
+        // read after griddepcontrol.wait.
+        const int sp = *(volatile const int *)p.pos_dev + 1;
+        const int ch = (sp + kExactCluster - 1) / kExactCluster;
+        const int a = min(sp, rank * ch), b = min(sp, a + ch);
+        L2Prefetch kv{};
+        if (b > a) {
+            kv.ptr[0] = kf + (size_t)a * HD;
+            kv.bytes[0] = (int64_t)(b - a) * HD * 4;
+            kv.ptr[1] = vf + (size_t)a * HD;
+            kv.bytes[1] = (int64_t)(b - a) * HD * 4;
+            kv.n = 2;
+            prefetch_l2_slice(kv, 0, 1);
+        }
+    }
     pdl_wait();
+    if (tid == 0) trace_mark(p.trace, TR_WAITED);
+#ifdef OVF_ATTN_TIMING
+    long long T0 = clock64(), T1 = 0, T2 = 0, T3 = 0, T4 = 0, T5 = 0;
+#define ATM(x) x = clock64();
+#else
+#define ATM(x)
+#endif
     const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
     const int seq = pos + 1;
     const int chunk = (seq + kExactCluster - 1) / kExactCluster;
@@ -83,21 +120,24 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const int nblk = (seq + kVBlock - 1) / kVBlock;
     // value block b -> vbuf[b % kVBufs] with 16-byte asynchronous copies
     // (the row at `pos` is replaced from v_new when it is used)
-    constexpr int Q4 = DPC / 4, NQ = kVBlock * Q4 / kExactThreads;
+    // block b is stored transposed, [DPC][kVRow]: dimension d's values of
+    // the block are contiguous for its chain thread (4-byte copies; the
+    // global reads stay coalesced along d)
+    constexpr int NE = kVBlock * DPC / kExactThreads;
     auto stage_values = [&](int blk) {
         if (blk < nblk) {
-            float *dst = vbuf + (blk % kVBufs) * kVBlock * DPC;
+            float *dst = vbuf + (blk % NBUF) * kVRow * DPC;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
 #pragma unroll
-            for (int j = 0; j < NQ; ++j) {
-                const int i = tid + j * kExactThreads, t = i / Q4, q4 = i % Q4;
-                if (t < n) cp_async16(dst + 4 * i, vf + (size_t)(tb + t) * HD + d0 + 4 * q4);
+            for (int j = 0; j < NE; ++j) {
+                const int i = tid + j * kExactThreads, t = i / DPC, dd = i % DPC;
+                if (t < n) cp_async4(dst + dd * kVRow + t, vf + (size_t)(tb + t) * HD + d0 + dd);
             }
         }
         cp_async_commit();
     };
 #pragma unroll
-    for (int b = 0; b < kVBufs; ++b) stage_values(b);
+    for (int b = 0; b < NBUF; ++b) stage_values(b);
 
     for (int i = tid; i < HD; i += kExactThreads) {
         qs[i] = p.q[(size_t)h * HD + i];
@@ -159,6 +199,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             }
         }
     }
+    ATM(T1)
     // 2. cluster-wide maximum
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xFFFFFFFFu, lmax, o));
@@ -167,14 +208,15 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     if (tid == 0) {
         float m = red[0];
         for (int w = 1; w < kExactThreads / 32; ++w) m = fmaxf(m, red[w]);
-        red[4] = m;
+        red[8] = m;
     }
     cluster.sync();
     float gmax = -INFINITY;
-    for (int r = 0; r < kExactCluster; ++r) gmax = fmaxf(gmax, cluster.map_shared_rank(red, r)[4]);
+    for (int r = 0; r < kExactCluster; ++r) gmax = fmaxf(gmax, cluster.map_shared_rank(red, r)[8]);
     for (int t = t0 + tid; t < t1; t += kExactThreads) ex[t - t0] = exp_rn(fsub(ex[t - t0], gmax));
     cluster.sync();
 
+    ATM(T2)
     // 3. every CTA gathers all probabilities' numerators into its own shared
     //    memory, then thread 0 forms sumExp over t in order (the same chain,
     //    so the same value, in every CTA)
@@ -199,68 +241,91 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         }
     }
     __syncthreads();
+    ATM(T3)
     if (tid == 0) {
         float sum = 0.0f;
-        const int s32 = seq & ~31;
+        const int s64 = seq & ~63;
         const float4 *e4 = reinterpret_cast<const float4 *>(eall);
-        float4 cur[8];
+        for (int i = 0; i < s64; i += 64) {
+            float4 a[8], b[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cur[j] = s32 ? e4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i = 0; i < s32; i += 32) {
-            float4 nxt[8];
+            for (int j = 0; j < 8; ++j) a[j] = e4[i / 4 + j];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) nxt[j] = i + 32 < s32 ? e4[(i + 32) / 4 + j] : cur[j];
+            for (int j = 0; j < 8; ++j) b[j] = e4[i / 4 + 8 + j];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                sum = fadd(sum, cur[j].x);
-                sum = fadd(sum, cur[j].y);
-                sum = fadd(sum, cur[j].z);
-                sum = fadd(sum, cur[j].w);
+                sum = fadd(sum, a[j].x);
+                sum = fadd(sum, a[j].y);
+                sum = fadd(sum, a[j].z);
+                sum = fadd(sum, a[j].w);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+            for (int j = 0; j < 8; ++j) {
+                sum = fadd(sum, b[j].x);
+                sum = fadd(sum, b[j].y);
+                sum = fadd(sum, b[j].z);
+                sum = fadd(sum, b[j].w);
+            }
         }
+        const int s32 = s64;
         for (int t = s32; t < seq; ++t) sum = fadd(sum, eall[t]);
-        red[5] = sum;
+        red[9] = sum;
     }
     __syncthreads();
-    const float sumExp = red[5];
+    ATM(T4)
+    const float sumExp = red[9];
     const bool bad = !(sumExp > 0.0f) || isinf(sumExp);
     const float invSum = bad ? 0.0f : fdiv(1.0f, sumExp);
 
     // 4. out[d] for this CTA's dimensions over t in order; the values are
     //    staged block by block in shared memory by all threads while the
     //    DPC chain threads consume the previous block
+    // p_t = e_t * invSum once, by all threads (the reference's probability)
+    if (!bad)
+        for (int t = tid; t < seq; t += kExactThreads) eall[t] = fmul(eall[t], invSum);
     float acc = 0.0f;
-    const float vnew_d = tid < DPC && has_new ? vn[d0 + tid] : 0.0f;
     for (int blk = 0; blk < nblk; ++blk) {
-        cp_async_wait<kVBufs - 1>();  // block blk has landed (this thread's part)
+        cp_async_wait<NBUF - 1>();  // block blk has landed (this thread's part)
         __syncthreads();
         if (tid < DPC && !bad) {
-            const float *vb = vbuf + (blk % kVBufs) * kVBlock * DPC + tid;
+            float *vb = vbuf + (blk % NBUF) * kVRow * DPC + tid * kVRow;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+            // the current token's value was not in the cache when staged
+            if (has_new && pos >= tb && pos < tb + n) vb[pos - tb] = vn[d0 + tid];
+            const float *pb = eall + tb;
             int i = 0;
-            for (; i + 8 <= n; i += 8) {
-                float ev[8], vv[8];
+            // 32 values and probabilities in registers ahead of the adds
+#pragma unroll 1
+            for (; i + 32 <= n; i += 32) {
+                float4 pv[8], vv[8];
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    ev[j] = eall[tb + i + j];
-                    vv[j] = (has_new && tb + i + j == pos) ? vnew_d : vb[(i + j) * DPC];
+                    pv[j] = *reinterpret_cast<const float4 *>(pb + i + 4 * j);
+                    vv[j] = *reinterpret_cast<const float4 *>(vb + i + 4 * j);
                 }
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc = fadd(acc, fmul(fmul(ev[j], invSum), vv[j]));
+                for (int j = 0; j < 8; ++j) {
+                    acc = fadd(acc, fmul(pv[j].x, vv[j].x));
+                    acc = fadd(acc, fmul(pv[j].y, vv[j].y));
+                    acc = fadd(acc, fmul(pv[j].z, vv[j].z));
+                    acc = fadd(acc, fmul(pv[j].w, vv[j].w));
+                }
             }
-            for (; i < n; ++i) {
-                const float vv = (has_new && tb + i == pos) ? vnew_d : vb[i * DPC];
-                acc = fadd(acc, fmul(fmul(eall[tb + i], invSum), vv));
-            }
+            for (; i < n; ++i) acc = fadd(acc, fmul(pb[i], vb[i]));
         }
         __syncthreads();
-        stage_values(blk + kVBufs);  // into the buffer just consumed
+        stage_values(blk + NBUF);  // into the buffer just consumed
     }
     cp_async_wait<0>();
+    ATM(T5)
+#ifdef OVF_ATTN_TIMING
+    if (tid == 0 && blockIdx.x < 16 && p.pos_dev)
+        printf("attn cta %d pos %d: pre %lld scores %lld max+exp %lld gather %lld sumexp %lld out %lld\n", blockIdx.x,
+               pos, T1 - T0, T2 - T1, T3 - T2, T4 - T3, T5 - T4, 0ll);
+#endif
     if (tid < DPC) p.out[(size_t)h * HD + d0 + tid] = acc;
     cluster.sync();  // no CTA leaves while another may still read its shared memory
+    if (tid == 0) trace_mark(p.trace, TR_END);
 }
 
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }

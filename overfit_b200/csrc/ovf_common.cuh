@@ -309,6 +309,28 @@ __device__ __forceinline__ void prefetch_l2_slice(const L2Prefetch &pf, int cta,
     }
 }
 
+// Per-launch timeline for OVF_TRACE (debugging): first CTA start, last
+// griddepcontrol.wait return and last exit, in %globaltimer nanoseconds;
+// start is kept as its complement so that every field is an atomicMax.
+struct TraceSlot {
+    unsigned long long start_c, waited, end, pad;
+};
+
+__device__ __forceinline__ unsigned long long gtime_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+enum : int { TR_START = 0, TR_WAITED = 1, TR_END = 2 };
+__device__ __forceinline__ void trace_mark(TraceSlot *t, int what) {
+    if (!t) return;
+    const unsigned long long v = gtime_ns();
+    if (what == TR_START) atomicMax(&t->start_c, ~v);
+    else if (what == TR_WAITED) atomicMax(&t->waited, v);
+    else atomicMax(&t->end, v);
+}
+
 int sm_count(int device);
 
 }  // namespace ovf

@@ -340,20 +340,28 @@ __device__ __forceinline__ float q6k_unit(const uint8_t *blk, const uint8_t *q8,
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
 #pragma unroll
-        for (int lw = 0; lw < 8; ++lw) {
-            const uint32_t qla = ldw_shifted(base, 16 * h + lw, sh);
-            const uint32_t qlb = ldw_shifted(base, 16 * h + 8 + lw, sh);
-            const uint32_t qhw = ldw_shifted(base, 32 + 8 * h + lw, sh);
-            const uint32_t M = 0x0F0F0F0Fu, H = 0x30303030u;
-            const int q1 = (int)((qla & M) | ((qhw << 4) & H));
-            const int q2 = (int)((qlb & M) | ((qhw << 2) & H));
-            const int q3 = (int)(((qla >> 4) & M) | (qhw & H));
-            const int q4 = (int)(((qlb >> 4) & M) | ((qhw >> 2) & H));
-            const int is = lw >> 2;
-            const int base8 = 32 * h + lw;
-            sum += sc[8 * h + is] * dp4a(q1, (int)q8w[base8], 0) + sc[8 * h + is + 2] * dp4a(q2, (int)q8w[base8 + 8], 0) +
-                   sc[8 * h + is + 4] * dp4a(q3, (int)q8w[base8 + 16], 0) +
-                   sc[8 * h + is + 6] * dp4a(q4, (int)q8w[base8 + 24], 0);
+        for (int is = 0; is < 2; ++is) {
+            // the four 16-element groups sharing scales sc[8h+is+{0,2,4,6}]:
+            // integer dots first, one scale multiply per group
+            int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
+#pragma unroll
+            for (int l4 = 0; l4 < 4; ++l4) {
+                const int lw = 4 * is + l4;
+                const uint32_t qla = ldw_shifted(base, 16 * h + lw, sh);
+                const uint32_t qlb = ldw_shifted(base, 16 * h + 8 + lw, sh);
+                const uint32_t qhw = ldw_shifted(base, 32 + 8 * h + lw, sh);
+                const uint32_t M = 0x0F0F0F0Fu, H = 0x30303030u;
+                const int q1 = (int)((qla & M) | ((qhw << 4) & H));
+                const int q2 = (int)((qlb & M) | ((qhw << 2) & H));
+                const int q3 = (int)(((qla >> 4) & M) | (qhw & H));
+                const int q4 = (int)(((qlb >> 4) & M) | ((qhw >> 2) & H));
+                const int base8 = 32 * h + lw;
+                d1 = dp4a(q1, (int)q8w[base8], d1);
+                d2 = dp4a(q2, (int)q8w[base8 + 8], d2);
+                d3 = dp4a(q3, (int)q8w[base8 + 16], d3);
+                d4 = dp4a(q4, (int)q8w[base8 + 24], d4);
+            }
+            sum += sc[8 * h + is] * d1 + sc[8 * h + is + 2] * d2 + sc[8 * h + is + 4] * d3 + sc[8 * h + is + 6] * d4;
         }
     }
     const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
@@ -747,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     const int tgrid = (int)gridDim.x - nfirst, tcta = (int)blockIdx.x - nfirst;
     const int items = tcta >= 0 && tcta < p.total_groups ? (p.total_groups - tcta + tgrid - 1) / tgrid : 0;
 
+    if (tid == 0) trace_mark(p.trace, TR_START);
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&B.full[s], 1);
@@ -770,6 +779,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     }
 
     pdl_wait();
+    if (tid == 0) trace_mark(p.trace, TR_WAITED);
     if (p.fill_sentinel) {
         // mark the buffer a later residual launch of this step will write
         // (its norm CTA waits for the marks to be overwritten)
@@ -787,6 +797,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     pdl_launch_dependents();
     if (p.norm_out && blockIdx.x == 0) {
         norm_cta(p, reinterpret_cast<float *>(ring));
+        if (tid == 0) trace_mark(p.trace, TR_END);
         return;
     }
 
@@ -802,6 +813,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                         pol);
         }
         if (p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
+        trace_mark(p.trace, TR_END);
         return;
     }
 
@@ -915,6 +927,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                 }
             }
         }
+        if (lane == 0) trace_mark(p.trace, TR_END);
         return;
     }
 
@@ -1011,6 +1024,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             mbar_arrive(&B.tready[j]);  // the terms may be summed (release)
         }
     }
+    if (lane == 0) trace_mark(p.trace, TR_END);
 #ifdef OVF_GEMV_TIMING
     if (lane == 0 && blockIdx.x == 0)
         printf("cw %d items %d rps %d T %d S %d tfree %lld full %lld comp %lld rest %lld\n", warp, items, rps, T,

@@ -82,6 +82,7 @@ struct GemvParams {
     DevStep *step;       // EPI_LOGITS_ARGMAX
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
     L2Prefetch pf;       // weights of a later launch to pull into L2 once this one's are issued
+    TraceSlot *trace;    // OVF_TRACE timeline slot, or null
 };
 
 struct GemvPlan {

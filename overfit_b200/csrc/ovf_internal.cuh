@@ -67,6 +67,8 @@ struct AttnParams {
     int split_half, H, KVH, hd, max_ctx, seq_len_host, n_splits, chunk_max, sc_floats;
     float scale;
     L2Prefetch pf;            // weights of later launches to pull into L2 during the chains
+    TraceSlot *trace;         // OVF_TRACE timeline slot, or null
+    int no_kv_prefetch;       // skip the early L2 prefetch of the cache rows
 };
 int attn_splits(int n_kv_heads);
 int64_t attn_scratch_bytes(int H, int KVH, int hd);
@@ -81,7 +83,8 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
-                        DevStep *step_mut, float *norm_out, float eps, cudaStream_t st, bool pdl);
+                        DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,
+                        bool pdl);
 ovf_status launch_silu_mul(const float *g, const float *u, float *h, int64_t n, cudaStream_t st, bool pdl);
 
 }  // namespace ovf

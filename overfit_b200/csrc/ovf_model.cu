@@ -66,6 +66,9 @@ struct ovf_session {
           *partial = nullptr;
     int *counters = nullptr, *tokens_log = nullptr;
     float *norm_s = nullptr;  // [0]: RMSNorm scale of hidden, [1]: of after
+    TraceSlot *trace = nullptr;  // OVF_TRACE=1: per-launch timeline of the last step
+    int trace_cap = 0, trace_n = 0;
+    std::vector<std::string> trace_labels;
     DevStep *step = nullptr;
     int32_t *pinned_tok = nullptr;  // host staging
     int pinned_cap = 0;
@@ -257,14 +260,54 @@ static void prof_report() {
     g_prof.acc.clear();
 }
 
+// OVF_TRACE=1: the last step's timeline, per launch role: mean duration
+// (first CTA start to last exit), mean time spent before griddepcontrol.wait
+// returned, and mean gap / overlap with the previous launch's end.
+static void trace_report(ovf_session *s) {
+    if (!s->trace || s->trace_n == 0) return;
+    std::vector<TraceSlot> t(s->trace_n);
+    if (cudaMemcpy(t.data(), s->trace, t.size() * sizeof(TraceSlot), cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    struct Acc { double dur = 0, wait = 0, gap = 0; int n = 0; };
+    std::vector<std::pair<std::string, Acc>> acc;
+    const unsigned long long t0 = ~t[0].start_c;
+    unsigned long long prev_end = t0;
+    for (int i = 0; i < s->trace_n; ++i) {
+        const unsigned long long st = ~t[i].start_c, en = t[i].end, wt = t[i].waited;
+        Acc *a = nullptr;
+        for (auto &x : acc)
+            if (x.first == s->trace_labels[i]) a = &x.second;
+        if (!a) {
+            acc.push_back({s->trace_labels[i], Acc{}});
+            a = &acc.back().second;
+        }
+        a->dur += (double)(en - st) / 1e3;
+        a->wait += wt > st ? (double)(wt - st) / 1e3 : 0.0;
+        a->gap += ((double)st - (double)prev_end) / 1e3;
+        a->n += 1;
+        prev_end = en;
+    }
+    fprintf(stderr, "[ovf trace] step span %.1f us over %d launches\n", (double)(prev_end - t0) / 1e3, s->trace_n);
+    for (auto &x : acc)
+        fprintf(stderr, "[ovf trace] %-8s n=%3d  dur %8.2f us  pre-wait %7.2f us  start-after-prev-end %7.2f us\n",
+                x.first.c_str(), x.second.n, x.second.dur / x.second.n, x.second.wait / x.second.n,
+                x.second.gap / x.second.n);
+}
+
 // Enqueues one token's kernels on s->stream.
 ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     ovf_model *m = s->m;
     const ovf_model_config &c = m->cfg;
     const cudaStream_t st = s->stream;
     const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim;
+    s->trace_n = 0;
+    auto tslot = [&](const char *label) -> TraceSlot * {
+        if (!s->trace || s->trace_n >= s->trace_cap) return nullptr;
+        if ((int)s->trace_labels.size() <= s->trace_n) s->trace_labels.push_back(label);
+        return &s->trace[s->trace_n++];
+    };
+    if (s->trace) OVF_CUDA_TRY(cudaMemsetAsync(s->trace, 0, (size_t)s->trace_cap * sizeof(TraceSlot), st));
     ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step,
-                                &s->norm_s[0], c.eps, st, true);
+                                &s->norm_s[0], c.eps, tslot("embed"), st, true);
     prof_mark(st, "embed");
     if (r) return r;
     for (int l = 0; l < c.n_layers; ++l) {
@@ -287,6 +330,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.epi = EPI_STORE;
             p.fill_sentinel = s->after;  // Wo's norm CTA watches `after` being written
             p.fill_n = D;
+            p.trace = tslot("qkv");
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "qkv");
         } else {
@@ -308,6 +352,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                     p.fill_sentinel = s->after;
                     p.fill_n = D;
                 }
+                p.trace = tslot("qkv");
                 if ((r = gemv_launch(p, st, true))) return r;
                 prof_mark(st, "qkv");
             }
@@ -336,6 +381,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             add_prefetch(a.pf, L.gate);
             add_prefetch(a.pf, L.up);
         }
+        a.trace = tslot("attn");
+        a.no_kv_prefetch = env_flag("OVF_ATTN_NOPF") ? 1 : 0;
         if (s->kv_dtype == OVF_KV_F32) {
             if ((r = launch_attention_exact(a, s->max_ctx, st, true))) return r;
         } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
@@ -359,6 +406,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
             if (l2_prefetch_mode() & 4) add_prefetch(p.pf, L.down);
             p.eps = c.eps;
+            p.trace = tslot("wo");
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "wo");
         }
@@ -383,6 +431,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 add_prefetch(p.pf, N.wk);
                 add_prefetch(p.pf, N.wv);
             }
+            p.trace = tslot("gateup");
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "gateup");
         } else {
@@ -403,6 +452,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                     p.fill_sentinel = s->hidden;
                     p.fill_n = D;
                 }
+                p.trace = tslot("gateup");
                 if ((r = gemv_launch(p, st, true))) return r;
                 prof_mark(st, "gateup");
             }
@@ -420,6 +470,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.resid = s->after;
             p.norm_out = &s->norm_s[0];  // RMSNorm scale of the new hidden: next layer / final norm
             p.eps = c.eps;
+            p.trace = tslot("down");
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "down");
         }
@@ -437,6 +488,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         p.epi = EPI_LOGITS_ARGMAX;
         p.step = s->step;
         p.tokens_out = s->tokens_log;
+        p.trace = tslot("lmhead");
         if ((r = gemv_launch(p, st, true))) return r;
         prof_mark(st, "lmhead");
     }
@@ -641,6 +693,10 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     A((void **)&s->partial, (size_t)attn_scratch_bytes(c.n_heads, c.n_kv_heads, c.head_dim));
     A((void **)&s->counters, (size_t)c.n_kv_heads * 4);
     A((void **)&s->norm_s, 2 * 4);
+    if (env_flag("OVF_TRACE")) {
+        s->trace_cap = 8 * c.n_layers + 16;
+        A((void **)&s->trace, (size_t)s->trace_cap * sizeof(TraceSlot));
+    }
     A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
     A((void **)&s->step, sizeof(DevStep));
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
@@ -666,6 +722,7 @@ ovf_status ovf_session_destroy(ovf_session *s) {
     DeviceGuard guard(s->m->device);
     if (s->stream) cudaStreamSynchronize(s->stream);
     prof_report();
+    trace_report(s);
     if (s->graph_logits) cudaGraphExecDestroy(s->graph_logits);
     if (s->graph_nologits) cudaGraphExecDestroy(s->graph_nologits);
     for (void *p : s->allocs) cudaFree(p);

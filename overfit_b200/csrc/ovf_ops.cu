@@ -358,8 +358,10 @@ ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float 
 // position; then warp 0 runs the first layer's RMSNorm sum of squares in
 // the reference's order and leaves the scale in norm_out (one CTA).
 __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict__ w, const float *__restrict__ q8s,
-                             int d, float *__restrict__ hidden, float *norm_out, float eps) {
+                             int d, float *__restrict__ hidden, float *norm_out, float eps, TraceSlot *trace) {
+    if (threadIdx.x == 0) trace_mark(trace, TR_START);
     pdl_wait();
+    if (threadIdx.x == 0) trace_mark(trace, TR_WAITED);
     const int token = step->token;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         float v;
@@ -380,13 +382,14 @@ __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict_
         const float ss = cta_seq_sumsq(hidden, d, 0.0f, stage);
         if (threadIdx.x == 0) *norm_out = rms_scale(ss, d, eps);
     }
+    if (threadIdx.x == 0) trace_mark(trace, TR_END);
     pdl_launch_dependents();
 }
 
 ovf_status launch_embed(const DevStep *, int type, const void *w, const float *q8s, int d, float *hidden,
-                        DevStep *step, float *norm_out, float eps, cudaStream_t st, bool pdl) {
+                        DevStep *step, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st, bool pdl) {
     cudaError_t e = launch_pdl(embed_kernel, dim3(1), dim3(1024), 0, st, pdl, step, type, (const uint8_t *)w, q8s, d,
-                               hidden, norm_out, eps);
+                               hidden, norm_out, eps, trace);
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "embed");
 }
 

@@ -98,3 +98,28 @@ def test_session_edge_cases(E):
     l1 = s.get_last_logits()
     s.reset([1, 2])
     np.testing.assert_array_equal(s.get_last_logits(), l1)
+
+
+@pytest.mark.parametrize("cfg", [TINY_LLAMA, TINY_QWEN], ids=["llama_q4km", "qwen2_q8_0"])
+def test_fp16_kv_session_tracks_fp16_restatement(E, orc, cfg):
+    """The fp16-KV session (the benchmark config's cache; flash-decode
+    attention, no reference counterpart) against the restatement with its
+    cache rounded to fp16 the same way: within the 1e-2 bar at every step and
+    identical greedy tokens for 32 steps."""
+    mf = make_model_file(cfg, seed=1)
+    eng = E.CudaLlamaInferenceEngine(cfg, mf)
+    sess = eng.create_session(128, "f16")
+    ref = oracle_session(cfg, mf, 128)
+    ref.set_kv_fp16(True)
+    prompt = np.random.default_rng(7).integers(0, cfg["vocab"], 20)
+    tok = sess.prefill(prompt)
+    for t in prompt:
+        lg_ref = ref.decode(int(t))
+    assert rel_l2(sess.get_last_logits(), lg_ref) < REL_L2
+    for step in range(32):
+        nxt_ref = int(np.argmax(lg_ref))
+        assert tok == nxt_ref, f"greedy token differs at step {step}"
+        tok = sess.decode(tok)
+        lg_ref = ref.decode(nxt_ref)
+        assert rel_l2(sess.get_last_logits(), lg_ref) < REL_L2, step
+
