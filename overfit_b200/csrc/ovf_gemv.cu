@@ -1101,7 +1101,19 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     // the busiest CTA's streamed bytes plus a fixed per-tile cost (~2 KB
     // equivalent): balanced tile counts matter for the small matrices.
     const int budget = (smem_optin(device) + 1024) / kCtasPerSm - 2048;  // leaves room for static smem
-    const int t_cap = std::max(1, std::min(64, (OVF_GEMV_TILE_KB * 1024) / (rb * parts))) * parts;
+    // Long rows (few blocks per row fill few compute threads) may take
+    // larger tiles: each tile costs the larger of its streaming time and its
+    // contraction latency, one round per kComputeThreads blocks (a round
+    // weighs about as much as streaming 16 KB of Q4_K, 36 KB of Q6_K or
+    // 4 KB of Q8_0 per CTA: the per-block instruction counts differ).
+    int t_cap = std::max(1, std::min(64, (OVF_GEMV_TILE_KB * 1024) / (rb * parts))) * parts;
+    const int t_fill = ((kComputeThreads + nb - 1) / nb + parts - 1) / parts * parts;
+    while (t_cap < t_fill && (t_cap + parts) * rb * 2 <= budget - 16 * 1024) t_cap += parts;
+    double round_bytes = 4096.0;
+    for (int s = 0; s < p.nseg; ++s)
+        round_bytes = std::max(round_bytes, p.seg[s].type == OVF_TYPE_Q6_K   ? 36864.0
+                                            : p.seg[s].type == OVF_TYPE_Q4_K ? 16384.0
+                                                                             : 4096.0);
     int best_T = parts;
     double best_cost = 1e300;
     for (int T = parts; T <= t_cap; T += parts) {
@@ -1112,7 +1124,9 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
             for (int s = 0; s < p.nseg; ++s) tiles += (p.seg[s].rows + rows_per - 1) / rows_per;
         if (tiles == 0) break;
         const int grid = std::min(nsm * kCtasPerSm, tiles);
-        const double cost = (double)((tiles + grid - 1) / grid) * ((double)T * rb + 2048.0);
+        const double rounds = (double)((T * nb + kComputeThreads - 1) / kComputeThreads);
+        const double cost = (double)((tiles + grid - 1) / grid) *
+                            std::max((double)T * rb + 2048.0, rounds * round_bytes);
         if (cost < best_cost * 0.999) {
             best_cost = cost;
             best_T = T;
