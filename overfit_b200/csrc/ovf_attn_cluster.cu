@@ -47,7 +47,27 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     float *knew = fold + G * hd;                                  // [hd]
     float *vnew = knew + hd;                                      // [hd]
 
+    if (tid == 0) trace_mark(p.trace, TR_START);
+    if (tid == 0 && p.pos_dev) {
+        // The cache rows before this token do not depend on the previous
+        // kernel: pull this CTA's keys and values into L2 while it finishes
+        // (the position read here may still be the previous step's; it only
+        // bounds the hint).
+        const int sp = *(volatile const int *)p.pos_dev + 1;
+        const int pr = (sp + kCNC - 1) / kCNC;
+        const int a = min(sp, rank * pr), b = min(sp, a + pr);
+        if (b > a) {
+            L2Prefetch kv{};
+            const size_t hb = (size_t)g * p.max_ctx * hd;
+            kv.ptr[0] = p.kc + hb + (size_t)a * hd;
+            kv.ptr[1] = p.vc + hb + (size_t)a * hd;
+            kv.bytes[0] = kv.bytes[1] = (int64_t)(b - a) * hd * 2;
+            kv.n = 2;
+            prefetch_l2_slice(kv, 0, 1);
+        }
+    }
     pdl_wait();
+    if (tid == 0) trace_mark(p.trace, TR_WAITED);
     const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
     const int seq = pos + 1;
     const int per = (seq + kCNC - 1) / kCNC;
@@ -218,31 +238,45 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
         __syncthreads();
     }
     (void)fold;
-    // merge the cluster's partials on rank 0 through distributed shared memory
+    // merge the cluster's partials through distributed shared memory: every
+    // rank copies all ranks' (max, sum) per head, then finalises its own
+    // 1/kCNC of the outputs (16 independent remote loads per output)
     cluster.sync();
-    if (rank == 0) {
-        for (int i = tid; i < G * hd; i += kCThr) {
+    float *stm = fold, *stl = fold + kCNC * G;  // [kCNC][G] each (fold is free here)
+    for (int idx = tid; idx < kCNC * G; idx += kCThr) {
+        const int r = idx / G, h = idx % G;
+        const float *rst = cluster.map_shared_rank(st, r);
+        stm[idx] = rst[h];
+        stl[idx] = rst[G + h];
+    }
+    __syncthreads();
+    {
+        constexpr int PER = G * HD / kCNC;
+        for (int i = rank * PER + tid; i < (rank + 1) * PER; i += kCThr) {
             const int h = i / hd;
+            float pv[kCNC];
+#pragma unroll
+            for (int r = 0; r < kCNC; ++r) pv[r] = cluster.map_shared_rank(po, r)[i];
             float M = -INFINITY;
-            for (int r = 0; r < kCNC; ++r) {
-                const float *rst = cluster.map_shared_rank(st, r);
-                if (rst[G + h] > 0.0f) M = fmaxf(M, rst[h]);
-            }
+#pragma unroll
+            for (int r = 0; r < kCNC; ++r)
+                if (stl[r * G + h] > 0.0f) M = fmaxf(M, stm[r * G + h]);
             float L = 0.0f, acc = 0.0f;
+#pragma unroll
             for (int r = 0; r < kCNC; ++r) {
-                const float *rst = cluster.map_shared_rank(st, r);
-                const float lr = rst[G + h];
+                const float lr = stl[r * G + h];
                 if (lr > 0.0f) {
-                    const float w = expf(fsub(rst[h], M));
+                    const float w = expf(fsub(stm[r * G + h], M));
                     L = fadd(L, fmul(lr, w));
-                    acc = fadd(acc, fmul(w, cluster.map_shared_rank(po, r)[i]));
+                    acc = fadd(acc, fmul(w, pv[r]));
                 }
             }
             const bool ok = L > 0.0f && isfinite(L);
             p.out[(size_t)g * G * hd + i] = ok ? fdiv(acc, L) : 0.0f;
         }
     }
-    cluster.sync();  // partners' shared memory must outlive rank 0's reads
+    cluster.sync();  // partners' shared memory must outlive the other ranks' reads
+    if (tid == 0) trace_mark(p.trace, TR_END);
 }
 
 size_t attn_cluster_smem(int G, int hd) {
