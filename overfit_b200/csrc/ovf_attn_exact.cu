@@ -105,12 +105,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     }
     pdl_wait();
     if (tid == 0) trace_mark(p.trace, TR_WAITED);
-#ifdef OVF_ATTN_TIMING
-    long long T0 = clock64(), T1 = 0, T2 = 0, T3 = 0, T4 = 0, T5 = 0;
-#define ATM(x) x = clock64();
-#else
-#define ATM(x)
-#endif
     const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
     const int seq = pos + 1;
     const int chunk = (seq + kExactCluster - 1) / kExactCluster;
@@ -199,7 +193,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             }
         }
     }
-    ATM(T1)
     // 2. cluster-wide maximum
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xFFFFFFFFu, lmax, o));
@@ -216,7 +209,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     for (int t = t0 + tid; t < t1; t += kExactThreads) ex[t - t0] = exp_rn(fsub(ex[t - t0], gmax));
     cluster.sync();
 
-    ATM(T2)
     // 3. every CTA gathers all probabilities' numerators into its own shared
     //    memory, then thread 0 forms sumExp over t in order (the same chain,
     //    so the same value, in every CTA)
@@ -241,7 +233,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         }
     }
     __syncthreads();
-    ATM(T3)
     if (tid == 0) {
         float sum = 0.0f;
         const int s64 = seq & ~63;
@@ -272,7 +263,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         red[9] = sum;
     }
     __syncthreads();
-    ATM(T4)
     const float sumExp = red[9];
     const bool bad = !(sumExp > 0.0f) || isinf(sumExp);
     const float invSum = bad ? 0.0f : fdiv(1.0f, sumExp);
@@ -317,12 +307,6 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         stage_values(blk + NBUF);  // into the buffer just consumed
     }
     cp_async_wait<0>();
-    ATM(T5)
-#ifdef OVF_ATTN_TIMING
-    if (tid == 0 && blockIdx.x < 16 && p.pos_dev)
-        printf("attn cta %d pos %d: pre %lld scores %lld max+exp %lld gather %lld sumexp %lld out %lld\n", blockIdx.x,
-               pos, T1 - T0, T2 - T1, T3 - T2, T4 - T3, T5 - T4, 0ll);
-#endif
     if (tid < DPC) p.out[(size_t)h * HD + d0 + tid] = acc;
     cluster.sync();  // no CTA leaves while another may still read its shared memory
     if (tid == 0) trace_mark(p.trace, TR_END);

@@ -108,38 +108,16 @@ static __host__ __device__ inline size_t layout_smem(const Layout &L, int stages
 
 // ------------------------------------------------------------- dot units
 // One thread contracts one block of a row: a K-quant super-block (256
-// weights) or a Q8_0 block (32).  A thread keeps the activation of its
-// block in registers for the whole launch (the activation is the same for
-// every row), so a row costs only its weight bytes from shared memory.  The
+// weights, activation block read from shared memory) or a Q8_0 block (32;
+// the activation block is kept in registers for the whole launch).  The
 // integer parts are exact and the fp32 tail of every block follows the
 // reference's operand order.
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
 
-struct KqAct {        // Q8_K block: 256 quants, 16-element sums, scale
-    uint32_t q[64];
-    uint32_t bs[8];   // int16 pairs: sums (2i, 2i+1) of 16 elements
-    float s;
-};
 struct Q8Act {        // Q8_0 block: 32 quants + scale
     uint32_t q[8];
     float s;
 };
-
-__device__ __forceinline__ void load_kq_act(const uint8_t *aq, const uint8_t *meta, KqAct &a) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(aq + 16 * i);
-        a.q[4 * i] = v.x;
-        a.q[4 * i + 1] = v.y;
-        a.q[4 * i + 2] = v.z;
-        a.q[4 * i + 3] = v.w;
-    }
-    const uint4 b0 = *reinterpret_cast<const uint4 *>(meta);
-    const uint4 b1 = *reinterpret_cast<const uint4 *>(meta + 16);
-    a.bs[0] = b0.x; a.bs[1] = b0.y; a.bs[2] = b0.z; a.bs[3] = b0.w;
-    a.bs[4] = b1.x; a.bs[5] = b1.y; a.bs[6] = b1.z; a.bs[7] = b1.w;
-    a.s = *reinterpret_cast<const float *>(meta + 32);
-}
 
 __device__ __forceinline__ void load_q8_act(const uint8_t *act, Q8Act &a) {
     const uint4 v0 = *reinterpret_cast<const uint4 *>(act);
@@ -149,106 +127,9 @@ __device__ __forceinline__ void load_q8_act(const uint8_t *act, Q8Act &a) {
     a.s = *reinterpret_cast<const float *>(act + 32);
 }
 
-__device__ __forceinline__ int lo16(uint32_t w) { return (int)(int16_t)(w & 0xFFFFu); }
-__device__ __forceinline__ int hi16(uint32_t w) { return (int)(int16_t)(w >> 16); }
-
-// Q4_K x Q8_K over one super-block (Runtime/Q4KDotKernel.cs:216-256).
-__device__ __forceinline__ float q4k_block(const uint8_t *blk, const KqAct &a) {
-    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-    const float d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
-    const float dmin = h2f_bits((uint16_t)(h.x >> 16));
-    // 6-bit scales and mins (Loading/GgmlDequant.cs:49-77), four per word
-    const uint32_t sc03 = h.y & 0x3F3F3F3Fu, mn03 = h.z & 0x3F3F3F3Fu;
-    const uint32_t sc47 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
-    const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
-    int mainAcc = 0, mainAccH = 0;  // mainAccH: exact multiple of 16
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
-        const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
-        const uint32_t *l0 = a.q + 16 * p, *l1 = l0 + 4, *h0 = l0 + 8, *h1 = l0 + 12;
-        const uint32_t M = 0x0F0F0F0Fu, HM = 0xF0F0F0F0u;
-        // High nibbles stay in place (16 x nibble as the unsigned operand):
-        // that sum is 16x the nibble dot and is divided out exactly below.
-        int lo = dp4a((int)(qa.x & M), (int)l0[0], 0);
-        int lo2 = dp4a((int)(qb.x & M), (int)l1[0], 0);
-        int hi = dp4a_us(qa.x & HM, (int)h0[0], 0);
-        int hi2 = dp4a_us(qb.x & HM, (int)h1[0], 0);
-        lo = dp4a((int)(qa.y & M), (int)l0[1], lo);
-        lo2 = dp4a((int)(qb.y & M), (int)l1[1], lo2);
-        hi = dp4a_us(qa.y & HM, (int)h0[1], hi);
-        hi2 = dp4a_us(qb.y & HM, (int)h1[1], hi2);
-        lo = dp4a((int)(qa.z & M), (int)l0[2], lo);
-        lo2 = dp4a((int)(qb.z & M), (int)l1[2], lo2);
-        hi = dp4a_us(qa.z & HM, (int)h0[2], hi);
-        hi2 = dp4a_us(qb.z & HM, (int)h1[2], hi2);
-        lo = dp4a((int)(qa.w & M), (int)l0[3], lo);
-        lo2 = dp4a((int)(qb.w & M), (int)l1[3], lo2);
-        hi = dp4a_us(qa.w & HM, (int)h0[3], hi);
-        hi2 = dp4a_us(qb.w & HM, (int)h1[3], hi2);
-        const uint32_t scw = p < 2 ? sc03 : sc47;
-        mainAcc += (int)byte_of(scw, (2 * p) & 3) * (lo + lo2);
-        mainAccH += (int)byte_of(scw, (2 * p + 1) & 3) * (hi + hi2);
-    }
-    mainAcc += mainAccH >> 4;
-    // min correction: sum_s m[s] * (sum of the sub-block's 32 activations)
-    int minAcc = 0;
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-        const uint32_t mw = s < 4 ? mn03 : mn47;
-        const int ps = lo16(a.bs[s]) + hi16(a.bs[s]);
-        minAcc += (int)byte_of(mw, s & 3) * ps;
-    }
-    return fmul(a.s, fsub(fmul(d, i2f(mainAcc)), fmul(dmin, i2f(minAcc))));
-}
-
 // 32-bit word `w` of a block that may start 2 bytes past a word boundary.
 __device__ __forceinline__ uint32_t ldw_shifted(const uint32_t *base, int w, int sh) {
     return __funnelshift_r(base[w], base[w + 1], sh);
-}
-
-// Q6_K x Q8_K over one super-block (Runtime/Q6KDotKernel.cs:77-121 with the
-// unsigned dot :186-215): weight (k, l) of half h is ql[l + 32(k&1)] (low
-// nibble for k < 2, high for k >= 2) with qh[l] bits 2k..2k+1 and scale
-// sc[8h + l/16 + 2k]; the unsigned 6-bit dot minus 32 x the scaled
-// 16-element activation sums gives the signed dot exactly.
-__device__ __forceinline__ float q6k_block(const uint8_t *blk, const KqAct &a) {
-    const uintptr_t ad = reinterpret_cast<uintptr_t>(blk);
-    const uint32_t *base = reinterpret_cast<const uint32_t *>(ad & ~uintptr_t(3));
-    const int sh = (int)(ad & 3u) * 8;
-    int sc[16];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t w = ldw_shifted(base, 48 + i, sh);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) sc[4 * i + j] = (int)(int8_t)byte_of(w, j);
-    }
-    const float d = h2f_bits((uint16_t)(ldw_shifted(base, 52, sh) & 0xFFFFu));
-    int sum = 0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int lw = 0; lw < 8; ++lw) {
-            const uint32_t qla = ldw_shifted(base, 16 * h + lw, sh);
-            const uint32_t qlb = ldw_shifted(base, 16 * h + 8 + lw, sh);
-            const uint32_t qhw = ldw_shifted(base, 32 + 8 * h + lw, sh);
-            const uint32_t M = 0x0F0F0F0Fu, H = 0x30303030u;
-            const int q1 = (int)((qla & M) | ((qhw << 4) & H));
-            const int q2 = (int)((qlb & M) | ((qhw << 2) & H));
-            const int q3 = (int)(((qla >> 4) & M) | (qhw & H));
-            const int q4 = (int)(((qlb >> 4) & M) | ((qhw >> 2) & H));
-            const int is = lw >> 2;
-            const int b8 = 32 * h + lw;
-            sum += sc[8 * h + is] * dp4a(q1, (int)a.q[b8], 0) + sc[8 * h + is + 2] * dp4a(q2, (int)a.q[b8 + 8], 0) +
-                   sc[8 * h + is + 4] * dp4a(q3, (int)a.q[b8 + 16], 0) +
-                   sc[8 * h + is + 6] * dp4a(q4, (int)a.q[b8 + 24], 0);
-        }
-    }
-    int bsumTerm = 0;
-#pragma unroll
-    for (int s = 0; s < 8; ++s) bsumTerm += sc[2 * s] * lo16(a.bs[s]) + sc[2 * s + 1] * hi16(a.bs[s]);
-    const int mainAcc = sum - 32 * bsumTerm;
-    return fmul(fmul(d, a.s), i2f(mainAcc));
 }
 
 // Q8_0 x Q8_0 over one 32-block (Runtime/Q8DotKernel.cs:99-140).
@@ -631,11 +512,7 @@ __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L
 #ifndef OVF_GEMV_CW
 #define OVF_GEMV_CW 4
 #endif
-#ifndef OVF_GEMV_ACTREG
-#define OVF_GEMV_ACTREG 0
-#endif
 static constexpr int kComputeWarps = OVF_GEMV_CW;
-static constexpr bool kActRegs = OVF_GEMV_ACTREG;
 #ifndef OVF_GEMV_CTAS
 #define OVF_GEMV_CTAS 3
 #endif
@@ -956,26 +833,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
         }
     }
     const int rps = (T + RS - 1) / RS;
-    KqAct kact[(KQ && kActRegs) ? BPS : 1];
     Q8Act qact[KQ ? 1 : BPS];
 #pragma unroll
-    for (int b = 0; b < BPS; ++b) {
-        if (KQ && !kActRegs) continue;
-        if (KQ)
-            load_kq_act(smem + L.act_q_off + mblk[b] * kQ8kActStride, smem + L.act_meta_off + mblk[b] * kQ8kMetaStride,
-                        kact[(KQ && kActRegs) ? b : 0]);
-        else
-            load_q8_act(smem + L.act_q_off + mblk[b] * kQ80ActStride, qact[KQ ? 0 : b]);
-    }
+    for (int b = 0; b < BPS; ++b)
+        if (!KQ) load_q8_act(smem + L.act_q_off + mblk[b] * kQ80ActStride, qact[KQ ? 0 : b]);
     const size_t sb = (size_t)(p.K / 8);
-#ifdef OVF_GEMV_TIMING
-    long long t_tf = 0, t_full = 0, t_comp = 0, t_rest = 0, t0 = clock64(), t1;
-#define TMARK(v) t1 = clock64(); v += t1 - t0; t0 = t1;
-#else
-#define TMARK(v)
-#endif
     for (int it = 0; it < items; ++it) {
-        TMARK(t_rest)
         const int s = it % p.stages, j = it % kTermBufs;
         const GroupRef g = locate(p, tcta + it * tgrid);
         const int ttype = p.seg[p.pair ? 0 : g.seg].type;  // a tile never mixes types
@@ -984,11 +847,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
         const uint8_t *qbase = stage + (((size_t)g.r0 * rb) & 15);
         const uint8_t *sbase = stage + L.s_region + (((size_t)g.r0 * sb) & 15);
         float *tb = tbuf + (size_t)j * T * nb;
-        TMARK(t_rest)
         if (it >= kTermBufs) wait_or_abort(&B.tfree[j], (uint32_t)(((it / kTermBufs) - 1) & 1), B.abort_flag);
-        TMARK(t_tf)
         wait_or_abort(&B.full[s], (uint32_t)((it / p.stages) & 1), B.abort_flag);
-        TMARK(t_full)
         for (int rr = 0; rr < rps; ++rr) {
             const int r = subset + rr * RS;
             int useg = 0, urow = 0;
@@ -1000,11 +860,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             for (int b = 0; b < BPS; ++b) {
                 if (!mval[b]) continue;
                 float t;
-                if (KQ && kActRegs) {
-                    const KqAct &a = kact[(KQ && kActRegs) ? b : 0];
-                    t = ttype == OVF_TYPE_Q4_K ? q4k_block(rp + (size_t)mblk[b] * 144, a)
-                                               : q6k_block(rp + (size_t)mblk[b] * 210, a);
-                } else if (KQ) {
+                if (KQ) {
                     const uint8_t *aq = smem + L.act_q_off + mblk[b] * kQ8kActStride;
                     const uint8_t *am = smem + L.act_meta_off + mblk[b] * kQ8kMetaStride;
                     t = ttype == OVF_TYPE_Q4_K ? q4k_unit(rp + (size_t)mblk[b] * 144, aq, am)
@@ -1018,18 +874,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             }
         }
         __syncwarp();
-        TMARK(t_comp)
         if (lane == 0) {
             mbar_arrive(&B.empty[s]);   // the stage may be refilled
             mbar_arrive(&B.tready[j]);  // the terms may be summed (release)
         }
     }
     if (lane == 0) trace_mark(p.trace, TR_END);
-#ifdef OVF_GEMV_TIMING
-    if (lane == 0 && blockIdx.x == 0)
-        printf("cw %d items %d rps %d T %d S %d tfree %lld full %lld comp %lld rest %lld\n", warp, items, rps, T,
-               p.stages, t_tf, t_full, t_comp, t_rest);
-#endif
 }
 
 // ---------------------------------------------------------------- host side

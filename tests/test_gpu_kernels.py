@@ -226,13 +226,29 @@ def test_argument_errors_raise(K):
 
 
 # ------------------------------------------------------------------- small ops
-def test_rmsnorm_close(K, orc):
-    """Block-reduced sum of squares vs the reference's sequential sum: 2e-6 relative."""
-    x = np.random.default_rng(9).normal(0, 3, 4096).astype(np.float32)
-    gmm = np.random.default_rng(10).normal(1, 0.1, 4096).astype(np.float32)
-    y = torch.empty(4096, device="cuda")
+@pytest.mark.parametrize("d", [896, 4096, 14336])
+def test_rmsnorm_bit_exact(K, orc, d):
+    """RmsNormalize with the reference's sequential sum of squares: bit-exact."""
+    x = np.random.default_rng(9 + d).normal(0, 3, d).astype(np.float32)
+    gmm = np.random.default_rng(10 + d).normal(1, 0.1, d).astype(np.float32)
+    y = torch.empty(d, device="cuda")
     K.rms_normalize(dev(x), dev(gmm), y, 1e-6)
-    np.testing.assert_allclose(host(y), orc.rmsnorm(x, gmm, 1e-6), rtol=2e-6, atol=1e-7)
+    np.testing.assert_array_equal(host(y), orc.rmsnorm(x, gmm, 1e-6))
+
+
+def test_lm_head_full_size_bit_exact(K, orc):
+    """The largest projection of the benchmark step at its full size: the
+    Llama-3-8B Q6_K output head, 128256 x 4096, against the restatement."""
+    n, k = 128256, 4096
+    w = orc.fill_normal(n * k, 77, 0.0, 0.02).reshape(n, k)
+    wb = orc.quantize_q6k(w)
+    del w
+    x = np.random.default_rng(78).normal(0, 1, k).astype(np.float32)
+    ref = orc.kq_project(orc.Q6_K, x, wb, n, k)
+    y = torch.empty(n, device="cuda")
+    q, s, b = _act_scratch(k)
+    K.Q6KDotKernel.project_parallel(dev(x), K.KQuantWeight(dev(wb), k, n, orc.Q6_K), None, y, q, s, b)
+    np.testing.assert_array_equal(host(y), ref)
 
 
 @pytest.mark.parametrize("split_half", [0, 1])
