@@ -84,6 +84,7 @@ def _declare(L):
         "orc_session_destroy": (None, [P]),
         "orc_session_reset": (None, [P]),
         "orc_session_set_kv_fp16": (None, [P, C.c_int]),
+        "orc_set_exp_double_rounded": (None, [C.c_int]),
         "orc_session_position": (C.c_int, [P]),
         "orc_session_decode": (C.c_int, [P, C.c_int, P]),
         "orc_session_decode_layers": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P]),
@@ -406,3 +407,11 @@ class OracleSession:
             self.close()
         except Exception:
             pass
+
+
+def set_exp_double_rounded(on: bool = True):
+    """Test switch: the restatement's exp becomes a double-precision exp
+    rounded once (the GPU's), instead of the C library's expf (the
+    reference's MathF.Exp).  Isolates exp rounding from everything else."""
+    lib().orc_set_exp_double_rounded(int(on))
+

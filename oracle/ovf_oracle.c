@@ -574,6 +574,15 @@ void orc_rope_apply(float *v, int hd, const float *c, const float *s, int split_
     }
 }
 
+/* e^x as the reference computes it: MathF.Exp, i.e. the host C library's
+ * expf.  Test switch (orc_set_exp_double_rounded): round a double-precision
+ * exp once instead, as the GPU does, to separate the two libraries' rounding
+ * (ULP-level parity of MathF.Exp / TensorPrimitives.Sigmoid is unpinned)
+ * from everything else. */
+static int g_exp_double_rounded = 0;
+void orc_set_exp_double_rounded(int on) { g_exp_double_rounded = on; }
+static float orc_expf(float x) { return g_exp_double_rounded ? (float)exp((double)x) : expf(x); }
+
 /* Runtime/CachedAttentionKernel.cs:342-390 (Dot, AVX2 branch): two 8-lane
  * accumulators over 16-wide steps, then Vector256.Sum(acc0 + acc1).  The lane
  * fold order of Vector256.Sum is the .NET runtime's; it is restated as
@@ -617,7 +626,7 @@ void orc_attention_single_head(const float *q, const float *keys, const float *v
     }
     float sumExp = 0.0f;
     for (int t = 0; t < seq_len; t++) {
-        float e = expf(scratch[t] - maxScore);
+        float e = orc_expf(scratch[t] - maxScore);
         scratch[t] = e;
         sumExp += e;
     }
@@ -635,7 +644,7 @@ void orc_attention_single_head(const float *q, const float *keys, const float *v
  * multiply; TensorPrimitives.Sigmoid is 1/(1+e^-x) to a few ULP. */
 void orc_silu_inplace(float *v, int64_t n) {
     for (int64_t i = 0; i < n; i++) {
-        float sg = 1.0f / (1.0f + expf(-v[i]));
+        float sg = 1.0f / (1.0f + orc_expf(-v[i]));
         v[i] = v[i] * sg;
     }
 }

@@ -122,6 +122,8 @@ void orc_session_reset(orc_session *s);
 /* Test switch: store K/V rounded to fp16 (the GPU's cache format); the
  * reference's cache is F32 (Runtime/KeyValueCache.cs:593-602). */
 void orc_session_set_kv_fp16(orc_session *s, int on);
+/* Test switch: exp rounded once from double precision (as on the GPU). */
+void orc_set_exp_double_rounded(int on);
 int  orc_session_position(const orc_session *s);
 /* One token through the stack; writes logits[vocab] when logits != NULL. */
 int  orc_session_decode(orc_session *s, int token, float *logits);
