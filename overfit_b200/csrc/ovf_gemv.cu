@@ -521,6 +521,17 @@ static constexpr int kCtasPerSm = OVF_GEMV_CTAS;
 #define OVF_GEMV_TILE_KB 16
 #endif
 static constexpr int kComputeThreads = kComputeWarps * 32;
+// The compute warps may form kGroups groups that take alternate tiles (a
+// CTA then contracts kGroups tiles at once).  Measured on B200 the
+// contraction is issue-bound rather than latency-bound, and two groups were
+// slower, so one group is the default.
+#ifndef OVF_GEMV_GROUPS
+#define OVF_GEMV_GROUPS 1
+#endif
+static constexpr int kGroups = OVF_GEMV_GROUPS;
+static constexpr int kGroupWarps = kComputeWarps / kGroups;
+static constexpr int kGroupThreads = kGroupWarps * 32;
+static_assert(kComputeWarps % kGroups == 0 && kTermBufs % kGroups == 0, "compute groups");
 static constexpr int kSumWarp = kComputeWarps;
 static constexpr int kProducerWarp = kComputeWarps + 1;
 static constexpr int kThreads = (kComputeWarps + 2) * 32;
@@ -636,10 +647,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     if (tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&B.full[s], 1);
-            mbar_init(&B.empty[s], kComputeWarps);
+            mbar_init(&B.empty[s], kGroupWarps);  // stage s always serves the same group
         }
         for (int j = 0; j < kTermBufs; ++j) {
-            mbar_init(&B.tready[j], kComputeWarps);
+            mbar_init(&B.tready[j], kGroupWarps);
             mbar_init(&B.tfree[j], 1);
         }
         *B.abort_flag = 0;
@@ -813,21 +824,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     // super-block or Q8_0 32-block).  With fewer blocks than threads the
     // threads split the tile's rows into RS subsets; with more (Q8_0 only),
     // a thread takes BPS blocks.
-    constexpr int NS = kComputeThreads;
+    constexpr int NS = kGroupThreads;
+    const int grp = warp / kGroupWarps, gtid = tid - grp * kGroupThreads;
     int RS = 1, subset = 0;
     bool slot_ok = true;
     int mblk[BPS];
     bool mval[BPS];
     if (BPS == 1) {
         RS = max(1, NS / nb);
-        subset = tid / nb;
-        slot_ok = tid < RS * nb;
-        mblk[0] = slot_ok ? tid % nb : 0;
+        subset = gtid / nb;
+        slot_ok = gtid < RS * nb;
+        mblk[0] = slot_ok ? gtid % nb : 0;
         mval[0] = slot_ok;
     } else {
 #pragma unroll
         for (int b = 0; b < BPS; ++b) {
-            const int m = tid + b * NS;
+            const int m = gtid + b * NS;
             mval[b] = m < nb;
             mblk[b] = mval[b] ? m : 0;
         }
@@ -838,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     for (int b = 0; b < BPS; ++b)
         if (!KQ) load_q8_act(smem + L.act_q_off + mblk[b] * kQ80ActStride, qact[KQ ? 0 : b]);
     const size_t sb = (size_t)(p.K / 8);
-    for (int it = 0; it < items; ++it) {
+    for (int it = grp; it < items; it += kGroups) {
         const int s = it % p.stages, j = it % kTermBufs;
         const GroupRef g = locate(p, tcta + it * tgrid);
         const int ttype = p.seg[p.pair ? 0 : g.seg].type;  // a tile never mixes types
@@ -953,11 +965,11 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     const int budget = (smem_optin(device) + 1024) / kCtasPerSm - 2048;  // leaves room for static smem
     // Long rows (few blocks per row fill few compute threads) may take
     // larger tiles: each tile costs the larger of its streaming time and its
-    // contraction latency, one round per kComputeThreads blocks (a round
+    // contraction latency, one round per kGroupThreads blocks (a round
     // weighs about as much as streaming 16 KB of Q4_K, 36 KB of Q6_K or
     // 4 KB of Q8_0 per CTA: the per-block instruction counts differ).
     int t_cap = std::max(1, std::min(64, (OVF_GEMV_TILE_KB * 1024) / (rb * parts))) * parts;
-    const int t_fill = ((kComputeThreads + nb - 1) / nb + parts - 1) / parts * parts;
+    const int t_fill = ((kGroupThreads + nb - 1) / nb + parts - 1) / parts * parts;
     while (t_cap < t_fill && (t_cap + parts) * rb * 2 <= budget - 16 * 1024) t_cap += parts;
     double round_bytes = 4096.0;
     for (int s = 0; s < p.nseg; ++s)
@@ -974,7 +986,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
             for (int s = 0; s < p.nseg; ++s) tiles += (p.seg[s].rows + rows_per - 1) / rows_per;
         if (tiles == 0) break;
         const int grid = std::min(nsm * kCtasPerSm, tiles);
-        const double rounds = (double)((T * nb + kComputeThreads - 1) / kComputeThreads);
+        const double rounds = (double)((T * nb + kGroupThreads - 1) / kGroupThreads);
         const double cost = (double)((tiles + grid - 1) / grid) *
                             std::max((double)T * rb + 2048.0, rounds * round_bytes);
         if (cost < best_cost * 0.999) {
@@ -1003,6 +1015,7 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     int s_hi = 8, s_lo = 2;
     if (const char *e = getenv("OVF_GEMV_S")) s_hi = s_lo = std::max(2, std::min(8, atoi(e)));
     for (int S = s_hi; S >= s_lo; --S) {
+        if (S % kGroups) continue;  // stage s must always serve the same compute group
         p.stages = S;
         const Layout L = make_layout(p);
         if (layout_smem(L, S) <= (size_t)budget) {
@@ -1014,15 +1027,17 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
     OVF_CHECK_ARG(stages >= 2, "gemv: K=%d does not fit shared memory", p.K);
     p.stages = stages;
     // Blocks per compute slot: the activation slices live in registers.
-    int bps = (nb + kComputeThreads - 1) / kComputeThreads;
-    OVF_CHECK_ARG(bps <= (kq ? 1 : 4), "gemv: K=%d is too long (at most %d)", p.K,
-                  kq ? kComputeThreads * 256 : 4 * kComputeThreads * 32);
-    if (!kq && bps == 3) bps = 4;
-    void (*kern)(GemvParams) = kq ? gemv_kernel<true, 1>
-                               : (bps == 1 ? gemv_kernel<false, 1>
-                                           : (bps == 2 ? gemv_kernel<false, 2> : gemv_kernel<false, 4>));
-    const int ki = kq ? 0 : (bps == 1 ? 1 : (bps == 2 ? 2 : 3));
-    static bool attr_done[64][4] = {};
+    int bps = (nb + kGroupThreads - 1) / kGroupThreads;
+    OVF_CHECK_ARG(bps <= (kq ? 2 : 8), "gemv: K=%d is too long (at most %d)", p.K,
+                  kq ? 2 * kGroupThreads * 256 : 8 * kGroupThreads * 32);
+    bps = bps <= 1 ? 1 : bps <= 2 ? 2 : bps <= 4 ? 4 : 8;
+    void (*kern)(GemvParams) = kq ? (bps == 1 ? gemv_kernel<true, 1> : gemv_kernel<true, 2>)
+                               : (bps == 1   ? gemv_kernel<false, 1>
+                                  : bps == 2 ? gemv_kernel<false, 2>
+                                  : bps == 4 ? gemv_kernel<false, 4>
+                                             : gemv_kernel<false, 8>);
+    const int ki = kq ? (bps == 1 ? 0 : 1) : (bps == 1 ? 2 : bps == 2 ? 3 : bps == 4 ? 4 : 5);
+    static bool attr_done[64][6] = {};
     if (device < 64 && !attr_done[device][ki]) {
         cudaFuncAttributes fa{};
         OVF_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
