@@ -24,8 +24,9 @@ namespace cg = cooperative_groups;
 namespace ovf {
 
 static constexpr int kCNC = 16;    // CTAs per cluster (non-portable size, allowed on B200)
-static constexpr int kCThr = 128;  // threads per CTA
-static constexpr int kCTK = 64;    // keys per tile
+static constexpr int kCThr = 512;  // threads per CTA
+static constexpr int kCTK = 128;   // keys per tile
+static constexpr int kCBuf = 2;    // tiles in flight
 
 template <int GT, int HD>
 __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnParams p) {
@@ -36,10 +37,10 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     const int rank = (int)cluster.block_rank();
     const int g = blockIdx.y;
     // shared memory map (the mbarriers first: they need 8-byte alignment)
-    uint64_t *bar = reinterpret_cast<uint64_t *>(csm);            // [2]
-    __half *kt = reinterpret_cast<__half *>(csm + 128);         // [2][TK][hd]
-    __half *vt = kt + 2 * kCTK * hd;                              // [2][TK][hd]
-    float *qs = reinterpret_cast<float *>(vt + 2 * kCTK * hd);   // [G][hd]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(csm);            // [kCBuf]
+    __half *kt = reinterpret_cast<__half *>(csm + 128);         // [kCBuf][TK][hd]
+    __half *vt = kt + kCBuf * kCTK * hd;                          // [kCBuf][TK][hd]
+    float *qs = reinterpret_cast<float *>(vt + kCBuf * kCTK * hd);  // [G][hd]
     float *sc = qs + G * hd;                                      // [G][TK]
     float *st = sc + G * kCTK;                                    // m[G], l[G], alpha[G]
     float *po = st + 3 * G;                                       // [G][hd] partial (fold target)
@@ -78,8 +79,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     const uint64_t pol = l2_evict_first_policy();
 
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int b = 0; b < kCBuf; ++b) mbar_init(&bar[b], 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -90,10 +90,8 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
         bulk_g2s(kt + (size_t)buf * kCTK * hd, p.kc + head + (size_t)a * hd, bytes, &bar[buf], pol);
         bulk_g2s(vt + (size_t)buf * kCTK * hd, p.vc + head + (size_t)a * hd, bytes, &bar[buf], pol);
     };
-    if (tid == 0) {
-        if (ntiles > 0) issue(0, 0);
-        if (ntiles > 1) issue(1, 1);
-    }
+    if (tid == 0)
+        for (int b = 0; b < kCBuf && b < ntiles; ++b) issue(b, b);
     for (int i = tid; i < G * hd; i += kCThr) qs[i] = p.q[(size_t)g * G * hd + i];
     const bool owns_new = p.k_new != nullptr && pos >= t0 && pos < t1;
     if (owns_new)
@@ -132,9 +130,9 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
 
     bool failed = false;
     for (int tile = 0; tile < ntiles; ++tile) {
-        const int buf = tile & 1;
+        const int buf = tile % kCBuf;
         const int a = t0 + tile * kCTK, n = min(kCTK, t1 - a);
-        if (!mbar_wait_bounded(&bar[buf], (uint32_t)((tile >> 1) & 1))) {
+        if (!mbar_wait_bounded(&bar[buf], (uint32_t)((tile / kCBuf) & 1))) {
             failed = true;
             break;
         }
@@ -146,32 +144,43 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
             }
             __syncthreads();
         }
-        // scores: four threads per key, a quarter of the dimension each
-        for (int kb = 0; kb < kCTK; kb += kCThr / 4) {
-            const int t = kb + (tid >> 2), q4 = tid & 3;
-            const bool ok = t < n;
-            float kv[HQ];
-            const uint4 *kr = reinterpret_cast<const uint4 *>(K + (size_t)(ok ? t : 0) * hd + q4 * HQ);
-#pragma unroll
-            for (int i = 0; i < HQ / 8; ++i) {
-                const uint4 w = kr[i];
+        // scores: LPK lanes per key, each one 16-byte chunk (8 halves) of the
+        // key row, so the lanes of a quarter-warp read 128 contiguous bytes
+        // (no shared-memory bank conflicts); partial dots are reduced over
+        // the LPK lanes.  (This path is within tolerance of the reference,
+        // not bit-exact: fused multiply-adds.)
+        {
+            constexpr int LPK = HD / 8 < 32 ? HD / 8 : 32;
+            constexpr int KPP = kCThr / LPK;  // keys per pass
+            const int c16 = tid % LPK;
+            for (int kb = 0; kb < n; kb += KPP) {
+                const int t = kb + tid / LPK;
+                const bool ok = t < n;
+                float kv[8];
+                const uint4 w = *reinterpret_cast<const uint4 *>(K + (size_t)(ok ? t : 0) * hd + 8 * c16);
                 const __half2 *h2 = reinterpret_cast<const __half2 *>(&w);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const float2 f = __half22float2(h2[j]);
-                    kv[8 * i + 2 * j] = f.x;
-                    kv[8 * i + 2 * j + 1] = f.y;
+                    kv[2 * j] = f.x;
+                    kv[2 * j + 1] = f.y;
                 }
-            }
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float *qh = qs + h * hd + q4 * HQ;
-                float acc = 0.0f;
+                for (int h = 0; h < G; ++h) {
+                    const float4 qa = *reinterpret_cast<const float4 *>(qs + h * hd + 8 * c16);
+                    const float4 qb = *reinterpret_cast<const float4 *>(qs + h * hd + 8 * c16 + 4);
+                    float acc = qa.x * kv[0];
+                    acc = fmaf(qa.y, kv[1], acc);
+                    acc = fmaf(qa.z, kv[2], acc);
+                    acc = fmaf(qa.w, kv[3], acc);
+                    acc = fmaf(qb.x, kv[4], acc);
+                    acc = fmaf(qb.y, kv[5], acc);
+                    acc = fmaf(qb.z, kv[6], acc);
+                    acc = fmaf(qb.w, kv[7], acc);
 #pragma unroll
-                for (int i = 0; i < HQ; ++i) acc = fadd(acc, fmul(qh[i], kv[i]));
-                acc = fadd(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 1));
-                acc = fadd(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, 2));
-                if (ok && q4 == 0) sc[h * kCTK + t] = fmul(acc, p.scale);
+                    for (int o = 1; o < LPK; o <<= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+                    if (ok && c16 == 0) sc[h * kCTK + t] = acc * p.scale;
+                }
             }
         }
         __syncthreads();
@@ -210,14 +219,14 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
 #pragma unroll
             for (int h = 0; h < G; ++h) {
                 const float pr = sc[h * kCTK + t];
-                o0[h] = fadd(o0[h], fmul(pr, v.x));
-                o1[h] = fadd(o1[h], fmul(pr, v.y));
+                o0[h] = fmaf(pr, v.x, o0[h]);
+                o1[h] = fmaf(pr, v.y, o1[h]);
             }
         }
         __syncthreads();  // tile buffers and scores are free again
-        if (tid == 0 && tile + 2 < ntiles) {
+        if (tid == 0 && tile + kCBuf < ntiles) {
             fence_proxy_async_smem();
-            issue(tile + 2, buf);
+            issue(tile + kCBuf, buf);
         }
     }
     (void)failed;
@@ -280,7 +289,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
 }
 
 size_t attn_cluster_smem(int G, int hd) {
-    return 128 + (size_t)4 * kCTK * hd * 2 +
+    return 128 + (size_t)2 * kCBuf * kCTK * hd * 2 +
            sizeof(float) * ((size_t)G * hd + G * kCTK + 3 * G + 2 * G * hd + 2 * hd);
 }
 
