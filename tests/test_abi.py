@@ -57,6 +57,19 @@ def test_argument_errors_without_gpu(lib):
     assert lib.ovf_model_create(0, None, None, 0, None) == _lib.OVF_EINVAL
     assert lib.ovf_session_decode(None, 0, None, None) == _lib.OVF_EINVAL
     assert lib.ovf_attention_scratch_bytes(32, 8, 128) > 0
+    # ComputeSingleHead on F32 caches: null buffers, seq_len outside [1, max_ctx]
+    assert lib.ovf_attention_single_head(None, None, None, None, 32, 8, 128, 64, 8, 1.0, None) == _lib.OVF_EINVAL
+    p16 = C.c_void_p(16)
+    assert lib.ovf_attention_single_head(p16, p16, p16, p16, 32, 8, 128, 64, 65, 1.0, None) == _lib.OVF_EINVAL
+    assert lib.ovf_attention_single_head(p16, p16, p16, p16, 32, 8, 128, 64, 0, 1.0, None) == _lib.OVF_EINVAL
+    # unsupported head_dim / heads not a multiple of the KV heads
+    assert lib.ovf_attention_single_head(p16, p16, p16, p16, 32, 8, 96, 64, 8, 1.0, None) == _lib.OVF_EINVAL
+    assert lib.ovf_attention_single_head(p16, p16, p16, p16, 30, 8, 128, 64, 8, 1.0, None) == _lib.OVF_EINVAL
+    # sessions: null model / unknown KV dtype
+    out = C.c_void_p()
+    assert lib.ovf_session_create_kv(None, 64, 0, C.byref(out)) == _lib.OVF_EINVAL
+    # RMSNorm and the projections reject null buffers on the host
+    assert lib.ovf_q4k_project_gate_up(None, None, None, 4, 256, None, None, None, None, None, None) == _lib.OVF_EINVAL
 
 
 def test_python_mirror_raises_value_error():
