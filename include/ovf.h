@@ -149,6 +149,14 @@ int64_t ovf_attention_scratch_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t
 ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const float *v_cache, float *out,
                                      int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
                                      int32_t seq_len, float scale, void *stream);
+/* Runtime/CachedAttentionKernel.cs:139 ComputeSingleHeadQ8 for every query
+ * head over a Q8 cache (Q8KvQuant per-vector int8 [n_kv_heads x max_ctx x hd]
+ * + fp32 scales [n_kv_heads x max_ctx]), positions [0, seq_len): the
+ * reference's operation order. */
+ovf_status ovf_attention_single_head_q8(const float *q, const int8_t *k_cache, const float *k_scales,
+                                        const int8_t *v_cache, const float *v_scales, float *out, int32_t n_heads,
+                                        int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx, int32_t seq_len,
+                                        float scale, void *stream);
 ovf_status ovf_attention_decode(const float *q, const void *k_cache, const void *v_cache, float *out,
                                 int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                 int32_t max_ctx, int32_t seq_len, float scale, void *scratch,
@@ -210,10 +218,13 @@ int64_t ovf_model_weight_bytes(const ovf_model *m);
 
 /* KV-cache element types (Runtime/KvCacheDType.cs:15).  OVF_KV_F32 is the
  * reference's default: attention then runs in the reference's exact
- * operation order (CachedAttentionKernel.ComputeSingleHead).  OVF_KV_F16 has
+ * operation order (CachedAttentionKernel.ComputeSingleHead).  OVF_KV_Q8 is
+ * the reference's Q8 cache (per-vector int8 + fp32 scale, Q8KvQuant), attended
+ * in ComputeSingleHeadQ8's exact order.  OVF_KV_F16 has
  * no reference counterpart: half the KV traffic, flash-decode attention with
  * a log-sum-exp merge, results within tolerance of the F32 path only. */
 #define OVF_KV_F32 0
+#define OVF_KV_Q8 1
 #define OVF_KV_F16 2
 
 /* ISlmInferenceEngine.CreateSession (Contracts/ISlmInferenceEngine.cs:9):

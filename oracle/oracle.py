@@ -84,6 +84,9 @@ def _declare(L):
         "orc_session_destroy": (None, [P]),
         "orc_session_reset": (None, [P]),
         "orc_session_set_kv_fp16": (None, [P, C.c_int]),
+        "orc_session_set_kv_q8": (None, [P, C.c_int]),
+        "orc_q8kv_quantize": (C.c_float, [P, C.c_int, P]),
+        "orc_attention_single_head_q8": (None, [P, P, P, P, P, P, P, C.c_int, C.c_int, C.c_float]),
         "orc_set_exp_double_rounded": (None, [C.c_int]),
         "orc_session_position": (C.c_int, [P]),
         "orc_session_decode": (C.c_int, [P, C.c_int, P]),
@@ -389,6 +392,11 @@ class OracleSession:
     def reset(self):
         lib().orc_session_reset(self._s)
 
+    def set_kv_q8(self, on: bool = True):
+        """KvCacheDType.Q8: per-vector int8 K/V + one scale each (set before
+        the first token)."""
+        lib().orc_session_set_kv_q8(self._s, int(on))
+
     def set_kv_fp16(self, on: bool = True):
         """Round cached K/V to fp16 as the GPU cache does (test switch)."""
         lib().orc_session_set_kv_fp16(self._s, int(on))
@@ -414,4 +422,27 @@ def set_exp_double_rounded(on: bool = True):
     rounded once (the GPU's), instead of the C library's expf (the
     reference's MathF.Exp).  Isolates exp rounding from everything else."""
     lib().orc_set_exp_double_rounded(int(on))
+
+
+def q8kv_quantize(v: np.ndarray):
+    """Q8KvQuant.Quantize: one vector -> (int8 values, scale)."""
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    q = np.empty(v.size, np.int8)
+    sc = lib().orc_q8kv_quantize(_p(v), v.size, _p(q))
+    return q, np.float32(sc)
+
+
+def attention_single_head_q8(q, kq, ks, vq, vs, scale) -> np.ndarray:
+    """CachedAttentionKernel.ComputeSingleHeadQ8 over seq = len(ks) positions."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kq = np.ascontiguousarray(kq, dtype=np.int8)
+    vq = np.ascontiguousarray(vq, dtype=np.int8)
+    ks = np.ascontiguousarray(ks, dtype=np.float32)
+    vs = np.ascontiguousarray(vs, dtype=np.float32)
+    hd, seq = q.size, ks.size
+    out = np.empty(hd, np.float32)
+    scr = np.empty(max(seq, 1), np.float32)
+    lib().orc_attention_single_head_q8(_p(q), _p(kq), _p(ks), _p(vq), _p(vs), _p(out), _p(scr), seq, hd,
+                                       float(scale))
+    return out
 

@@ -640,6 +640,82 @@ void orc_attention_single_head(const float *q, const float *keys, const float *v
     }
 }
 
+/* Runtime/Q8KvQuant.cs:25-77 (Quantize): one K or V vector -> int8 + scale,
+ * scale = maxAbs/127, values round-half-even(x * (127/maxAbs)) clamped to
+ * +-127; a zero vector gives scale 0 and zero bytes. */
+float orc_q8kv_quantize(const float *src, int n, int8_t *dst) {
+    float maxAbs = 0.0f;
+    for (int i = 0; i < n; i++) {
+        float a = fabsf(src[i]);
+        if (a > maxAbs) maxAbs = a;
+    }
+    if (!(maxAbs > 0.0f)) {
+        for (int i = 0; i < n; i++) dst[i] = 0;
+        return 0.0f;
+    }
+    float scale = maxAbs / 127.0f;
+    float inv = 127.0f / maxAbs;
+    for (int d = 0; d < n; d++) {
+        float q = nearbyintf(src[d] * inv);
+        if (q > 127.0f) q = 127.0f;
+        else if (q < -127.0f) q = -127.0f;
+        dst[d] = (int8_t)q;
+    }
+    return scale;
+}
+
+/* Runtime/CachedAttentionKernel.cs:200-235 (DotF32I8): the two-accumulator
+ * dot of attn_dot with the int8 key widened to float. */
+static float attn_dot_i8(const float *l, const int8_t *r, int n) {
+    if (n >= 8) {
+        float a0[8] = {0}, a1[8] = {0};
+        int i = 0;
+        for (; i + 16 <= n; i += 16)
+            for (int j = 0; j < 8; j++) {
+                a0[j] = a0[j] + l[i + j] * (float)r[i + j];
+                a1[j] = a1[j] + l[i + 8 + j] * (float)r[i + 8 + j];
+            }
+        for (; i + 8 <= n; i += 8)
+            for (int j = 0; j < 8; j++) a0[j] = a0[j] + l[i + j] * (float)r[i + j];
+        float v[8];
+        for (int j = 0; j < 8; j++) v[j] = a0[j] + a1[j];
+        float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        for (; i < n; i++) sum += l[i] * (float)r[i];
+        return sum;
+    }
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s += l[i] * (float)r[i];
+    return s;
+}
+
+/* Runtime/CachedAttentionKernel.cs:139-200 (ComputeSingleHeadQ8): score =
+ * DotF32I8(q, kQ[t]) * keyScale[t] * scale; max-subtracted exp; sumExp in
+ * order; out[d] += (p_t * invSum * valueScale[t]) * vQ[t][d] in order. */
+void orc_attention_single_head_q8(const float *q, const int8_t *kq, const float *ks, const int8_t *vq,
+                                  const float *vs, float *out, float *scratch, int seq_len, int hd, float scale) {
+    for (int d = 0; d < hd; d++) out[d] = 0.0f;
+    if (seq_len == 0) return;
+    float maxScore = -INFINITY;
+    for (int t = 0; t < seq_len; t++) {
+        float sc = attn_dot_i8(q, kq + (int64_t)t * hd, hd) * ks[t] * scale;
+        scratch[t] = sc;
+        if (sc > maxScore) maxScore = sc;
+    }
+    float sumExp = 0.0f;
+    for (int t = 0; t < seq_len; t++) {
+        float e = orc_expf(scratch[t] - maxScore);
+        scratch[t] = e;
+        sumExp += e;
+    }
+    if (sumExp <= 0.0f || isnan(sumExp) || isinf(sumExp)) return;
+    float invSum = 1.0f / sumExp;
+    for (int t = 0; t < seq_len; t++) {
+        float coef = scratch[t] * invSum * vs[t];
+        const int8_t *v = vq + (int64_t)t * hd;
+        for (int d = 0; d < hd; d++) out[d] = out[d] + coef * (float)v[d];
+    }
+}
+
 /* Runtime/CachedFeedForwardBlock.cs:464-472 (ApplySiLU): sigmoid then
  * multiply; TensorPrimitives.Sigmoid is 1/(1+e^-x) to a few ULP. */
 void orc_silu_inplace(float *v, int64_t n) {
@@ -736,6 +812,9 @@ struct orc_session {
     int max_ctx, pos;
     int kv_fp16;                  /* test switch: round cached K/V to fp16 like the GPU cache */
     float *kcache, *vcache;       /* F32 [layer][kvh][max_ctx][hd] (KeyValueCache.cs:593-602) */
+    int kv_q8;                    /* KvCacheDType.Q8: int8 vectors + one scale each */
+    int8_t *kq8, *vq8;            /* [layer][kvh][max_ctx][hd] */
+    float *ks8, *vs8;             /* [layer][kvh][max_ctx] */
     float *rope_cos, *rope_sin;   /* [max_ctx][hd/2] */
     float *hidden, *after, *ln, *attn_out, *ffo, *fin;
     float *head_out;              /* [n_heads][d_model] per-head Wo outputs */
@@ -779,6 +858,7 @@ orc_session *orc_session_create(const orc_model *m, int max_ctx) {
 void orc_session_destroy(orc_session *s) {
     if (!s) return;
     free(s->kcache); free(s->vcache); free(s->rope_cos); free(s->rope_sin);
+    free(s->kq8); free(s->vq8); free(s->ks8); free(s->vs8);
     free(s->hidden); free(s->after); free(s->ln); free(s->attn_out); free(s->ffo); free(s->fin);
     free(s->head_out); free(s->gate); free(s->up); free(s->eo); free(s->moe_acc);
     free(s->q8); free(s->q8s); free(s->q8b);
@@ -786,6 +866,19 @@ void orc_session_destroy(orc_session *s) {
 }
 void orc_session_reset(orc_session *s) { s->pos = 0; }
 void orc_session_set_kv_fp16(orc_session *s, int on) { s->kv_fp16 = on; }
+/* CreateSession(kvCacheDType: Q8) (CachedLlamaInferenceEngine.cs:360): set
+ * before the first token. */
+void orc_session_set_kv_q8(orc_session *s, int on) {
+    s->kv_q8 = on;
+    if (on && !s->kq8) {
+        const orc_model *m = s->m;
+        int64_t vec = (int64_t)m->n_layers * m->n_kv_heads * s->max_ctx;
+        s->kq8 = (int8_t *)calloc((size_t)(vec * m->head_dim), 1);
+        s->vq8 = (int8_t *)calloc((size_t)(vec * m->head_dim), 1);
+        s->ks8 = (float *)calloc((size_t)vec, sizeof(float));
+        s->vs8 = (float *)calloc((size_t)vec, sizeof(float));
+    }
+}
 int orc_session_position(const orc_session *s) { return s->pos; }
 
 static int is_kq(int t) { return t == ORC_Q4_K || t == ORC_Q6_K; }
@@ -874,8 +967,14 @@ static void attention_block(orc_session *s, const orc_layer *L, int layer, int p
                 kb[i] = (float)(_Float16)kb[i];
                 vb[i] = (float)(_Float16)vb[i];
             }
-        memcpy(s->kcache + off, kb, (size_t)hd * sizeof(float));
-        memcpy(s->vcache + off, vb, (size_t)hd * sizeof(float));
+        if (s->kv_q8) {
+            int64_t vi = ((int64_t)layer * KVH + g) * s->max_ctx + pos;
+            s->ks8[vi] = orc_q8kv_quantize(kb, hd, s->kq8 + off);
+            s->vs8[vi] = orc_q8kv_quantize(vb, hd, s->vq8 + off);
+        } else {
+            memcpy(s->kcache + off, kb, (size_t)hd * sizeof(float));
+            memcpy(s->vcache + off, vb, (size_t)hd * sizeof(float));
+        }
     }
     free(kb);
     free(vb);
@@ -898,7 +997,13 @@ static void attention_block(orc_session *s, const orc_layer *L, int layer, int p
                          shared ? hq : NULL, hs, hb, lq, ls, lb);
             orc_rope_apply(qv, hd, cp, sp, m->rope_split_half);
             int64_t base = (((int64_t)layer * KVH + g) * s->max_ctx) * hd;
-            orc_attention_single_head(qv, s->kcache + base, s->vcache + base, att, scr, seq, hd, scale);
+            if (s->kv_q8) {
+                int64_t vb0 = ((int64_t)layer * KVH + g) * s->max_ctx;
+                orc_attention_single_head_q8(qv, s->kq8 + base, s->ks8 + vb0, s->vq8 + base, s->vs8 + vb0, att, scr,
+                                             seq, hd, scale);
+            } else {
+                orc_attention_single_head(qv, s->kcache + base, s->vcache + base, att, scr, seq, hd, scale);
+            }
             /* Wo_h: Q8_0 per head [D x hd] (GgufLlamaLoader.cs:977-995,1298-1336):
              * quantize att to Q8_0 and contract row o's slice for head h. */
             float *ho = s->head_out + (int64_t)h * D;

@@ -122,6 +122,10 @@ void orc_session_reset(orc_session *s);
 /* Test switch: store K/V rounded to fp16 (the GPU's cache format); the
  * reference's cache is F32 (Runtime/KeyValueCache.cs:593-602). */
 void orc_session_set_kv_fp16(orc_session *s, int on);
+void orc_session_set_kv_q8(orc_session *s, int on);
+float orc_q8kv_quantize(const float *src, int n, int8_t *dst);
+void orc_attention_single_head_q8(const float *q, const int8_t *kq, const float *ks, const int8_t *vq,
+                                  const float *vs, float *out, float *scratch, int seq_len, int hd, float scale);
 /* Test switch: exp rounded once from double precision (as on the GPU). */
 void orc_set_exp_double_rounded(int on);
 int  orc_session_position(const orc_session *s);

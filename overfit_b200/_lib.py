@@ -72,6 +72,7 @@ SIGNATURES = {
     "ovf_attention_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P, P, P]),
     "ovf_attention_decode_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_attention_single_head": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
+    "ovf_attention_single_head_q8": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_model_create": (I32, [I32, P, P, I32, P]),
     "ovf_model_destroy": (I32, [P]),
     "ovf_model_weight_bytes": (I64, [P]),

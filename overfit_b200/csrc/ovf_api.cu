@@ -292,4 +292,27 @@ ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const
     return launch_attention_exact(p, seq_len, S(stream), false);
 }
 
+ovf_status ovf_attention_single_head_q8(const float *q, const int8_t *k_cache, const float *k_scales,
+                                        const int8_t *v_cache, const float *v_scales, float *out, int32_t n_heads,
+                                        int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx, int32_t seq_len,
+                                        float scale, void *stream) {
+    OVF_CHECK_ARG(q && k_cache && k_scales && v_cache && v_scales && out, "ComputeSingleHeadQ8: null buffer");
+    OVF_CHECK_ARG(seq_len >= 1 && seq_len <= max_ctx, "ComputeSingleHeadQ8: seq_len must be in [1, max_ctx]");
+    OVF_CHECK_ARG(head_dim % 32 == 0, "ComputeSingleHeadQ8: head_dim must be a multiple of 32");
+    AttnParams p{};
+    p.q = q;
+    p.kc = (__half *)k_cache;
+    p.vc = (__half *)v_cache;
+    p.ks = const_cast<float *>(k_scales);
+    p.vs = const_cast<float *>(v_scales);
+    p.out = out;
+    p.H = n_heads;
+    p.KVH = n_kv_heads;
+    p.hd = head_dim;
+    p.max_ctx = max_ctx;
+    p.seq_len_host = seq_len;
+    p.scale = scale;
+    return launch_attention_exact(p, seq_len, S(stream), false, true);
+}
+
 }  // extern "C"

@@ -31,7 +31,7 @@ static constexpr int kCBuf = 2;    // tiles in flight
 template <int GT, int HD>
 __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnParams p) {
     extern __shared__ __align__(128) uint8_t csm[];
-    constexpr int G = GT, hd = HD, HQ = HD / 4;
+    constexpr int G = GT, hd = HD;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();

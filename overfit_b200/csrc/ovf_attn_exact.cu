@@ -42,13 +42,14 @@ struct VStage {
     static constexpr int bufs = HD <= 128 ? kVBufs : kVBufs / 2;
 };
 
-// shared memory: q, k_new, v_new [hd each] | 16 scalars | value blocks
+// shared memory: q, k_new, v_new [hd each] | 16 scalars | quantized new
+// K/V row (Q8 cache, 2 x hd bytes) | value blocks
 // [kVBufs][kVBlock][hd/CL] | own score slice [chunk] | all probabilities [seq]
 int64_t attn_exact_smem_bytes(int hd, int seq_len) {
     const int chunk = (seq_len + kExactCluster - 1) / kExactCluster;
     const int dpc = hd / kExactCluster;
     const int bufs = hd <= 128 ? kVBufs : kVBufs / 2;
-    return (int64_t)(3 * hd + 16 + bufs * kVRow * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
+    return (int64_t)(3 * hd + 16 + hd / 2 + bufs * kVRow * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
 }
 
 __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
@@ -63,7 +64,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 int attn_exact_max_seq(int) { return kExactMaxSeq; }
 
-template <int HD>
+// Q8 = true: the reference's Q8 KV cache (KvCacheDType.Q8, per-vector int8
+// + one fp32 scale, Runtime/Q8KvQuant.cs) attended in ComputeSingleHeadQ8's
+// order (Runtime/CachedAttentionKernel.cs:139-235): score = DotF32I8(q, kQ)
+// * keyScale * scale, out[d] += (p * invSum * valueScale) * vQ[d].
+template <int HD, bool Q8>
 __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactThreads)
     attention_exact_kernel(const AttnParams p) {
     extern __shared__ __align__(16) float esm[];
@@ -74,11 +79,17 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int DPC = HD / kExactCluster;
     float *qs = esm, *kn = esm + HD, *vn = esm + 2 * HD, *red = esm + 3 * HD;
-    float *vbuf = esm + 3 * HD + 16;                    // [kVBufs][kVBlock][DPC]
+    int8_t *kq8n = reinterpret_cast<int8_t *>(esm + 3 * HD + 16), *vq8n = kq8n + HD;  // Q8: the new row
+    float *vbuf = esm + 3 * HD + 16 + HD / 2;           // [kVBufs][kVBlock][DPC]
     constexpr int NBUF = VStage<HD>::bufs;
     float *ex = vbuf + NBUF * kVRow * DPC;              // own slice of scores / exponentials
     const float *kf = reinterpret_cast<const float *>(p.kc) + (size_t)g * p.max_ctx * HD;
     const float *vf = reinterpret_cast<const float *>(p.vc) + (size_t)g * p.max_ctx * HD;
+    const int8_t *k8 = reinterpret_cast<const int8_t *>(p.kc) + (size_t)g * p.max_ctx * HD;
+    const int8_t *v8 = reinterpret_cast<const int8_t *>(p.vc) + (size_t)g * p.max_ctx * HD;
+    const float *ksc = Q8 ? p.ks + (size_t)g * p.max_ctx : nullptr;
+    const float *vsc = Q8 ? p.vs + (size_t)g * p.max_ctx : nullptr;
+    constexpr int EB = Q8 ? 1 : 4;  // bytes per cached element
 
     // the next projections' weights do not depend on this kernel: pull them
     // into L2 while the (latency-bound) attention runs
@@ -95,10 +106,10 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         const int a = min(sp, rank * ch), b = min(sp, a + ch);
         L2Prefetch kv{};
         if (b > a) {
-            kv.ptr[0] = kf + (size_t)a * HD;
-            kv.bytes[0] = (int64_t)(b - a) * HD * 4;
-            kv.ptr[1] = vf + (size_t)a * HD;
-            kv.bytes[1] = (int64_t)(b - a) * HD * 4;
+            kv.ptr[0] = reinterpret_cast<const char *>(p.kc) + ((size_t)g * p.max_ctx + a) * HD * EB;
+            kv.bytes[0] = (int64_t)(b - a) * HD * EB;
+            kv.ptr[1] = reinterpret_cast<const char *>(p.vc) + ((size_t)g * p.max_ctx + a) * HD * EB;
+            kv.bytes[1] = (int64_t)(b - a) * HD * EB;
             kv.n = 2;
             prefetch_l2_slice(kv, 0, 1);
         }
@@ -117,15 +128,27 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     // block b is stored transposed, [DPC][kVRow]: dimension d's values of
     // the block are contiguous for its chain thread (4-byte copies; the
     // global reads stay coalesced along d)
+    // (Q8: raw int8 rows [kVBlock][DPC], 4-byte pieces)
     constexpr int NE = kVBlock * DPC / kExactThreads;
+    constexpr int NE8 = (kVBlock * DPC / 4 + kExactThreads - 1) / kExactThreads;
     auto stage_values = [&](int blk) {
         if (blk < nblk) {
             float *dst = vbuf + (blk % NBUF) * kVRow * DPC;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+            if (Q8) {
+                int8_t *d8 = reinterpret_cast<int8_t *>(dst);
 #pragma unroll
-            for (int j = 0; j < NE; ++j) {
-                const int i = tid + j * kExactThreads, t = i / DPC, dd = i % DPC;
-                if (t < n) cp_async4(dst + dd * kVRow + t, vf + (size_t)(tb + t) * HD + d0 + dd);
+                for (int j = 0; j < NE8; ++j) {
+                    const int i = tid + j * kExactThreads, t = i / (DPC / 4), q4 = i % (DPC / 4);
+                    if (i < kVBlock * DPC / 4 && t < n)
+                        cp_async4(d8 + t * DPC + 4 * q4, v8 + (size_t)(tb + t) * HD + d0 + 4 * q4);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < NE; ++j) {
+                    const int i = tid + j * kExactThreads, t = i / DPC, dd = i % DPC;
+                    if (t < n) cp_async4(dst + dd * kVRow + t, vf + (size_t)(tb + t) * HD + d0 + dd);
+                }
             }
         }
         cp_async_commit();
@@ -147,12 +170,53 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         if (has_new) rope_rotate(kn, HD, c, s, p.split_half, tid, kExactThreads);
         __syncthreads();
     }
-    if (has_new && h % G == 0 && rank == 0) {
-        float *kw = reinterpret_cast<float *>(p.kc) + ((size_t)g * p.max_ctx + pos) * HD;
-        float *vw = reinterpret_cast<float *>(p.vc) + ((size_t)g * p.max_ctx + pos) * HD;
+    if (Q8 && has_new) {
+        // Q8KvQuant.Quantize of the rotated key and the value (every CTA
+        // computes the same bytes; the current token is attended from them)
+        if (warp == 0) {
+            float mk = 0.0f, mv = 0.0f;
+            for (int i = lane; i < HD; i += 32) {
+                mk = fmaxf(mk, fabsf(kn[i]));
+                mv = fmaxf(mv, fabsf(vn[i]));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mk = fmaxf(mk, __shfl_xor_sync(0xFFFFFFFFu, mk, o));
+                mv = fmaxf(mv, __shfl_xor_sync(0xFFFFFFFFu, mv, o));
+            }
+            if (lane == 0) {
+                red[10] = mk > 0.0f ? fdiv(mk, 127.0f) : 0.0f;
+                red[11] = mv > 0.0f ? fdiv(mv, 127.0f) : 0.0f;
+                red[12] = mk > 0.0f ? fdiv(127.0f, mk) : 0.0f;
+                red[13] = mv > 0.0f ? fdiv(127.0f, mv) : 0.0f;
+            }
+        }
+        __syncthreads();
         for (int i = tid; i < HD; i += kExactThreads) {
-            kw[i] = kn[i];
-            vw[i] = vn[i];
+            kq8n[i] = (int8_t)quant_elem(kn[i], red[12]);
+            vq8n[i] = (int8_t)quant_elem(vn[i], red[13]);
+        }
+        __syncthreads();
+    }
+    if (has_new && h % G == 0 && rank == 0) {
+        if (Q8) {
+            int8_t *kw = reinterpret_cast<int8_t *>(p.kc) + ((size_t)g * p.max_ctx + pos) * HD;
+            int8_t *vw = reinterpret_cast<int8_t *>(p.vc) + ((size_t)g * p.max_ctx + pos) * HD;
+            for (int i = tid; i < HD; i += kExactThreads) {
+                kw[i] = kq8n[i];
+                vw[i] = vq8n[i];
+            }
+            if (tid == 0) {
+                p.ks[(size_t)g * p.max_ctx + pos] = red[10];
+                p.vs[(size_t)g * p.max_ctx + pos] = red[11];
+            }
+        } else {
+            float *kw = reinterpret_cast<float *>(p.kc) + ((size_t)g * p.max_ctx + pos) * HD;
+            float *vw = reinterpret_cast<float *>(p.vc) + ((size_t)g * p.max_ctx + pos) * HD;
+            for (int i = tid; i < HD; i += kExactThreads) {
+                kw[i] = kn[i];
+                vw[i] = vn[i];
+            }
         }
     }
     pdl_launch_dependents();
@@ -171,9 +235,15 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         for (int u = 0; u < U; ++u) {
             const int t = tb + u * KPI + 2 * warp + hw;
             const bool ok = t < t1;
-            const float *kr = (has_new && t == pos) ? kn : kf + (size_t)(ok ? t : t0) * HD;
+            if (Q8) {
+                const int8_t *kr = (has_new && t == pos) ? kq8n : k8 + (size_t)(ok ? t : t0) * HD;
 #pragma unroll
-            for (int i = 0; i < HD / 16; ++i) kv[u][i] = kr[16 * i + c];
+                for (int i = 0; i < HD / 16; ++i) kv[u][i] = (float)kr[16 * i + c];
+            } else {
+                const float *kr = (has_new && t == pos) ? kn : kf + (size_t)(ok ? t : t0) * HD;
+#pragma unroll
+                for (int i = 0; i < HD / 16; ++i) kv[u][i] = kr[16 * i + c];
+            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -186,7 +256,13 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
             v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
-            const float sc = fmul(v, p.scale);
+            float sc;
+            if (Q8) {
+                const float kscale = (has_new && t == pos) ? red[10] : (t < t1 ? ksc[t] : 0.0f);
+                sc = fmul(fmul(v, kscale), p.scale);
+            } else {
+                sc = fmul(v, p.scale);
+            }
             if (c == 0 && t < t1) {
                 ex[t - t0] = sc;
                 lmax = sc > lmax ? sc : lmax;
@@ -271,13 +347,37 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     //    staged block by block in shared memory by all threads while the
     //    DPC chain threads consume the previous block
     // p_t = e_t * invSum once, by all threads (the reference's probability)
+    // (Q8: coef_t = p_t * invSum * valueScale_t, the reference's AxpyI8 factor)
     if (!bad)
-        for (int t = tid; t < seq; t += kExactThreads) eall[t] = fmul(eall[t], invSum);
+        for (int t = tid; t < seq; t += kExactThreads) {
+            float pr = fmul(eall[t], invSum);
+            if (Q8) pr = fmul(pr, (has_new && t == pos) ? red[11] : vsc[t]);
+            eall[t] = pr;
+        }
     float acc = 0.0f;
     for (int blk = 0; blk < nblk; ++blk) {
         cp_async_wait<NBUF - 1>();  // block blk has landed (this thread's part)
         __syncthreads();
-        if (tid < DPC && !bad) {
+        if (Q8 && tid < DPC && !bad) {
+            int8_t *vb8 = reinterpret_cast<int8_t *>(vbuf + (blk % NBUF) * kVRow * DPC) + tid;
+            const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+            if (has_new && pos >= tb && pos < tb + n) vb8[(pos - tb) * DPC] = vq8n[d0 + tid];
+            const float *pb = eall + tb;
+            int i = 0;
+#pragma unroll 1
+            for (; i + 16 <= n; i += 16) {
+                float pv[16], vv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    pv[j] = pb[i + j];
+                    vv[j] = (float)vb8[(i + j) * DPC];
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc = fadd(acc, fmul(pv[j], vv[j]));
+            }
+            for (; i < n; ++i) acc = fadd(acc, fmul(pb[i], (float)vb8[i * DPC]));
+        }
+        if (!Q8 && tid < DPC && !bad) {
             float *vb = vbuf + (blk % NBUF) * kVRow * DPC + tid * kVRow;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
             // the current token's value was not in the cache when staged
@@ -314,9 +414,10 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
 
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }
 
-ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl) {
+ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8) {
     OVF_CHECK_ARG(attn_exact_supported(p.hd), "attention: head_dim %d unsupported (32, 64, 128 or 256)", p.hd);
     OVF_CHECK_ARG(p.H > 0 && p.KVH > 0 && p.H % p.KVH == 0, "attention: n_heads must be a multiple of n_kv_heads");
+    OVF_CHECK_ARG(!q8 || (p.ks && p.vs), "attention: Q8 cache without its scales");
     OVF_CHECK_ARG(seq_len_max >= 1 && seq_len_max <= attn_exact_max_seq(p.hd),
                   "attention: sequence length %d outside [1, %d]", seq_len_max, attn_exact_max_seq(p.hd));
     const size_t smem = (size_t)attn_exact_smem_bytes(p.hd, seq_len_max);
@@ -331,21 +432,21 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaSuccess;
-#define OVF_EXACT(HDV)                                                                                      \
-    do {                                                                                                    \
-        static bool attr_set = false;                                                                       \
-        if (!attr_set && smem > 48 * 1024) {                                                                \
-            e = cudaFuncSetAttribute(attention_exact_kernel<HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                     (int)attn_exact_smem_bytes(HDV, attn_exact_max_seq(HDV)));             \
-            attr_set = e == cudaSuccess;                                                                    \
-        }                                                                                                   \
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, attention_exact_kernel<HDV>, p);                 \
+#define OVF_EXACT(HDV, Q)                                                                                      \
+    do {                                                                                                       \
+        static bool attr_set = false;                                                                          \
+        if (!attr_set && smem > 48 * 1024) {                                                                   \
+            e = cudaFuncSetAttribute(attention_exact_kernel<HDV, Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                     (int)attn_exact_smem_bytes(HDV, attn_exact_max_seq(HDV)));                \
+            attr_set = e == cudaSuccess;                                                                       \
+        }                                                                                                      \
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, attention_exact_kernel<HDV, Q>, p);                 \
     } while (0)
     switch (p.hd) {
-        case 32: OVF_EXACT(32); break;
-        case 64: OVF_EXACT(64); break;
-        case 128: OVF_EXACT(128); break;
-        default: OVF_EXACT(256); break;
+        case 32: if (q8) OVF_EXACT(32, true); else OVF_EXACT(32, false); break;
+        case 64: if (q8) OVF_EXACT(64, true); else OVF_EXACT(64, false); break;
+        case 128: if (q8) OVF_EXACT(128, true); else OVF_EXACT(128, false); break;
+        default: if (q8) OVF_EXACT(256, true); else OVF_EXACT(256, false); break;
     }
 #undef OVF_EXACT
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "attention_exact_kernel launch");

@@ -57,7 +57,8 @@ struct AttnParams {
     const float *k_new;       // [KVH*hd] key of the current token (raw), or null
     const float *v_new;       // [KVH*hd] value of the current token, or null
     __half *kc, *vc;          // this layer's cache [KVH][max_ctx][hd] (fp16 kernels; the
-                              // exact kernel reads these pointers as fp32)
+                              // exact kernel reads these pointers as fp32 or int8)
+    float *ks, *vs;           // Q8 cache: per-vector scales [KVH][max_ctx]
     float *out;               // [H*hd]
     const float *rope_cos;    // [max_ctx][hd/2] or null
     const float *rope_sin;
@@ -79,7 +80,7 @@ ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool p
 // ovf_attn_exact.cu: F32 cache, the reference's operation order (bit-exact).
 bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);
-ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl);
+ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8 = false);
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,

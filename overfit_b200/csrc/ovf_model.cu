@@ -60,7 +60,8 @@ struct ovf_session {
     int n_logits = 0;      // host mirror of DevStep::n_generated
     cudaStream_t stream = nullptr;
     int kv_dtype = OVF_KV_F32;
-    void *kc = nullptr, *vc = nullptr;  // [layers][KVH][max_ctx][hd], fp32 or fp16
+    void *kc = nullptr, *vc = nullptr;  // [layers][KVH][max_ctx][hd], fp32, int8 or fp16
+    float *ks = nullptr, *vs = nullptr;  // Q8 cache: scales [layers][KVH][max_ctx]
     float *hidden = nullptr, *after = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *h = nullptr,
           *gtmp = nullptr, *utmp = nullptr, *logits = nullptr, *rope_cos = nullptr, *rope_sin = nullptr,
           *partial = nullptr;
@@ -361,9 +362,13 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         a.q = s->q;
         a.k_new = s->k;
         a.v_new = s->v;
-        const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : 2;
+        const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
         a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
         a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
+        if (s->kv_dtype == OVF_KV_Q8) {
+            a.ks = s->ks + (size_t)l * KVH * s->max_ctx;
+            a.vs = s->vs + (size_t)l * KVH * s->max_ctx;
+        }
         a.out = s->attn;
         a.rope_cos = s->rope_cos;
         a.rope_sin = s->rope_sin;
@@ -383,8 +388,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         }
         a.trace = tslot("attn");
         a.no_kv_prefetch = env_flag("OVF_ATTN_NOPF") ? 1 : 0;
-        if (s->kv_dtype == OVF_KV_F32) {
-            if ((r = launch_attention_exact(a, s->max_ctx, st, true))) return r;
+        if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
+            if ((r = launch_attention_exact(a, s->max_ctx, st, true, s->kv_dtype == OVF_KV_Q8))) return r;
         } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
             if ((r = launch_attention_cluster(a, st, true))) return r;
         } else if ((r = launch_attention(a, st, true))) {
@@ -656,9 +661,9 @@ ovf_status ovf_session_create(ovf_model *m, int32_t max_ctx, ovf_session **out) 
 ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype, ovf_session **out) {
     OVF_CHECK_ARG(m && out, "ovf_session_create: null argument");
     OVF_CHECK_ARG(max_ctx > 0 && max_ctx <= (1 << 20), "ovf_session_create: bad max_ctx");
-    OVF_CHECK_ARG(kv_dtype == OVF_KV_F32 || kv_dtype == OVF_KV_F16, "ovf_session_create: unknown KV dtype %d",
-                  kv_dtype);
-    if (kv_dtype == OVF_KV_F32) {
+    OVF_CHECK_ARG(kv_dtype == OVF_KV_F32 || kv_dtype == OVF_KV_Q8 || kv_dtype == OVF_KV_F16,
+                  "ovf_session_create: unknown KV dtype %d", kv_dtype);
+    if (kv_dtype != OVF_KV_F16) {
         OVF_CHECK_ARG(attn_exact_supported(m->cfg.head_dim), "ovf_session_create: head_dim %d unsupported",
                       m->cfg.head_dim);
         OVF_CHECK_ARG(max_ctx <= attn_exact_max_seq(m->cfg.head_dim), "ovf_session_create: max_ctx too large");
@@ -675,9 +680,13 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     auto A = [&](void **p, size_t bytes) {
         if (!st) st = dalloc(s->allocs, p, bytes);
     };
-    const size_t esz = kv_dtype == OVF_KV_F32 ? 4 : 2;
+    const size_t esz = kv_dtype == OVF_KV_F32 ? 4 : kv_dtype == OVF_KV_Q8 ? 1 : 2;
     A((void **)&s->kc, kv * esz);
     A((void **)&s->vc, kv * esz);
+    if (kv_dtype == OVF_KV_Q8) {
+        A((void **)&s->ks, kv / c.head_dim * 4);
+        A((void **)&s->vs, kv / c.head_dim * 4);
+    }
     A((void **)&s->hidden, D * 4);
     A((void **)&s->after, D * 4);
     A((void **)&s->q, QD * 4);

@@ -101,7 +101,8 @@ class CudaLlamaInferenceEngine:
 
     def create_session(self, max_context: int, kv_cache_dtype: str = "f32") -> "CudaLlamaSession":
         """CreateSession(maxContextLength, kvCacheDType): "f32" (the reference's
-        default, bit-exact attention) or "f16" (no reference counterpart)."""
+        default, bit-exact attention), "q8" (the reference's Q8 cache, its
+        exact ComputeSingleHeadQ8 order) or "f16" (no reference counterpart)."""
         return CudaLlamaSession(self, max_context, kv_cache_dtype)
 
     def close(self):
@@ -120,7 +121,7 @@ class CudaLlamaSession:
     """ISlmSession over the device-resident decode loop (greedy sampling on
     the device; logits are copied out only when asked for)."""
 
-    KV_DTYPES = {"f32": 0, "f16": 2}
+    KV_DTYPES = {"f32": 0, "q8": 1, "f16": 2}
 
     def __init__(self, engine: CudaLlamaInferenceEngine, max_context: int, kv_cache_dtype: str = "f32"):
         self.engine = engine

@@ -345,6 +345,18 @@ class CachedAttentionKernel:
                                                     _stream()), "ComputeSingleHead")
 
     @staticmethod
+    def compute_single_head_q8_all(query, k_q, k_scales, v_q, v_scales, output, n_heads, n_kv_heads, head_dim,
+                                   seq_len, scale) -> None:
+        """ComputeSingleHeadQ8 (Runtime/CachedAttentionKernel.cs:139-200) for
+        every query head over a Q8 cache: int8 [n_kv_heads, max_ctx, hd] and
+        fp32 scales [n_kv_heads, max_ctx], in the reference's order."""
+        max_ctx = k_q.shape[1]
+        check(_lib.load().ovf_attention_single_head_q8(_ptr(query), _ptr(k_q), _ptr(k_scales), _ptr(v_q),
+                                                       _ptr(v_scales), _ptr(output), n_heads, n_kv_heads, head_dim,
+                                                       max_ctx, seq_len, float(scale), _stream()),
+              "ComputeSingleHeadQ8")
+
+    @staticmethod
     def compute_all_heads(query, k_cache, v_cache, output, n_heads, n_kv_heads, head_dim, seq_len, scale,
                           scratch, counters) -> None:
         """ComputeSingleHead (Runtime/CachedAttentionKernel.cs:36-128) for every

@@ -290,6 +290,37 @@ def test_attention_exact_f32(K, orc, H, KVH, hd, seq):
         assert exact_heads >= 0.75 * H, exact_heads
 
 
+@pytest.mark.parametrize("H,KVH,hd,seq", [(32, 8, 128, 1), (32, 8, 128, 2049), (14, 2, 64, 300), (7, 1, 32, 20),
+                                          (8, 2, 256, 33)])
+def test_attention_q8_cache_bit_exact(K, orc, H, KVH, hd, seq):
+    """Q8 KV cache (Q8KvQuant vectors) attended in ComputeSingleHeadQ8's order
+    vs the restatement with its exp rounded like the GPU's: bit-identical."""
+    rng = np.random.default_rng(seq * 3 + hd)
+    max_ctx = seq + 5
+    kf = rng.normal(0, 1, (KVH, max_ctx, hd)).astype(np.float32)
+    vf = rng.normal(0, 1, (KVH, max_ctx, hd)).astype(np.float32)
+    kq = np.zeros((KVH, max_ctx, hd), np.int8); vq = np.zeros((KVH, max_ctx, hd), np.int8)
+    ks = np.zeros((KVH, max_ctx), np.float32); vs = np.zeros((KVH, max_ctx), np.float32)
+    for g in range(KVH):
+        for t in range(max_ctx):
+            kq[g, t], ks[g, t] = orc.q8kv_quantize(kf[g, t])
+            vq[g, t], vs[g, t] = orc.q8kv_quantize(vf[g, t])
+    q = rng.normal(0, 1, (H, hd)).astype(np.float32)
+    scale = np.float32(1.0 / np.sqrt(hd))
+    out = torch.empty(H * hd, device="cuda")
+    K.CachedAttentionKernel.compute_single_head_q8_all(dev(q), dev(kq), dev(ks), dev(vq), dev(vs), out, H, KVH, hd,
+                                                       seq, scale)
+    got = host(out).reshape(H, hd)
+    orc.set_exp_double_rounded(True)
+    try:
+        G = H // KVH
+        ref = np.stack([orc.attention_single_head_q8(q[h], kq[h // G, :seq], ks[h // G, :seq], vq[h // G, :seq],
+                                                     vs[h // G, :seq], scale) for h in range(H)])
+    finally:
+        orc.set_exp_double_rounded(False)
+    np.testing.assert_array_equal(got, ref)
+
+
 @pytest.mark.parametrize("H,KVH,hd,seq", [(32, 8, 128, 1), (32, 8, 128, 2049), (14, 2, 64, 300), (4, 4, 32, 7)])
 def test_attention_close(K, orc, H, KVH, hd, seq):
     """Split-K flash-decode vs the reference's single-head loop on the same

@@ -214,3 +214,37 @@ def test_parity_fixtures_reproduce(orc):
     np.testing.assert_array_equal(orc.kq_project(orc.Q6_K, z["q6k_x"], z["q6k_w"], 64, 768), z["q6k_y"])
     q, s = orc.q8_0_deinterleave(z["q8_gguf"], 80 * 352)
     np.testing.assert_array_equal(orc.q8_0_project(z["q8_x"], q, s, 80, 352), z["q8_y"])
+
+
+def test_q8kv_quantize_properties(orc):
+    """Q8KvQuant.Quantize (Runtime/Q8KvQuant.cs:25-77): |scale*q - x| <= scale/2
+    (round to nearest), max |q| = 127 at the largest element, zero vector ->
+    scale 0 and zero bytes."""
+    rng = np.random.default_rng(31)
+    for n in (32, 64, 128):
+        x = rng.normal(0, 2, n).astype(np.float32)
+        q, s = orc.q8kv_quantize(x)
+        assert s == np.float32(np.abs(x).max() / np.float32(127))
+        assert np.abs(q).max() == 127
+        assert np.all(np.abs(s * q.astype(np.float32) - x) <= s * 0.5 + 1e-7)
+    q, s = orc.q8kv_quantize(np.zeros(64, np.float32))
+    assert s == 0.0 and not q.any()
+
+
+def test_q8kv_attention_tracks_f32(orc):
+    """ComputeSingleHeadQ8 vs ComputeSingleHead on the same keys/values:
+    the int8 round trip is not bit-identical but cosine ~ 1 (the reference's
+    own claim, Runtime/CachedAttentionKernel.cs:129-137)."""
+    rng = np.random.default_rng(32)
+    hd, seq = 128, 300
+    K = rng.normal(size=(seq, hd)).astype(np.float32)
+    V = rng.normal(size=(seq, hd)).astype(np.float32)
+    kq = np.empty((seq, hd), np.int8); vq = np.empty((seq, hd), np.int8)
+    ks = np.empty(seq, np.float32); vs = np.empty(seq, np.float32)
+    for t in range(seq):
+        kq[t], ks[t] = orc.q8kv_quantize(K[t])
+        vq[t], vs[t] = orc.q8kv_quantize(V[t])
+    q = rng.normal(size=hd).astype(np.float32)
+    a = orc.attention_single_head_q8(q, kq, ks, vq, vs, 1 / np.sqrt(hd))
+    b = orc.attention_single_head(q, K, V, np.float32(1 / np.sqrt(hd)))
+    assert float(a @ b / np.linalg.norm(a) / np.linalg.norm(b)) > 0.999
