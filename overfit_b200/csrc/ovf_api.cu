@@ -143,12 +143,14 @@ ovf_status ovf_kq_project_batched(int32_t type, const float *x, int64_t rows, co
     if (st) return st;
     OVF_CHECK_ARG(rows > 0, "ProjectBatched: rows must be positive");
     OVF_CHECK_ARG(x && y && act_q && act_scales && act_bsums, "ProjectBatched: null buffer");
-    for (int64_t r = 0; r < rows; ++r) {
-        st = ovf_kq_project(type, x + r * k, w, n, k, bias, y + r * n, act_q + r * k, act_scales + r * (k / 256),
-                            act_bsums + r * (k / 16), stream);
-        if (st) return st;
-    }
-    return OVF_OK;
+    OVF_CHECK_ARG(aligned16(x) && aligned16(act_q), "ProjectBatched: input and act_q must be 16-byte aligned");
+    // One row: the streaming decode GEMV is the faster kernel for the same sums.
+    if (rows == 1) return ovf_kq_project(type, x, w, n, k, bias, y, act_q, act_scales, act_bsums, stream);
+    st = launch_quantize_q8k(x, rows * k, act_q, act_scales, act_bsums, S(stream));
+    if (st) return st;
+    const size_t wbytes = (size_t)n * (size_t)(k / 256) * (type == OVF_TYPE_Q4_K ? 144 : 210);
+    return launch_batched_project(type, w, nullptr, wbytes, bias, act_q, act_scales, act_bsums, y, n, k, rows,
+                                  S(stream));
 }
 
 static ovf_status q8_project_impl(const float *x, const int8_t *wq, const float *ws, int64_t n, int64_t k,
@@ -180,12 +182,15 @@ ovf_status ovf_q8_0_project(const float *x, const int8_t *wq, const float *wscal
 ovf_status ovf_q8_0_project_batched(const float *x, int64_t rows, const int8_t *wq, const float *wscales, int64_t n,
                                     int64_t k, const float *bias, float *y, int8_t *x_q, float *x_scales, void *stream) {
     OVF_CHECK_ARG(rows > 0, "Q8 ProjectBatched: rows must be positive");
-    for (int64_t r = 0; r < rows; ++r) {
-        ovf_status st = q8_project_impl(x + r * k, wq, wscales, n, k, bias, y + r * n, x_q + r * k,
-                                        x_scales + r * (k / 32), S(stream));
-        if (st) return st;
-    }
-    return OVF_OK;
+    OVF_CHECK_ARG(n >= 0 && n <= 0x7FFFFFFF, "Q8 ProjectBatched: bad output size");
+    OVF_CHECK_ARG(k > 0 && k % 32 == 0 && k <= 32 * 512, "Q8 ProjectBatched: inputSize %lld must be a multiple of 32",
+                  (long long)k);
+    OVF_CHECK_ARG(x && wq && wscales && y && x_q && x_scales, "Q8 ProjectBatched: null buffer");
+    OVF_CHECK_ARG(aligned16(x) && aligned16(wq) && aligned16(x_q), "Q8 ProjectBatched: buffers must be 16-byte aligned");
+    ovf_status st = launch_quantize_q8_0(x, rows * k, x_q, x_scales, S(stream));
+    if (st) return st;
+    return launch_batched_project(OVF_TYPE_Q8_0, wq, wscales, (size_t)n * (size_t)k, bias, x_q, x_scales, nullptr, y,
+                                  n, k, rows, S(stream));
 }
 
 // --------------------------------------------------------------- codecs

@@ -51,6 +51,12 @@ ovf_status launch_dequant_rows(int type, const void *w, const float *q8s, int64_
 ovf_status launch_requant_q8_0(int type, const void *w, int64_t rows, int64_t k, int8_t *q, float *s,
                                cudaStream_t st);
 
+// ---- ovf_batched.cu: weight-stationary projection of `rows` pre-quantized
+// activation rows (Q8_K for K-quants, Q8_0 for Q8_0 weights).
+ovf_status launch_batched_project(int type, const void *w, const float *ws, size_t w_bytes, const float *bias,
+                                  const int8_t *aq, const float *as, const int16_t *ab, float *y, int64_t n,
+                                  int64_t k, int64_t rows, cudaStream_t st);
+
 // ---- ovf_ops.cu
 struct AttnParams {
     const float *q;           // [H*hd] query (raw when rope tables are given)

@@ -4,6 +4,7 @@
 #include "ovf_api.cu"
 #include "ovf_quant.cu"
 #include "ovf_gemv.cu"
+#include "ovf_batched.cu"
 #include "ovf_ops.cu"
 #include "ovf_attn_cluster.cu"
 #include "ovf_attn_exact.cu"

@@ -196,6 +196,56 @@ def test_batched_bit_exact(K, orc, rows):
     np.testing.assert_array_equal(host(y).reshape(rows, n), orc.kq_project_batched(orc.Q4_K, x, w, n, k, bias))
 
 
+@pytest.mark.parametrize("type_name,rows,n,k,with_bias", [
+    ("Q4_K", 5, 33, 1280, True),      # ragged: 5 activation rows, 33 weight rows, 5 super-blocks (partial chunk)
+    ("Q6_K", 9, 70, 768, False),      # Q6_K rows start 2 bytes past a 16-byte boundary
+    ("Q6_K", 17, 31, 4096, True),
+    ("Q4_K", 64, 14336, 4096, False),  # prefill GEMM shape (gate/up, M = 64)
+    ("Q6_K", 24, 4096, 14336, False),  # down projection shape
+])
+def test_weight_stationary_kq_bit_exact(K, orc, type_name, rows, n, k, with_bias):
+    """ProjectBatchedWeightStationary over ragged tiles: every row equal to
+    the restatement's per-row projection, and the scratch holds each row's
+    own Q8_K activation (Q4KDotKernelTests.cs:96-136)."""
+    t = getattr(orc, type_name)
+    rng = np.random.default_rng(rows * 7 + n)
+    wf = orc.fill_normal(n * k, rows + 3, 0.0, 0.02).reshape(n, k)
+    w = orc.quantize_q4k(wf) if type_name == "Q4_K" else orc.quantize_q6k(wf)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    x[0, :256] = 0.0  # an all-zero activation block
+    bias = rng.uniform(-1, 1, n).astype(np.float32) if with_bias else None
+    y = torch.empty(rows * n, device="cuda")
+    q = torch.empty(rows * k, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows * k // 256, device="cuda")
+    b = torch.empty(rows * k // 16, dtype=torch.int16, device="cuda")
+    cls = K.Q4KDotKernel if type_name == "Q4_K" else K.Q6KDotKernel
+    cls.project_batched(dev(x), rows, K.KQuantWeight(dev(w), k, n, t), None if bias is None else dev(bias), y, q, s, b)
+    np.testing.assert_array_equal(host(y).reshape(rows, n), orc.kq_project_batched(t, x, w, n, k, bias))
+    rq, rs, rb = orc.quantize_q8k(x.reshape(-1))
+    np.testing.assert_array_equal(host(q), rq)
+    np.testing.assert_array_equal(host(s), rs)
+    np.testing.assert_array_equal(host(b), rb)
+
+
+@pytest.mark.parametrize("rows,n,k,with_bias", [(1, 80, 352, True), (11, 45, 1056, False), (16, 896, 4864, True),
+                                                (40, 4864, 896, False)])
+def test_q8_project_batched_bit_exact(K, orc, rows, n, k, with_bias):
+    """Q8DotKernel.ProjectBatched: ragged row/activation tiles and a partial
+    32-block chunk (k = 1056 = 33 blocks), bit-exact to the restatement."""
+    rng = np.random.default_rng(rows + n + k)
+    w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    bias = rng.normal(0, 0.1, n).astype(np.float32) if with_bias else None
+    g = orc.quantize_q8_0_gguf(w)
+    rq, rs = orc.q8_0_deinterleave(g, n * k)
+    ref = orc.q8_0_project_batched(x, rq, rs, n, k, bias)
+    w8 = K.Q8Weight.from_gguf(dev(g), k, n)
+    y = torch.empty(rows * n, device="cuda")
+    xq, xs = torch.empty(rows * k, dtype=torch.int8, device="cuda"), torch.empty(rows * k // 32, device="cuda")
+    K.Q8DotKernel.project_batched(dev(x), rows, w8, None if bias is None else dev(bias), y, xq, xs)
+    np.testing.assert_array_equal(host(y).reshape(rows, n), ref)
+
+
 @pytest.mark.parametrize("n,k,with_bias", [(80, 352, True), (896, 896, False), (4864, 896, False),
                                            (896, 4864, True), (4096, 4096, False), (151936 // 64, 896, False)])
 def test_q8_project_bit_exact(K, orc, n, k, with_bias):
