@@ -220,6 +220,40 @@ def gemv_roofline(torch, eng_cfg, model_file, device, peaks) -> dict:
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback 6650"}
 
 
+def prefill_gemm(torch, eng_cfg, model_file, device) -> dict:
+    """Config-2 prefill projection: the weight-stationary batched Q4_K
+    kernel (ProjectBatchedWeightStationary) on the gate matrices
+    [14336 x 4096] for M activation rows, CUDA-event timed, rotating over the
+    layers' weights.  2*M*N*K integer multiply-adds per launch."""
+    from overfit_b200.kernels import Q4KDotKernel, Q4KWeight
+
+    FF, D = eng_cfg["d_ff"], eng_cfg["d_model"]
+    layers = model_file["layers"][:8]
+    gates = [Q4KWeight(torch.from_numpy(L["gate"][1]).to(device), D, FF) for L in layers]
+    out = {}
+    for M in (16, 128, 512):
+        x = torch.randn(M * D, device=device)
+        y = torch.empty(M * FF, device=device)
+        q = torch.empty(M * D, dtype=torch.int8, device=device)
+        s = torch.empty(M * D // 256, device=device)
+        b = torch.empty(M * D // 16, dtype=torch.int16, device=device)
+        for i in range(3):
+            Q4KDotKernel.project_batched(x, M, gates[i % len(gates)], None, y, q, s, b)
+        torch.cuda.synchronize()
+        reps = 2 * len(gates)
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(reps):
+            Q4KDotKernel.project_batched(x, M, gates[i % len(gates)], None, y, q, s, b)
+        e1.record(st)
+        torch.cuda.synchronize()
+        dt = e0.elapsed_time(e1) / 1e3 / reps
+        out[str(M)] = {"us": dt * 1e6, "int_tops": 2 * M * FF * D / dt / 1e12}
+    del gates
+    return {"kernel": "batched_project_kernel (Q4_K, 14336 x 4096, quantize included)", "rows": out}
+
+
 def profiled_traffic():
     """DRAM bytes per launch of the gate/up GEMV from the committed ncu
     summary (profiles/gemv_q4k_gateup.md, line `traffic_bytes_per_launch:`),
@@ -347,6 +381,7 @@ def run_ours(args):
     kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * kv_elem * (args.prompt + args.warmup +
                                                                                       args.steps // 2)
     roof = gemv_roofline(torch, cfg, mf, device, peaks) if rank == 0 else None
+    pgemm = prefill_gemm(torch, cfg, mf, device) if rank == 0 and not args.layers else None
     sess.close()
     eng.close()
     del mf
@@ -379,6 +414,7 @@ def run_ours(args):
                 "gpu_launches": launches_per_step * args.steps,
                 "f32_kv_exact": exact.get("f32"),
                 "q8_kv_exact": exact.get("q8"),
+                "prefill_gemm": pgemm,
                 "setup_s": {"model_gen_upload": gen_s, "prefill": prefill_s}}
         print(json.dumps(line), flush=True)
     if world > 1:

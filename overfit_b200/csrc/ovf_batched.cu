@@ -62,8 +62,10 @@ struct BatParams {
     const float *as;       // Q8_K [M x K/256] or Q8_0 [M x K/32]
     const int16_t *ab;     // Q8_K bsums [M x K/16]
     float *y;              // [M x n]
+    const float *resid;    // [M x n] residual added after the bias (or null)
     size_t w_bytes;        // size of the weight buffer (bounds the aligned-down copies)
     int n, K, M;
+    int group;             // Q8_0: blocks per head-ordered summation group (0 = one sequential sum)
 };
 
 // Copy `len` bytes from `src` into shared memory at `dst`, starting at the
@@ -119,7 +121,13 @@ __global__ void __launch_bounds__(kBatThreads) batched_project_kernel(const __gr
     const uint8_t *wend = p.w + p.w_bytes;
     const int o = o0 + lane, m = m0 + warp;
     const bool active = o < p.n && m < p.M;
-    float acc = 0.0f;
+    // Grouped (Wo per head, CachedMultiHeadAttention head-ordered sum): each
+    // group of G blocks is summed from zero, and the group sums are added in
+    // order on top of the bias.  Ungrouped: one sum, the bias added last.
+    const int G = KQ ? 0 : p.group;
+    const float bo = active && p.bias ? p.bias[o] : 0.0f;
+    float acc = G ? bo : 0.0f, grp = 0.0f;
+    int gp = 0;
 
     for (int c0 = 0; c0 < nb; c0 += KB) {
         const int cb = min(KB, nb - c0);
@@ -183,21 +191,31 @@ __global__ void __launch_bounds__(kBatThreads) batched_project_kernel(const __gr
                     qa.s = s_as[warp * KB + b];
                     t = q80_block(wr + 32 * b, s_ws[lane * KB + b], qa);
                 }
-                acc = fadd(acc, t);
+                if (G) {
+                    grp = gp == 0 ? fadd(0.0f, t) : fadd(grp, t);
+                    if (++gp == G) {
+                        acc = fadd(acc, grp);
+                        gp = 0;
+                    }
+                } else {
+                    acc = fadd(acc, t);
+                }
             }
         }
         __syncthreads();
     }
     if (active) {
-        const float bo = p.bias ? p.bias[o] : 0.0f;
-        p.y[(size_t)m * p.n + o] = fadd(bo, acc);
+        float y = G || !p.bias ? acc : fadd(bo, acc);
+        if (p.resid) y = fadd(p.resid[(size_t)m * p.n + o], y);
+        p.y[(size_t)m * p.n + o] = y;
     }
 }
 
 ovf_status launch_batched_project(int type, const void *w, const float *ws, size_t w_bytes, const float *bias,
                                   const int8_t *aq, const float *as, const int16_t *ab, float *y, int64_t n,
-                                  int64_t k, int64_t rows, cudaStream_t st) {
+                                  int64_t k, int64_t rows, cudaStream_t st, int group, const float *resid) {
     if (n == 0 || rows == 0) return OVF_OK;
+    OVF_CHECK_ARG(group >= 0 && (group == 0 || type == OVF_TYPE_Q8_0), "batched projection: bad group");
     BatParams p{};
     p.w = (const uint8_t *)w;
     p.ws = ws;
@@ -210,6 +228,8 @@ ovf_status launch_batched_project(int type, const void *w, const float *ws, size
     p.n = (int)n;
     p.K = (int)k;
     p.M = (int)rows;
+    p.group = group;
+    p.resid = resid;
     const dim3 grid((unsigned)((rows + kBatActs - 1) / kBatActs), (unsigned)((n + kBatRows - 1) / kBatRows));
     OVF_CHECK_ARG(grid.y <= 65535u, "batched projection: %lld output rows is too many", (long long)n);
     switch (type) {

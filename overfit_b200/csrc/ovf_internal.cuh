@@ -52,10 +52,13 @@ ovf_status launch_requant_q8_0(int type, const void *w, int64_t rows, int64_t k,
                                cudaStream_t st);
 
 // ---- ovf_batched.cu: weight-stationary projection of `rows` pre-quantized
-// activation rows (Q8_K for K-quants, Q8_0 for Q8_0 weights).
+// activation rows (Q8_K for K-quants, Q8_0 for Q8_0 weights).  `group` > 0
+// (Q8_0 only): head-ordered sums of `group` blocks; `resid` [rows x n]:
+// added after the bias.
 ovf_status launch_batched_project(int type, const void *w, const float *ws, size_t w_bytes, const float *bias,
                                   const int8_t *aq, const float *as, const int16_t *ab, float *y, int64_t n,
-                                  int64_t k, int64_t rows, cudaStream_t st);
+                                  int64_t k, int64_t rows, cudaStream_t st, int group = 0,
+                                  const float *resid = nullptr);
 
 // ---- ovf_ops.cu
 struct AttnParams {
@@ -88,6 +91,11 @@ bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);
 ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8 = false);
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
+ovf_status launch_rmsnorm_rows(const float *x, const float *g, float *y, int rows, int d, float eps, float *scales,
+                               cudaStream_t st);
+ovf_status launch_embed_rows(const int32_t *tokens, int n, int type, const void *w, const float *q8s, int d,
+                             float *out, cudaStream_t st);
+ovf_status launch_set_step_pos(DevStep *step, int cur, int next, cudaStream_t st);
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
                         DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,

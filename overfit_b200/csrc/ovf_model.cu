@@ -74,6 +74,13 @@ struct ovf_session {
     int32_t *pinned_tok = nullptr;  // host staging
     int pinned_cap = 0;
     cudaGraphExec_t graph_logits = nullptr, graph_nologits = nullptr;
+    // batched prefill scratch (allocated on first use): rows of one chunk
+    int pf_rows = 0;
+    float *px = nullptr, *pa = nullptr, *pn = nullptr, *pq = nullptr, *pk = nullptr, *pv = nullptr, *patt = nullptr,
+          *pg = nullptr, *pu = nullptr, *ph = nullptr, *pas = nullptr, *pscale = nullptr;
+    int8_t *paq = nullptr;
+    int16_t *pab = nullptr;
+    int32_t *ptok = nullptr;
     std::vector<void *> allocs;
 };
 
@@ -541,6 +548,163 @@ ovf_status run_step(ovf_session *s, bool with_logits) {
     return OVF_OK;
 }
 
+// ------------------------------------------------------- batched prefill
+// CachedLlamaSession.PrefillBatchedQuant (:818-835) with
+// CachedTransformerBlock.DecodeBatchedQuant (:388-478): the prompt runs
+// through each layer as a chunk of rows — RMSNorm per row, the
+// weight-stationary projections (each weight tile read once per chunk),
+// attention per row in position order (the row's key and value appended
+// before it attends, causal over [0, pos]), Wo with head-ordered sums and
+// the residual, the FFN the same way — and only the last row is projected
+// to logits.  Every row's arithmetic is the single-token step's, so the
+// session ends in the state n decode steps would leave, bit for bit.
+constexpr int kPrefillRows = 256;       // rows per chunk
+constexpr int kPrefillThreshold = 16;   // BatchedPrefillThreshold (CachedLlamaSession.cs:805)
+
+ovf_status prefill_alloc(ovf_session *s) {
+    if (s->pf_rows) return OVF_OK;
+    const ovf_model_config &c = s->m->cfg;
+    const size_t R = kPrefillRows, D = c.d_model, QD = (size_t)c.n_heads * c.head_dim,
+                 KD = (size_t)c.n_kv_heads * c.head_dim, FF = c.d_ff;
+    const size_t KM = std::max(std::max(D, QD), FF);
+    ovf_status st = OVF_OK;
+    auto A = [&](void **p, size_t bytes) {
+        if (!st) st = dalloc(s->allocs, p, bytes);
+    };
+    A((void **)&s->px, R * D * 4);
+    A((void **)&s->pa, R * D * 4);
+    A((void **)&s->pn, R * D * 4);
+    A((void **)&s->pq, R * QD * 4);
+    A((void **)&s->pk, R * KD * 4);
+    A((void **)&s->pv, R * KD * 4);
+    A((void **)&s->patt, R * QD * 4);
+    A((void **)&s->pg, R * FF * 4);
+    A((void **)&s->pu, R * FF * 4);
+    A((void **)&s->ph, R * FF * 4);
+    A((void **)&s->paq, R * KM);
+    A((void **)&s->pas, R * KM / 32 * 4);
+    A((void **)&s->pab, R * KM / 16 * 2);
+    A((void **)&s->ptok, (size_t)(s->max_ctx + 1) * 4);
+    A((void **)&s->pscale, 16);
+    if (!st) s->pf_rows = kPrefillRows;
+    return st;
+}
+
+// Activation rows of `x` quantized for weight `w` (Q8_K for K-quants, Q8_0
+// otherwise), unless they already are (`*fam`: 1 = Q8_K, 2 = Q8_0).
+ovf_status quantize_rows_for(ovf_session *s, const DevWeight &w, const float *x, int rows, int64_t k, int *fam,
+                             cudaStream_t st) {
+    const int want = is_kq(w.type) ? 1 : 2;
+    if (*fam == want) return OVF_OK;
+    *fam = want;
+    return want == 1 ? launch_quantize_q8k(x, rows * k, s->paq, s->pas, s->pab, st)
+                     : launch_quantize_q8_0(x, rows * k, s->paq, s->pas, st);
+}
+
+ovf_status project_rows(ovf_session *s, const DevWeight &w, const float *bias, float *y, int rows, cudaStream_t st,
+                        int group = 0, const float *resid = nullptr) {
+    const size_t wb = (size_t)tensor_bytes(w.type == OVF_TYPE_Q8_0 ? OVF_TYPE_Q8_0 : w.type, w.rows, w.cols);
+    const size_t qbytes = w.type == OVF_TYPE_Q8_0 ? (size_t)w.rows * w.cols : wb;
+    return launch_batched_project(w.type, w.data, w.scales, qbytes, bias, s->paq, s->pas, s->pab, y, w.rows, w.cols,
+                                  rows, st, group, resid);
+}
+
+// Enqueues the batched prefill of tokens [0, n) (already in s->ptok) at
+// positions s->pos ..; the last row's logits and argmax land where a decode
+// step's would.
+ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
+    ovf_model *m = s->m;
+    const ovf_model_config &c = m->cfg;
+    const cudaStream_t st = s->stream;
+    const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, FF = c.d_ff;
+    const int QD = H * hd, KD = KVH * hd;
+    const int base = s->pos;
+    ovf_status r = OVF_OK;
+    int last_rows = 0;
+    for (int r0 = 0; r0 < n; r0 += s->pf_rows) {
+        const int M = std::min(s->pf_rows, n - r0);
+        last_rows = M;
+        if ((r = launch_embed_rows(s->ptok + r0, M, m->embed.type, m->embed.data, m->embed.scales, D, s->px, st)))
+            return r;
+        for (int l = 0; l < c.n_layers; ++l) {
+            const DevLayer &L = m->layers[l];
+            int fam = 0;
+            if ((r = launch_rmsnorm_rows(s->px, L.attn_norm, s->pn, M, D, c.eps, nullptr, st))) return r;
+            if ((r = quantize_rows_for(s, L.wq, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(s, L.wq, L.bq, s->pq, M, st))) return r;
+            if ((r = quantize_rows_for(s, L.wk, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(s, L.wk, L.bk, s->pk, M, st))) return r;
+            if ((r = quantize_rows_for(s, L.wv, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(s, L.wv, L.bv, s->pv, M, st))) return r;
+            const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
+            for (int i = 0; i < M; ++i) {
+                AttnParams a{};
+                a.q = s->pq + (size_t)i * QD;
+                a.k_new = s->pk + (size_t)i * KD;
+                a.v_new = s->pv + (size_t)i * KD;
+                a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
+                a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
+                if (s->kv_dtype == OVF_KV_Q8) {
+                    a.ks = s->ks + (size_t)l * KVH * s->max_ctx;
+                    a.vs = s->vs + (size_t)l * KVH * s->max_ctx;
+                }
+                a.out = s->patt + (size_t)i * QD;
+                a.rope_cos = s->rope_cos;
+                a.rope_sin = s->rope_sin;
+                a.pos_dev = nullptr;
+                a.seq_len_host = base + r0 + i + 1;
+                a.partial = s->partial;
+                a.counters = s->counters;
+                a.split_half = c.rope_split_half;
+                a.H = H;
+                a.KVH = KVH;
+                a.hd = hd;
+                a.max_ctx = s->max_ctx;
+                a.scale = 1.0f / sqrtf((float)hd);
+                if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
+                    if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype == OVF_KV_Q8))) return r;
+                } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
+                    if ((r = launch_attention_cluster(a, st, false))) return r;
+                } else if ((r = launch_attention(a, st, false))) {
+                    return r;
+                }
+            }
+            // Wo (Q8_0) per head, heads in order on the bias, + residual
+            fam = 0;
+            if ((r = quantize_rows_for(s, L.wo, s->patt, M, QD, &fam, st))) return r;
+            const int g = hd / 32 < QD / 32 ? hd / 32 : 0;
+            if ((r = project_rows(s, L.wo, L.bo, s->pa, M, st, g, s->px))) return r;
+            if ((r = launch_rmsnorm_rows(s->pa, L.ffn_norm, s->pn, M, D, c.eps, nullptr, st))) return r;
+            fam = 0;
+            if ((r = quantize_rows_for(s, L.gate, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(s, L.gate, nullptr, s->pg, M, st))) return r;
+            if ((r = quantize_rows_for(s, L.up, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(s, L.up, nullptr, s->pu, M, st))) return r;
+            if ((r = launch_silu_mul(s->pg, s->pu, s->ph, (int64_t)M * FF, st, false))) return r;
+            fam = 0;
+            if ((r = quantize_rows_for(s, L.down, s->ph, M, FF, &fam, st))) return r;
+            if ((r = project_rows(s, L.down, nullptr, s->px, M, st, 0, s->pa))) return r;
+        }
+    }
+    // final norm + logits + argmax of the last prompt row
+    const float *last = s->px + (size_t)(last_rows - 1) * D;
+    if ((r = launch_rmsnorm_rows(last, m->final_norm, s->pn, 1, D, c.eps, s->pscale, st))) return r;
+    if ((r = launch_set_step_pos(s->step, base + n - 1, base + n, st))) return r;
+    GemvParams p{};
+    p.nseg = 1;
+    p.seg[0] = seg_of(m->lm_head, nullptr, s->logits);
+    p.K = D;
+    p.act_mode = ACT_F32_RMSNORM;
+    p.x = last;
+    p.gamma = m->final_norm;
+    p.norm_scale = s->pscale;
+    p.eps = c.eps;
+    p.epi = EPI_LOGITS_ARGMAX;
+    p.step = s->step;
+    p.tokens_out = s->tokens_log;
+    return gemv_launch(p, st, false);
+}
+
 struct DeviceGuard {
     int prev = -1;
     explicit DeviceGuard(int d) {
@@ -764,6 +928,17 @@ static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, 
     DeviceGuard guard(s->m->device);
     OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
     int done = 0;
+    if (n >= kPrefillThreshold && !env_flag("OVF_PREFILL_SINGLE")) {
+        // the batched path (n <= max_ctx <= pinned_cap)
+        ovf_status r = prefill_alloc(s);
+        if (r) return r;
+        memcpy(s->pinned_tok, tokens, (size_t)n * 4);
+        OVF_CUDA_TRY(cudaMemcpyAsync(s->ptok, s->pinned_tok, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
+        if ((r = enqueue_prefill_batched(s, n))) return r;
+        s->pos += n;
+        s->n_logits += 1;
+        done = n;
+    }
     while (done < n) {
         const int chunk = std::min(n - done, s->pinned_cap);
         memcpy(s->pinned_tok, tokens + done, (size_t)chunk * 4);

@@ -340,6 +340,26 @@ ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, f
     return cuda_status(cudaGetLastError(), "rmsnorm");
 }
 
+// Row-wise form for the batched prefill: one CTA per row, the same
+// sequential sum of squares per row; `scales` (optional) receives each
+// row's 1/rms.
+__global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__restrict__ gm, float *__restrict__ y,
+                                    int d, float eps, float *scales) {
+    __shared__ __align__(16) float stage[2048];
+    const float *xr = x + (size_t)blockIdx.x * d;
+    float *yr = y + (size_t)blockIdx.x * d;
+    const float scale = rms_scale(cta_seq_sumsq(xr, d, 0.0f, stage), d, eps);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) yr[i] = gm ? fmul(fmul(xr[i], scale), gm[i]) : fmul(xr[i], scale);
+    if (scales && threadIdx.x == 0) scales[blockIdx.x] = scale;
+}
+
+ovf_status launch_rmsnorm_rows(const float *x, const float *g, float *y, int rows, int d, float eps, float *scales,
+                               cudaStream_t st) {
+    if (rows == 0) return OVF_OK;
+    rmsnorm_rows_kernel<<<rows, 1024, 0, st>>>(x, g, y, d, eps, scales);
+    return cuda_status(cudaGetLastError(), "rmsnorm_rows");
+}
+
 // --------------------------------------------------------------------- RoPE
 __global__ void rope_kernel(float *v, int n_vec, int hd, const float *c, const float *s, int split_half) {
     const int vec = blockIdx.x;
@@ -391,6 +411,42 @@ ovf_status launch_embed(const DevStep *, int type, const void *w, const float *q
     cudaError_t e = launch_pdl(embed_kernel, dim3(1), dim3(1024), 0, st, pdl, step, type, (const uint8_t *)w, q8s, d,
                                hidden, norm_out, eps, trace);
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "embed");
+}
+
+// Embedding rows of a prompt chunk (CachedLlamaSession.PrefillBatchedQuant
+// :818-835, DequantizeRow per token), one CTA per token, the same element
+// decode as embed_kernel.
+__global__ void embed_rows_kernel(const int32_t *__restrict__ tokens, int type, const uint8_t *__restrict__ w,
+                                  const float *__restrict__ q8s, int d, float *__restrict__ out) {
+    const int64_t token = tokens[blockIdx.x];
+    float *row = out + (size_t)blockIdx.x * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float v;
+        if (type == OVF_TYPE_Q4_K) v = q4k_elem(w + (token * (d / 256) + i / 256) * 144, i % 256);
+        else if (type == OVF_TYPE_Q6_K) v = q6k_elem(w + (token * (d / 256) + i / 256) * 210, i % 256);
+        else if (type == OVF_TYPE_Q8_0)
+            v = fmul(q8s[token * (d / 32) + i / 32], (float)reinterpret_cast<const int8_t *>(w)[token * d + i]);
+        else v = reinterpret_cast<const float *>(w)[token * d + i];
+        row[i] = v;
+    }
+}
+
+ovf_status launch_embed_rows(const int32_t *tokens, int n, int type, const void *w, const float *q8s, int d,
+                             float *out, cudaStream_t st) {
+    if (n == 0) return OVF_OK;
+    embed_rows_kernel<<<n, 256, 0, st>>>(tokens, type, (const uint8_t *)w, q8s, d, out);
+    return cuda_status(cudaGetLastError(), "embed_rows");
+}
+
+// Positions after a batched prefill: the state n single-token steps leave.
+__global__ void set_step_pos_kernel(DevStep *step, int cur, int next) {
+    step->cur_pos = cur;
+    step->next_pos = next;
+}
+
+ovf_status launch_set_step_pos(DevStep *step, int cur, int next, cudaStream_t st) {
+    set_step_pos_kernel<<<1, 1, 0, st>>>(step, cur, next);
+    return cuda_status(cudaGetLastError(), "set_step_pos");
 }
 
 // --------------------------------------------------------------- SiLU * up

@@ -152,8 +152,10 @@ class CudaLlamaSession:
             self.prefill(prompt_tokens)
 
     def prefill(self, prompt_tokens) -> int:
-        """CachedLlamaSession.Prefill (single-token path); returns the greedy
-        next token and keeps the last logits."""
+        """CachedLlamaSession.Prefill; returns the greedy next token and keeps
+        the last logits.  Prompts of 16 tokens or more take the batched path
+        (PrefillBatchedQuant, bit-identical to the single-token loop, which
+        OVF_PREFILL_SINGLE=1 forces)."""
         toks = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32))
         if toks.size == 0:
             return -1

@@ -182,3 +182,44 @@ def test_q8_kv_session_bit_exact(E, orc, cfg):
     finally:
         orc.set_exp_double_rounded(False)
 
+
+
+@pytest.mark.parametrize("kv", ["f32", "q8", "f16"])
+@pytest.mark.parametrize("cfg", [TINY_LLAMA, TINY_QWEN], ids=["llama_q4km", "qwen2_q8_0"])
+def test_batched_prefill_matches_single_token_loop(E, cfg, kv):
+    """PrefillBatchedQuant leaves the session exactly where the single-token
+    loop does (CachedLlamaSession.cs:813-817): same last logits, bit for bit,
+    and the same KV cache (the greedy continuation and its logits agree).
+    300 + 40 prompt tokens: two chunks of rows, then a second prefill from a
+    non-zero position."""
+    import os
+    mf = make_model_file(cfg, seed=3)
+    eng = E.CudaLlamaInferenceEngine(cfg, mf)
+    rng = np.random.default_rng(23)
+    p1, p2 = rng.integers(0, cfg["vocab"], 300), rng.integers(0, cfg["vocab"], 40)
+    runs = []
+    for single in (False, True):
+        if single:
+            os.environ["OVF_PREFILL_SINGLE"] = "1"
+        try:
+            s = eng.create_session(384, kv)
+            s.prefill(p1)
+            l1 = s.get_last_logits().copy()
+            tok = s.prefill(p2)
+            l2 = s.get_last_logits().copy()
+        finally:
+            os.environ.pop("OVF_PREFILL_SINGLE", None)
+        steps = []
+        for _ in range(8):
+            tok = s.decode(tok)
+            steps.append((tok, s.get_last_logits().copy()))
+        assert s.current_position == 340 + 8
+        runs.append((l1, l2, steps))
+        s.close()
+    (a1, a2, sa), (b1, b2, sb) = runs
+    np.testing.assert_array_equal(a1, b1)
+    np.testing.assert_array_equal(a2, b2)
+    for i, ((ta, la), (tb, lb)) in enumerate(zip(sa, sb)):
+        assert ta == tb, i
+        np.testing.assert_array_equal(la, lb, err_msg=f"decode step {i}")
+    eng.close()
