@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int g = blockIdx.y;
+    const int row = blockIdx.z;  // batched prefill: query row (position seq_len_host - 1 + row)
     // shared memory map (the mbarriers first: they need 8-byte alignment)
     uint64_t *bar = reinterpret_cast<uint64_t *>(csm);            // [kCBuf]
     __half *kt = reinterpret_cast<__half *>(csm + 128);         // [kCBuf][TK][hd]
@@ -69,7 +70,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     }
     pdl_wait();
     if (tid == 0) trace_mark(p.trace, TR_WAITED);
-    const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
+    const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1 + row;
     const int seq = pos + 1;
     const int per = (seq + kCNC - 1) / kCNC;
     const int t0 = min(seq, rank * per), t1 = min(seq, t0 + per);
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
     };
     if (tid == 0)
         for (int b = 0; b < kCBuf && b < ntiles; ++b) issue(b, b);
-    for (int i = tid; i < G * hd; i += kCThr) qs[i] = p.q[(size_t)g * G * hd + i];
+    for (int i = tid; i < G * hd; i += kCThr) qs[i] = p.q[(size_t)row * p.H * hd + (size_t)g * G * hd + i];
     const bool owns_new = p.k_new != nullptr && pos >= t0 && pos < t1;
     if (owns_new)
         for (int i = tid; i < hd; i += kCThr) {
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(kCThr) attention_cluster_kernel(const AttnPara
                 }
             }
             const bool ok = L > 0.0f && isfinite(L);
-            p.out[(size_t)g * G * hd + i] = ok ? fdiv(acc, L) : 0.0f;
+            p.out[(size_t)row * p.H * hd + (size_t)g * G * hd + i] = ok ? fdiv(acc, L) : 0.0f;
         }
     }
     cluster.sync();  // partners' shared memory must outlive the other ranks' reads
@@ -305,7 +306,7 @@ static cudaError_t launch_cluster_inst(const AttnParams &p, size_t smem, cudaStr
         attr = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kCNC, p.KVH);
+    cfg.gridDim = dim3(kCNC, p.KVH, p.rows > 1 ? p.rows : 1);
     cfg.blockDim = dim3(kCThr);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

@@ -75,6 +75,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int h = blockIdx.x / kExactCluster;
+    const int row = blockIdx.y;  // batched prefill: query row (position seq_len_host - 1 + row)
     const int G = p.H / p.KVH, g = h / G;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int DPC = HD / kExactCluster;
@@ -116,7 +117,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     }
     pdl_wait();
     if (tid == 0) trace_mark(p.trace, TR_WAITED);
-    const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1;
+    const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1 + row;
     const int seq = pos + 1;
     const int chunk = (seq + kExactCluster - 1) / kExactCluster;
     const int t0 = min(seq, rank * chunk), t1 = min(seq, t0 + chunk);
@@ -157,7 +158,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     for (int b = 0; b < NBUF; ++b) stage_values(b);
 
     for (int i = tid; i < HD; i += kExactThreads) {
-        qs[i] = p.q[(size_t)h * HD + i];
+        qs[i] = p.q[((size_t)row * p.H + h) * HD + i];
         if (has_new) {
             kn[i] = p.k_new[(size_t)g * HD + i];
             vn[i] = p.v_new[(size_t)g * HD + i];
@@ -407,9 +408,91 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         stage_values(blk + NBUF);  // into the buffer just consumed
     }
     cp_async_wait<0>();
-    if (tid < DPC) p.out[(size_t)h * HD + d0 + tid] = acc;
+    if (tid < DPC) p.out[((size_t)row * p.H + h) * HD + d0 + tid] = acc;
     cluster.sync();  // no CTA leaves while another may still read its shared memory
     if (tid == 0) trace_mark(p.trace, TR_END);
+}
+
+// One CTA per (row, KV head): the key rotated with RoPE at the row's
+// position and, with the value, stored as the attention kernels store the
+// token they decode — fp32, fp16 (round to nearest) or Q8KvQuant (absmax/127
+// per vector, the same ops as attention_exact_kernel's Q8 append).
+template <int HD>
+__global__ void kv_append_rows_kernel(const AttnParams p, const float *__restrict__ k, const float *__restrict__ v,
+                                      int pos0, int kv_dtype) {
+    __shared__ float kn[HD], vn[HD];
+    __shared__ float sc[4];
+    const int row = blockIdx.x, g = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    const int pos = pos0 + row;
+    const size_t src = ((size_t)row * p.KVH + g) * HD;
+    for (int i = tid; i < HD; i += blockDim.x) {
+        kn[i] = k[src + i];
+        vn[i] = v[src + i];
+    }
+    __syncthreads();
+    if (p.rope_cos) {
+        rope_rotate(kn, HD, p.rope_cos + (size_t)pos * (HD / 2), p.rope_sin + (size_t)pos * (HD / 2), p.split_half,
+                    tid, blockDim.x);
+        __syncthreads();
+    }
+    const size_t dst = ((size_t)g * p.max_ctx + pos) * HD;
+    if (kv_dtype == OVF_KV_F32) {
+        float *kw = reinterpret_cast<float *>(p.kc) + dst, *vw = reinterpret_cast<float *>(p.vc) + dst;
+        for (int i = tid; i < HD; i += blockDim.x) {
+            kw[i] = kn[i];
+            vw[i] = vn[i];
+        }
+    } else if (kv_dtype == OVF_KV_F16) {
+        for (int i = tid; i < HD; i += blockDim.x) {
+            p.kc[dst + i] = __float2half_rn(kn[i]);
+            p.vc[dst + i] = __float2half_rn(vn[i]);
+        }
+    } else {
+        if (tid < 32) {
+            float mk = 0.0f, mv = 0.0f;
+            for (int i = lane; i < HD; i += 32) {
+                mk = fmaxf(mk, fabsf(kn[i]));
+                mv = fmaxf(mv, fabsf(vn[i]));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                mk = fmaxf(mk, __shfl_xor_sync(0xFFFFFFFFu, mk, o));
+                mv = fmaxf(mv, __shfl_xor_sync(0xFFFFFFFFu, mv, o));
+            }
+            if (lane == 0) {
+                sc[0] = mk > 0.0f ? fdiv(mk, 127.0f) : 0.0f;
+                sc[1] = mv > 0.0f ? fdiv(mv, 127.0f) : 0.0f;
+                sc[2] = mk > 0.0f ? fdiv(127.0f, mk) : 0.0f;
+                sc[3] = mv > 0.0f ? fdiv(127.0f, mv) : 0.0f;
+            }
+        }
+        __syncthreads();
+        int8_t *kw = reinterpret_cast<int8_t *>(p.kc) + dst, *vw = reinterpret_cast<int8_t *>(p.vc) + dst;
+        for (int i = tid; i < HD; i += blockDim.x) {
+            kw[i] = (int8_t)quant_elem(kn[i], sc[2]);
+            vw[i] = (int8_t)quant_elem(vn[i], sc[3]);
+        }
+        if (tid == 0) {
+            p.ks[(size_t)g * p.max_ctx + pos] = sc[0];
+            p.vs[(size_t)g * p.max_ctx + pos] = sc[1];
+        }
+    }
+}
+
+ovf_status launch_kv_append_rows(const AttnParams &p, const float *k, const float *v, int rows, int pos0, int kv_dtype,
+                                 cudaStream_t st) {
+    if (rows == 0) return OVF_OK;
+    OVF_CHECK_ARG(rows <= 65535 && pos0 >= 0 && pos0 + rows <= p.max_ctx, "kv append: rows out of range");
+    OVF_CHECK_ARG(kv_dtype != OVF_KV_Q8 || (p.ks && p.vs), "kv append: Q8 cache without its scales");
+    const dim3 grid((unsigned)rows, (unsigned)p.KVH);
+    switch (p.hd) {
+        case 32: kv_append_rows_kernel<32><<<grid, 64, 0, st>>>(p, k, v, pos0, kv_dtype); break;
+        case 64: kv_append_rows_kernel<64><<<grid, 64, 0, st>>>(p, k, v, pos0, kv_dtype); break;
+        case 128: kv_append_rows_kernel<128><<<grid, 64, 0, st>>>(p, k, v, pos0, kv_dtype); break;
+        case 256: kv_append_rows_kernel<256><<<grid, 128, 0, st>>>(p, k, v, pos0, kv_dtype); break;
+        default: OVF_CHECK_ARG(false, "kv append: head_dim %d unsupported", p.hd);
+    }
+    return cuda_status(cudaGetLastError(), "kv_append_rows");
 }
 
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }
@@ -422,7 +505,8 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
                   "attention: sequence length %d outside [1, %d]", seq_len_max, attn_exact_max_seq(p.hd));
     const size_t smem = (size_t)attn_exact_smem_bytes(p.hd, seq_len_max);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.H * kExactCluster);
+    OVF_CHECK_ARG(p.rows <= 1 || (p.k_new == nullptr && !p.pos_dev && p.rows <= 65535), "attention: bad row batch");
+    cfg.gridDim = dim3(p.H * kExactCluster, p.rows > 1 ? p.rows : 1);
     cfg.blockDim = dim3(kExactThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

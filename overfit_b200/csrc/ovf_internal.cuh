@@ -79,6 +79,9 @@ struct AttnParams {
     L2Prefetch pf;            // weights of later launches to pull into L2 during the chains
     TraceSlot *trace;         // OVF_TRACE timeline slot, or null
     int no_kv_prefetch;       // skip the early L2 prefetch of the cache rows
+    int rows;                 // query rows in one launch (batched prefill; 0 or 1 = one): row r is at
+                              // position seq_len_host - 1 + r, its q/out at r * H * hd; k_new must be
+                              // null (the rows' keys and values are appended beforehand)
 };
 int attn_splits(int n_kv_heads);
 int64_t attn_scratch_bytes(int H, int KVH, int hd);
@@ -90,6 +93,11 @@ ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool p
 bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);
 ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8 = false);
+// RoPE + append of `rows` keys/values ([rows][KVH*hd] each) at positions
+// pos0 .. pos0+rows-1 into the cache of `p` (kv_dtype: OVF_KV_*), exactly as
+// the attention kernels append the token they decode.
+ovf_status launch_kv_append_rows(const AttnParams &p, const float *k, const float *v, int rows, int pos0,
+                                 int kv_dtype, cudaStream_t st);
 ovf_status launch_rmsnorm(const float *x, const float *g, float *y, int64_t d, float eps, cudaStream_t st);
 ovf_status launch_rmsnorm_rows(const float *x, const float *g, float *y, int rows, int d, float eps, float *scales,
                                cudaStream_t st);

@@ -637,11 +637,17 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
             if ((r = quantize_rows_for(s, L.wv, s->pn, M, D, &fam, st))) return r;
             if ((r = project_rows(s, L.wv, L.bv, s->pv, M, st))) return r;
             const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
-            for (int i = 0; i < M; ++i) {
+            const bool exact = s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8;
+            const bool cluster = !exact && attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK");
+            // exact and cluster kernels: append every row's key/value first,
+            // then one launch attends all rows (each causal at its position)
+            const bool multi = (exact || cluster) && !env_flag("OVF_PREFILL_ATTN_PER_ROW");
+            for (int i = 0; i < (multi ? 1 : M); ++i) {
                 AttnParams a{};
                 a.q = s->pq + (size_t)i * QD;
-                a.k_new = s->pk + (size_t)i * KD;
-                a.v_new = s->pv + (size_t)i * KD;
+                a.k_new = multi ? nullptr : s->pk + (size_t)i * KD;
+                a.v_new = multi ? nullptr : s->pv + (size_t)i * KD;
+                a.rows = multi ? M : 1;
                 a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
                 a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
                 if (s->kv_dtype == OVF_KV_Q8) {
@@ -661,9 +667,10 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
                 a.hd = hd;
                 a.max_ctx = s->max_ctx;
                 a.scale = 1.0f / sqrtf((float)hd);
-                if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
+                if (multi && (r = launch_kv_append_rows(a, s->pk, s->pv, M, base + r0, s->kv_dtype, st))) return r;
+                if (exact) {
                     if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype == OVF_KV_Q8))) return r;
-                } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
+                } else if (cluster) {
                     if ((r = launch_attention_cluster(a, st, false))) return r;
                 } else if ((r = launch_attention(a, st, false))) {
                     return r;
