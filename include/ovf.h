@@ -241,8 +241,10 @@ int32_t ovf_session_position(const ovf_session *s);
  * token through the stack; logits_host (vocab floats) may be NULL;
  * argmax_out (first index of the max, TokenSampler.ArgMax) may be NULL. */
 ovf_status ovf_session_decode(ovf_session *s, int32_t token, float *logits_host, int32_t *argmax_out);
-/* CachedLlamaSession.Prefill (Runtime/CachedLlamaSession.cs:167), the
- * single-token path: logits of the last token only. */
+/* CachedLlamaSession.Prefill (Runtime/CachedLlamaSession.cs:167): logits
+ * of the last token only.  Like the reference, n >= 16 tokens take the
+ * batched path (PrefillBatchedQuant, :818-835), which leaves the session in
+ * the state the single-token loop would, bit for bit. */
 ovf_status ovf_session_prefill(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host,
                                int32_t *argmax_out);
 /* Greedy generation (GenerateNextToken with temperature 0, repeated): feeds

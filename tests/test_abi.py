@@ -70,6 +70,18 @@ def test_argument_errors_without_gpu(lib):
     assert lib.ovf_session_create_kv(None, 64, 0, C.byref(out)) == _lib.OVF_EINVAL
     # RMSNorm and the projections reject null buffers on the host
     assert lib.ovf_q4k_project_gate_up(None, None, None, 4, 256, None, None, None, None, None, None) == _lib.OVF_EINVAL
+    # ProjectBatched / ProjectBatchedWeightStationary: rows must be positive,
+    # buffers non-null and 16-byte aligned (before any device work)
+    p16 = C.c_void_p(16)
+    assert lib.ovf_kq_project_batched(12, p16, 0, p16, 4, 256, None, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project_batched(12, None, 2, p16, 4, 256, None, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project_batched(12, C.c_void_p(20), 2, p16, 4, 256, None, p16, p16, p16, p16,
+                                      None) == _lib.OVF_EINVAL
+    assert b"aligned" in lib.ovf_last_error()
+    assert lib.ovf_q8_0_project_batched(p16, 0, p16, p16, 4, 64, None, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_q8_0_project_batched(p16, 2, p16, p16, 4, 48, None, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_q8_0_project_batched(p16, 2, C.c_void_p(8), p16, 4, 64, None, p16, p16, p16,
+                                        None) == _lib.OVF_EINVAL
 
 
 def test_python_mirror_raises_value_error():
