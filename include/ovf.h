@@ -254,6 +254,16 @@ ovf_status ovf_session_generate_greedy(ovf_session *s, int32_t n_steps, int32_t 
 /* The cudaStream_t (as void*) all of the session's device work is ordered
  * on, for callers that time it with events. */
 void *ovf_session_stream(const ovf_session *s);
+/* One DecodeToken in each of n (<= 64) distinct sessions of one model, run
+ * as one batch: every weight tile is read once for all n tokens, and each
+ * session ends in the state its own ovf_session_decode would leave (same
+ * logits and argmax, bit for bit).  logits_host: [n x vocab] or NULL;
+ * argmax_out: [n] or NULL.  The reference serves concurrent sessions one
+ * DecodeToken call at a time (a session per client from
+ * ISlmInferenceEngine.CreateSession, Contracts/ISlmInferenceEngine.cs:9-52);
+ * one batch call per model at a time. */
+ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, const int32_t *tokens,
+                                    float *logits_host, int32_t *argmax_out);
 
 #ifdef __cplusplus
 }

@@ -85,6 +85,7 @@ SIGNATURES = {
     "ovf_session_prefill": (I32, [P, P, I32, P, P]),
     "ovf_session_generate_greedy": (I32, [P, I32, P]),
     "ovf_session_stream": (P, [P]),
+    "ovf_session_decode_batch": (I32, [P, I32, P, P, P]),
 }
 
 _lib = None

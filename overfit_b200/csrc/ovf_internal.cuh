@@ -104,6 +104,9 @@ ovf_status launch_rmsnorm_rows(const float *x, const float *g, float *y, int row
 ovf_status launch_embed_rows(const int32_t *tokens, int n, int type, const void *w, const float *q8s, int d,
                              float *out, cudaStream_t st);
 ovf_status launch_set_step_pos(DevStep *step, int cur, int next, cudaStream_t st);
+ovf_status launch_argmax_rows(const float *logits, int rows, int vocab, int32_t *out, cudaStream_t st);
+ovf_status launch_batch_finish(DevStep *step, int cur, int next, const int32_t *token, int32_t *tokens_log,
+                               cudaStream_t st);
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
                         DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,

@@ -51,6 +51,14 @@ struct ovf_model {
     float *final_norm = nullptr;
     std::vector<void *> allocs;
     int64_t weight_bytes = 0;
+    // multi-session decode scratch (allocated on first use)
+    int b_rows = 0;
+    float *bx = nullptr, *ba = nullptr, *bn = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr, *batt = nullptr,
+          *bg = nullptr, *bu = nullptr, *bh = nullptr, *bas = nullptr, *blogits = nullptr;
+    int8_t *baq = nullptr;
+    int16_t *bab = nullptr;
+    int32_t *btok = nullptr, *bargmax = nullptr;
+    int32_t *btok_host = nullptr;  // pinned
 };
 
 struct ovf_session {
@@ -592,21 +600,69 @@ ovf_status prefill_alloc(ovf_session *s) {
 
 // Activation rows of `x` quantized for weight `w` (Q8_K for K-quants, Q8_0
 // otherwise), unless they already are (`*fam`: 1 = Q8_K, 2 = Q8_0).
-ovf_status quantize_rows_for(ovf_session *s, const DevWeight &w, const float *x, int rows, int64_t k, int *fam,
+struct ActRows {  // quantized activation rows (Q8_K or Q8_0) of a batch
+    int8_t *aq;
+    float *as;
+    int16_t *ab;
+};
+
+ovf_status quantize_rows_for(const ActRows &ar, const DevWeight &w, const float *x, int rows, int64_t k, int *fam,
                              cudaStream_t st) {
     const int want = is_kq(w.type) ? 1 : 2;
     if (*fam == want) return OVF_OK;
     *fam = want;
-    return want == 1 ? launch_quantize_q8k(x, rows * k, s->paq, s->pas, s->pab, st)
-                     : launch_quantize_q8_0(x, rows * k, s->paq, s->pas, st);
+    return want == 1 ? launch_quantize_q8k(x, rows * k, ar.aq, ar.as, ar.ab, st)
+                     : launch_quantize_q8_0(x, rows * k, ar.aq, ar.as, st);
 }
 
-ovf_status project_rows(ovf_session *s, const DevWeight &w, const float *bias, float *y, int rows, cudaStream_t st,
+ovf_status project_rows(const ActRows &ar, const DevWeight &w, const float *bias, float *y, int rows, cudaStream_t st,
                         int group = 0, const float *resid = nullptr) {
-    const size_t wb = (size_t)tensor_bytes(w.type == OVF_TYPE_Q8_0 ? OVF_TYPE_Q8_0 : w.type, w.rows, w.cols);
-    const size_t qbytes = w.type == OVF_TYPE_Q8_0 ? (size_t)w.rows * w.cols : wb;
-    return launch_batched_project(w.type, w.data, w.scales, qbytes, bias, s->paq, s->pas, s->pab, y, w.rows, w.cols,
+    const size_t qbytes = w.type == OVF_TYPE_Q8_0 ? (size_t)w.rows * w.cols : (size_t)tensor_bytes(w.type, w.rows, w.cols);
+    return launch_batched_project(w.type, w.data, w.scales, qbytes, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols,
                                   rows, st, group, resid);
+}
+
+// Row buffers of one batch of hidden states ([rows][width] each).
+struct RowBufs {
+    ActRows ar;
+    float *x, *a, *n, *q, *k, *v, *att, *g, *u, *h;
+};
+
+// RMSNorm of x (attn_norm) -> n, then Q/K/V of every row (with biases).
+ovf_status rows_norm_qkv(const ovf_model *m, const DevLayer &L, const RowBufs &b, int M, cudaStream_t st) {
+    const ovf_model_config &c = m->cfg;
+    const int D = c.d_model;
+    int fam = 0;
+    ovf_status r;
+    if ((r = launch_rmsnorm_rows(b.x, L.attn_norm, b.n, M, D, c.eps, nullptr, st))) return r;
+    if ((r = quantize_rows_for(b.ar, L.wq, b.n, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, L.wq, L.bq, b.q, M, st))) return r;
+    if ((r = quantize_rows_for(b.ar, L.wk, b.n, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, L.wk, L.bk, b.k, M, st))) return r;
+    if ((r = quantize_rows_for(b.ar, L.wv, b.n, M, D, &fam, st))) return r;
+    return project_rows(b.ar, L.wv, L.bv, b.v, M, st);
+}
+
+// Wo (Q8_0, heads in order on the bias) + residual x -> a; RMSNorm(a) ->
+// n; gate/up; SiLU*up -> h; down + residual a -> x.
+ovf_status rows_wo_ffn(const ovf_model *m, const DevLayer &L, const RowBufs &b, int M, cudaStream_t st) {
+    const ovf_model_config &c = m->cfg;
+    const int D = c.d_model, QD = c.n_heads * c.head_dim, hd = c.head_dim, FF = c.d_ff;
+    int fam = 0;
+    ovf_status r;
+    if ((r = quantize_rows_for(b.ar, L.wo, b.att, M, QD, &fam, st))) return r;
+    const int g = hd / 32 < QD / 32 ? hd / 32 : 0;
+    if ((r = project_rows(b.ar, L.wo, L.bo, b.a, M, st, g, b.x))) return r;
+    if ((r = launch_rmsnorm_rows(b.a, L.ffn_norm, b.n, M, D, c.eps, nullptr, st))) return r;
+    fam = 0;
+    if ((r = quantize_rows_for(b.ar, L.gate, b.n, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, L.gate, nullptr, b.g, M, st))) return r;
+    if ((r = quantize_rows_for(b.ar, L.up, b.n, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, L.up, nullptr, b.u, M, st))) return r;
+    if ((r = launch_silu_mul(b.g, b.u, b.h, (int64_t)M * FF, st, false))) return r;
+    fam = 0;
+    if ((r = quantize_rows_for(b.ar, L.down, b.h, M, FF, &fam, st))) return r;
+    return project_rows(b.ar, L.down, nullptr, b.x, M, st, 0, b.a);
 }
 
 // Enqueues the batched prefill of tokens [0, n) (already in s->ptok) at
@@ -619,6 +675,7 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
     const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, FF = c.d_ff;
     const int QD = H * hd, KD = KVH * hd;
     const int base = s->pos;
+    const ActRows ar{s->paq, s->pas, s->pab};
     ovf_status r = OVF_OK;
     int last_rows = 0;
     for (int r0 = 0; r0 < n; r0 += s->pf_rows) {
@@ -630,12 +687,12 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
             const DevLayer &L = m->layers[l];
             int fam = 0;
             if ((r = launch_rmsnorm_rows(s->px, L.attn_norm, s->pn, M, D, c.eps, nullptr, st))) return r;
-            if ((r = quantize_rows_for(s, L.wq, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(s, L.wq, L.bq, s->pq, M, st))) return r;
-            if ((r = quantize_rows_for(s, L.wk, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(s, L.wk, L.bk, s->pk, M, st))) return r;
-            if ((r = quantize_rows_for(s, L.wv, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(s, L.wv, L.bv, s->pv, M, st))) return r;
+            if ((r = quantize_rows_for(ar, L.wq, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(ar, L.wq, L.bq, s->pq, M, st))) return r;
+            if ((r = quantize_rows_for(ar, L.wk, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(ar, L.wk, L.bk, s->pk, M, st))) return r;
+            if ((r = quantize_rows_for(ar, L.wv, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(ar, L.wv, L.bv, s->pv, M, st))) return r;
             const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
             const bool exact = s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8;
             const bool cluster = !exact && attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK");
@@ -678,19 +735,19 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
             }
             // Wo (Q8_0) per head, heads in order on the bias, + residual
             fam = 0;
-            if ((r = quantize_rows_for(s, L.wo, s->patt, M, QD, &fam, st))) return r;
+            if ((r = quantize_rows_for(ar, L.wo, s->patt, M, QD, &fam, st))) return r;
             const int g = hd / 32 < QD / 32 ? hd / 32 : 0;
-            if ((r = project_rows(s, L.wo, L.bo, s->pa, M, st, g, s->px))) return r;
+            if ((r = project_rows(ar, L.wo, L.bo, s->pa, M, st, g, s->px))) return r;
             if ((r = launch_rmsnorm_rows(s->pa, L.ffn_norm, s->pn, M, D, c.eps, nullptr, st))) return r;
             fam = 0;
-            if ((r = quantize_rows_for(s, L.gate, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(s, L.gate, nullptr, s->pg, M, st))) return r;
-            if ((r = quantize_rows_for(s, L.up, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(s, L.up, nullptr, s->pu, M, st))) return r;
+            if ((r = quantize_rows_for(ar, L.gate, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(ar, L.gate, nullptr, s->pg, M, st))) return r;
+            if ((r = quantize_rows_for(ar, L.up, s->pn, M, D, &fam, st))) return r;
+            if ((r = project_rows(ar, L.up, nullptr, s->pu, M, st))) return r;
             if ((r = launch_silu_mul(s->pg, s->pu, s->ph, (int64_t)M * FF, st, false))) return r;
             fam = 0;
-            if ((r = quantize_rows_for(s, L.down, s->ph, M, FF, &fam, st))) return r;
-            if ((r = project_rows(s, L.down, nullptr, s->px, M, st, 0, s->pa))) return r;
+            if ((r = quantize_rows_for(ar, L.down, s->ph, M, FF, &fam, st))) return r;
+            if ((r = project_rows(ar, L.down, nullptr, s->px, M, st, 0, s->pa))) return r;
         }
     }
     // final norm + logits + argmax of the last prompt row
@@ -710,6 +767,107 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
     p.step = s->step;
     p.tokens_out = s->tokens_log;
     return gemv_launch(p, st, false);
+}
+
+// ------------------------------------------------- multi-session decode
+// N sessions of one model decode one token each as rows of one batch:
+// embedding rows, RMSNorm rows, the weight-stationary projections (each
+// weight tile read once for all N), attention per row on that session's own
+// cache at its own position, Wo/FFN rows, final norm, LM head rows and the
+// argmax per row.  Every row's arithmetic is its session's decode step, so
+// the results equal N single decodes, bit for bit (the reference serves
+// concurrent sessions one DecodeToken at a time).
+constexpr int kBatchMax = 64;
+
+ovf_status batch_alloc(ovf_model *m) {
+    if (m->b_rows) return OVF_OK;
+    const ovf_model_config &c = m->cfg;
+    const size_t R = kBatchMax, D = c.d_model, QD = (size_t)c.n_heads * c.head_dim,
+                 KD = (size_t)c.n_kv_heads * c.head_dim, FF = c.d_ff, V = c.vocab;
+    const size_t KM = std::max(std::max(D, QD), FF);
+    ovf_status st = OVF_OK;
+    auto A = [&](void **p, size_t bytes) {
+        if (!st) st = dalloc(m->allocs, p, bytes);
+    };
+    A((void **)&m->bx, R * D * 4);
+    A((void **)&m->ba, R * D * 4);
+    A((void **)&m->bn, R * D * 4);
+    A((void **)&m->bq, R * QD * 4);
+    A((void **)&m->bk, R * KD * 4);
+    A((void **)&m->bv, R * KD * 4);
+    A((void **)&m->batt, R * QD * 4);
+    A((void **)&m->bg, R * FF * 4);
+    A((void **)&m->bu, R * FF * 4);
+    A((void **)&m->bh, R * FF * 4);
+    A((void **)&m->baq, R * KM);
+    A((void **)&m->bas, R * KM / 32 * 4);
+    A((void **)&m->bab, R * KM / 16 * 2);
+    A((void **)&m->blogits, R * V * 4);
+    A((void **)&m->btok, R * 4);
+    A((void **)&m->bargmax, R * 4);
+    if (!st && !m->btok_host) st = cuda_status(cudaMallocHost(&m->btok_host, R * 4), "cudaMallocHost");
+    if (!st) m->b_rows = kBatchMax;
+    return st;
+}
+
+ovf_status enqueue_batch_decode(ovf_model *m, ovf_session *const *ss, int n, cudaStream_t st) {
+    const ovf_model_config &c = m->cfg;
+    const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, QD = H * hd, KD = KVH * hd;
+    const RowBufs rb{ActRows{m->baq, m->bas, m->bab}, m->bx, m->ba, m->bn, m->bq, m->bk, m->bv, m->batt,
+                     m->bg, m->bu, m->bh};
+    ovf_status r;
+    if ((r = launch_embed_rows(m->btok, n, m->embed.type, m->embed.data, m->embed.scales, D, m->bx, st))) return r;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const DevLayer &L = m->layers[l];
+        if ((r = rows_norm_qkv(m, L, rb, n, st))) return r;
+        for (int i = 0; i < n; ++i) {
+            ovf_session *s = ss[i];
+            const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
+            AttnParams a{};
+            a.q = m->bq + (size_t)i * QD;
+            a.k_new = m->bk + (size_t)i * KD;
+            a.v_new = m->bv + (size_t)i * KD;
+            a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
+            a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
+            if (s->kv_dtype == OVF_KV_Q8) {
+                a.ks = s->ks + (size_t)l * KVH * s->max_ctx;
+                a.vs = s->vs + (size_t)l * KVH * s->max_ctx;
+            }
+            a.out = m->batt + (size_t)i * QD;
+            a.rope_cos = s->rope_cos;
+            a.rope_sin = s->rope_sin;
+            a.seq_len_host = s->pos + 1;
+            a.partial = s->partial;
+            a.counters = s->counters;
+            a.split_half = c.rope_split_half;
+            a.H = H;
+            a.KVH = KVH;
+            a.hd = hd;
+            a.max_ctx = s->max_ctx;
+            a.scale = 1.0f / sqrtf((float)hd);
+            if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
+                if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype == OVF_KV_Q8))) return r;
+            } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
+                if ((r = launch_attention_cluster(a, st, false))) return r;
+            } else if ((r = launch_attention(a, st, false))) {
+                return r;
+            }
+        }
+        if ((r = rows_wo_ffn(m, L, rb, n, st))) return r;
+    }
+    // final norm, LM head rows, argmax per row
+    if ((r = launch_rmsnorm_rows(m->bx, m->final_norm, m->bn, n, D, c.eps, nullptr, st))) return r;
+    int fam = 0;
+    if ((r = quantize_rows_for(rb.ar, m->lm_head, m->bn, n, D, &fam, st))) return r;
+    if ((r = project_rows(rb.ar, m->lm_head, nullptr, m->blogits, n, st))) return r;
+    if ((r = launch_argmax_rows(m->blogits, n, c.vocab, m->bargmax, st))) return r;
+    for (int i = 0; i < n; ++i) {
+        ovf_session *s = ss[i];
+        OVF_CUDA_TRY(cudaMemcpyAsync(s->logits, m->blogits + (size_t)i * c.vocab, (size_t)c.vocab * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+        if ((r = launch_batch_finish(s->step, s->pos, s->pos + 1, m->bargmax + i, s->tokens_log, st))) return r;
+    }
+    return OVF_OK;
 }
 
 struct DeviceGuard {
@@ -818,6 +976,7 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
 ovf_status ovf_model_destroy(ovf_model *m) {
     if (!m) return OVF_OK;
     DeviceGuard guard(m->device);
+    if (m->btok_host) cudaFreeHost(m->btok_host);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return OVF_OK;
@@ -996,5 +1155,43 @@ ovf_status ovf_session_generate_greedy(ovf_session *s, int32_t n_steps, int32_t 
 }
 
 void *ovf_session_stream(const ovf_session *s) { return s ? (void *)s->stream : nullptr; }
+
+ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, const int32_t *tokens,
+                                    float *logits_host, int32_t *argmax_out) {
+    OVF_CHECK_ARG(sessions && tokens && n > 0, "decode batch: bad arguments");
+    OVF_CHECK_ARG(n <= kBatchMax, "decode batch: at most %d sessions per call, got %d", kBatchMax, n);
+    ovf_model *m = sessions[0] ? sessions[0]->m : nullptr;
+    OVF_CHECK_ARG(m, "decode batch: null session");
+    for (int i = 0; i < n; ++i) {
+        ovf_session *s = sessions[i];
+        OVF_CHECK_ARG(s && s->m == m, "decode batch: session %d is null or of another model", i);
+        for (int j = 0; j < i; ++j) OVF_CHECK_ARG(sessions[j] != s, "decode batch: session %d repeated", i);
+        OVF_CHECK_ARG(s->pos + 1 <= s->max_ctx, "KV cache is full (ContextLength=%d) in session %d", s->max_ctx, i);
+        OVF_CHECK_ARG(tokens[i] >= 0 && tokens[i] < m->cfg.vocab, "token id %d out of range", tokens[i]);
+    }
+    DeviceGuard guard(m->device);
+    ovf_status r = batch_alloc(m);
+    if (r) return r;
+    for (int i = 0; i < n; ++i) OVF_CUDA_TRY(cudaStreamSynchronize(sessions[i]->stream));
+    const cudaStream_t st = sessions[0]->stream;
+    memcpy(m->btok_host, tokens, (size_t)n * 4);
+    OVF_CUDA_TRY(cudaMemcpyAsync(m->btok, m->btok_host, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    if ((r = enqueue_batch_decode(m, sessions, n, st))) return r;
+    for (int i = 0; i < n; ++i) {
+        sessions[i]->pos += 1;
+        sessions[i]->n_logits += 1;
+    }
+    if (logits_host)
+        OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, m->blogits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
+    if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->bargmax, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    OVF_CUDA_TRY(cudaStreamSynchronize(st));
+    int code = 0;
+    cudaMemcpyFromSymbol(&code, g_dev_error, sizeof(int));
+    if (code) {
+        set_error("device wait timed out (code %d)", code);
+        return OVF_ETIMEDOUT;
+    }
+    return OVF_OK;
+}
 
 }  // extern "C"

@@ -438,6 +438,52 @@ ovf_status launch_embed_rows(const int32_t *tokens, int n, int type, const void 
     return cuda_status(cudaGetLastError(), "embed_rows");
 }
 
+// Greedy token of each logits row (TokenSampler.ArgMax: first index of the
+// maximum), one CTA per row, with the decode LM head's ordering key.
+__global__ void argmax_rows_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out) {
+    __shared__ unsigned long long red[32];
+    const float *row = logits + (size_t)blockIdx.x * vocab;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const unsigned long long k = argmax_key(row[i], i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+        out[blockIdx.x] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    }
+}
+
+ovf_status launch_argmax_rows(const float *logits, int rows, int vocab, int32_t *out, cudaStream_t st) {
+    if (rows == 0) return OVF_OK;
+    argmax_rows_kernel<<<rows, 1024, 0, st>>>(logits, vocab, out);
+    return cuda_status(cudaGetLastError(), "argmax_rows");
+}
+
+// A session's step state after one token of a multi-session batch: the
+// position advanced and the sampled token logged, as its own decode step
+// with logits leaves them.
+__global__ void batch_finish_kernel(DevStep *step, int cur, int next, const int32_t *token, int32_t *tokens_log) {
+    step->cur_pos = cur;
+    step->next_pos = next;
+    step->token = *token;
+    if (tokens_log) tokens_log[step->n_generated] = *token;
+    step->n_generated += 1;
+}
+
+ovf_status launch_batch_finish(DevStep *step, int cur, int next, const int32_t *token, int32_t *tokens_log,
+                               cudaStream_t st) {
+    batch_finish_kernel<<<1, 1, 0, st>>>(step, cur, next, token, tokens_log);
+    return cuda_status(cudaGetLastError(), "batch_finish");
+}
+
 // Positions after a batched prefill: the state n single-token steps leave.
 __global__ void set_step_pos_kernel(DevStep *step, int cur, int next) {
     step->cur_pos = cur;

@@ -105,6 +105,26 @@ class CudaLlamaInferenceEngine:
         exact ComputeSingleHeadQ8 order) or "f16" (no reference counterpart)."""
         return CudaLlamaSession(self, max_context, kv_cache_dtype)
 
+    def decode_batch(self, sessions, tokens, want_logits: bool = True) -> np.ndarray:
+        """One DecodeToken in each session (distinct sessions of this engine),
+        batched on the device; returns the argmax per session.  Each session
+        ends exactly as its own decode() would leave it."""
+        n = len(sessions)
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        if toks.size != n:
+            raise ValueError("one token per session")
+        handles = (C.c_void_p * n)(*[s._h for s in sessions])
+        am = np.empty(n, np.int32)
+        logits = np.empty((n, self.cfg["vocab"]), np.float32) if want_logits else None
+        check(_lib.load().ovf_session_decode_batch(handles, n, toks.ctypes.data,
+                                                   logits.ctypes.data if want_logits else None, am.ctypes.data),
+              "DecodeBatch")
+        for i, s in enumerate(sessions):
+            if want_logits:
+                s._logits[:] = logits[i]
+            s._have_logits = want_logits
+        return am
+
     def close(self):
         if self._h:
             _lib.load().ovf_model_destroy(self._h)

@@ -223,3 +223,34 @@ def test_batched_prefill_matches_single_token_loop(E, cfg, kv):
         assert ta == tb, i
         np.testing.assert_array_equal(la, lb, err_msg=f"decode step {i}")
     eng.close()
+
+
+@pytest.mark.parametrize("cfg", [TINY_LLAMA, TINY_QWEN], ids=["llama_q4km", "qwen2_q8_0"])
+def test_decode_batch_matches_single_sessions(E, cfg):
+    """Concurrent sessions decoded as one batch (weights read once for all of
+    them) end exactly where their own DecodeToken calls would: the same
+    logits bit for bit and the same greedy tokens, for sessions at different
+    positions with F32, Q8 and fp16 caches; the device greedy loop then
+    continues identically."""
+    mf = make_model_file(cfg, seed=5)
+    eng = E.CudaLlamaInferenceEngine(cfg, mf)
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, cfg["vocab"], n) for n in (3, 20, 7, 1)]
+    kvs = ["f32", "q8", "f16", "f32"]
+    batch = [eng.create_session(96, kv) for kv in kvs]
+    single = [eng.create_session(96, kv) for kv in kvs]
+    tb = [s.prefill(p) for s, p in zip(batch, prompts)]
+    ts = [s.prefill(p) for s, p in zip(single, prompts)]
+    assert tb == ts
+    for step in range(6):
+        tb = list(eng.decode_batch(batch, tb))
+        ts = [s.decode(t) for s, t in zip(single, ts)]
+        assert tb == ts, step
+        for a, b in zip(batch, single):
+            np.testing.assert_array_equal(a.get_last_logits(), b.get_last_logits(), err_msg=f"step {step}")
+    for a, b in zip(batch, single):
+        assert a.current_position == b.current_position
+        np.testing.assert_array_equal(a.generate_greedy(4), b.generate_greedy(4))
+    for s in batch + single:
+        s.close()
+    eng.close()
