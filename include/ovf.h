@@ -40,6 +40,7 @@ typedef int32_t ovf_status;
 #define OVF_ETIMEDOUT (-5)    /* a bounded device wait gave up (error word set by a kernel) */
 #define OVF_ESTATE (-6)       /* invalid state, e.g. KV cache full — OverfitRuntimeException */
 #define OVF_EUNSUPPORTED (-7) /* format/shape combination not supported */
+#define OVF_EBUSY (-8)        /* the object is in use by another call */
 
 /* ggml type ids (GGUF numbering, Loading/GgmlType.cs). */
 #define OVF_TYPE_F32 0
@@ -128,6 +129,14 @@ ovf_status ovf_requant_q8_0(int32_t src_type, const void *w, int64_t rows, int64
  * s = 1/sqrt(sum(x^2)/d + eps). gamma may be NULL. */
 ovf_status ovf_rmsnorm(const float *x, const float *gamma, float *y, int64_t d, float eps,
                        void *stream);
+/* MathF.Exp elementwise (the softmax and SiLU exponential of
+ * Runtime/CachedAttentionKernel.cs:36 and Runtime/CachedFeedForwardBlock.cs:464):
+ * the bits of the host C library's expf on an x86-64 host with FMA (glibc's
+ * ARM optimized-routines expf), which is what MathF.Exp calls on Linux. */
+ovf_status ovf_exp_f32(const float *x, float *y, int64_t n, void *stream);
+/* Runtime/CachedFeedForwardBlock.cs:464-472 ApplySiLU then :309 Multiply:
+ * h = (g * sigmoid(g)) * u with sigmoid(g) = 1 / (1 + exp(-g)). */
+ovf_status ovf_swiglu(const float *gate, const float *up, float *h, int64_t n, void *stream);
 /* Rope/RopeKernel.cs:46 Apply over n_vec vectors of head_dim, rotated at
  * the given cos/sin row (Rope/RopeTable.cs:109 layout [hd/2]). */
 ovf_status ovf_rope_apply(float *v, int32_t n_vec, int32_t head_dim, const float *cos_row,
@@ -260,8 +269,10 @@ void *ovf_session_stream(const ovf_session *s);
  * logits and argmax, bit for bit).  logits_host: [n x vocab] or NULL;
  * argmax_out: [n] or NULL.  The reference serves concurrent sessions one
  * DecodeToken call at a time (a session per client from
- * ISlmInferenceEngine.CreateSession, Contracts/ISlmInferenceEngine.cs:9-52);
- * one batch call per model at a time. */
+ * ISlmInferenceEngine.CreateSession, Contracts/ISlmInferenceEngine.cs:9-52).
+ * One batch call per model at a time: a second concurrent call returns
+ * OVF_EBUSY.  If a call fails after enqueuing work, its sessions return
+ * OVF_ESTATE until ovf_session_reset. */
 ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, const int32_t *tokens,
                                     float *logits_host, int32_t *argmax_out);
 

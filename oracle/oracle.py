@@ -87,7 +87,7 @@ def _declare(L):
         "orc_session_set_kv_q8": (None, [P, C.c_int]),
         "orc_q8kv_quantize": (C.c_float, [P, C.c_int, P]),
         "orc_attention_single_head_q8": (None, [P, P, P, P, P, P, P, C.c_int, C.c_int, C.c_float]),
-        "orc_set_exp_double_rounded": (None, [C.c_int]),
+        "orc_expf_array": (None, [C.c_void_p, C.c_void_p, C.c_int64]),
         "orc_session_position": (C.c_int, [P]),
         "orc_session_decode": (C.c_int, [P, C.c_int, P]),
         "orc_session_decode_layers": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P]),
@@ -417,11 +417,12 @@ class OracleSession:
             pass
 
 
-def set_exp_double_rounded(on: bool = True):
-    """Test switch: the restatement's exp becomes a double-precision exp
-    rounded once (the GPU's), instead of the C library's expf (the
-    reference's MathF.Exp).  Isolates exp rounding from everything else."""
-    lib().orc_set_exp_double_rounded(int(on))
+def expf_array(x: np.ndarray) -> np.ndarray:
+    """MathF.Exp elementwise: the host C library's expf."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_expf_array(x.ctypes.data, y.ctypes.data, x.size)
+    return y
 
 
 def q8kv_quantize(v: np.ndarray):

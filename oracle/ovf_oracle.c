@@ -575,13 +575,14 @@ void orc_rope_apply(float *v, int hd, const float *c, const float *s, int split_
 }
 
 /* e^x as the reference computes it: MathF.Exp, i.e. the host C library's
- * expf.  Test switch (orc_set_exp_double_rounded): round a double-precision
- * exp once instead, as the GPU does, to separate the two libraries' rounding
- * (ULP-level parity of MathF.Exp / TensorPrimitives.Sigmoid is unpinned)
- * from everything else. */
-static int g_exp_double_rounded = 0;
-void orc_set_exp_double_rounded(int on) { g_exp_double_rounded = on; }
-static float orc_expf(float x) { return g_exp_double_rounded ? (float)exp((double)x) : expf(x); }
+ * expf (glibc's ARM optimized-routines expf on Linux). */
+static float orc_expf(float x) { return expf(x); }
+
+/* MathF.Exp over an array (test helper for the device exp). */
+void orc_expf_array(const float *x, float *y, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}
 
 /* Runtime/CachedAttentionKernel.cs:342-390 (Dot, AVX2 branch): two 8-lane
  * accumulators over 16-wide steps, then Vector256.Sum(acc0 + acc1).  The lane

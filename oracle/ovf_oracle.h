@@ -127,7 +127,7 @@ float orc_q8kv_quantize(const float *src, int n, int8_t *dst);
 void orc_attention_single_head_q8(const float *q, const int8_t *kq, const float *ks, const int8_t *vq,
                                   const float *vs, float *out, float *scratch, int seq_len, int hd, float scale);
 /* Test switch: exp rounded once from double precision (as on the GPU). */
-void orc_set_exp_double_rounded(int on);
+void orc_expf_array(const float *x, float *y, int64_t n);
 int  orc_session_position(const orc_session *s);
 /* One token through the stack; writes logits[vocab] when logits != NULL. */
 int  orc_session_decode(orc_session *s, int token, float *logits);

@@ -20,6 +20,7 @@ OVF_ENCCL = -4
 OVF_ETIMEDOUT = -5
 OVF_ESTATE = -6
 OVF_EUNSUPPORTED = -7
+OVF_EBUSY = -8
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 8, 12, 14
 TENSORS_PER_LAYER = 14
@@ -68,6 +69,8 @@ SIGNATURES = {
     "ovf_requant_q8_0": (I32, [I32, P, I64, I64, P, P, P]),
     "ovf_rmsnorm": (I32, [P, P, P, I64, F, P]),
     "ovf_rope_apply": (I32, [P, I32, I32, P, P, I32, P]),
+    "ovf_exp_f32": (I32, [P, P, I64, P]),
+    "ovf_swiglu": (I32, [P, P, P, I64, P]),
     "ovf_attention_scratch_bytes": (I64, [I32, I32, I32]),
     "ovf_attention_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P, P, P]),
     "ovf_attention_decode_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
@@ -118,7 +121,7 @@ def check(status: int, what: str = "") -> None:
     msg = f"{what}: {last_error()}" if what else last_error()
     if status == OVF_EINVAL:
         raise ValueError(msg)  # the reference's ArgumentException
-    if status == OVF_ESTATE:
+    if status in (OVF_ESTATE, OVF_EBUSY):
         raise OverfitRuntimeError(msg)
     if status == OVF_ENOMEM:
         raise MemoryError(msg)

@@ -245,6 +245,17 @@ ovf_status ovf_rmsnorm(const float *x, const float *gamma, float *y, int64_t d, 
     return launch_rmsnorm(x, gamma, y, d, eps, S(stream));
 }
 
+ovf_status ovf_exp_f32(const float *x, float *y, int64_t n, void *stream) {
+    OVF_CHECK_ARG(n >= 0 && (n == 0 || (x && y)), "Exp: bad arguments");
+    return launch_exp(x, y, n, S(stream));
+}
+
+ovf_status ovf_swiglu(const float *gate, const float *up, float *h, int64_t n, void *stream) {
+    OVF_CHECK_ARG(n >= 0 && (n == 0 || (gate && up && h)), "ApplySiLU: bad arguments");
+    if (n == 0) return OVF_OK;
+    return launch_silu_mul(gate, up, h, n, S(stream), false);
+}
+
 ovf_status ovf_rope_apply(float *v, int32_t n_vec, int32_t head_dim, const float *cos_row, const float *sin_row,
                           int32_t split_half, void *stream) {
     OVF_CHECK_ARG(head_dim > 0 && head_dim % 2 == 0, "RopeKernel.Apply: headDimension must be positive and even");

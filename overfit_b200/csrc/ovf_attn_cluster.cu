@@ -296,14 +296,15 @@ size_t attn_cluster_smem(int G, int hd) {
 
 template <int GT, int HD>
 static cudaError_t launch_cluster_inst(const AttnParams &p, size_t smem, cudaStream_t st, bool pdl) {
-    static bool attr = false;
-    if (!attr) {
+    static PerDeviceOnce attr_once;
+    const int dev = current_device();
+    if (attr_once.pending(dev)) {
         cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel<GT, HD>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(attention_cluster_kernel<GT, HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr_once.mark(dev);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCNC, p.KVH, p.rows > 1 ? p.rows : 1);

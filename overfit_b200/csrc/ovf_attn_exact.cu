@@ -283,7 +283,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     cluster.sync();
     float gmax = -INFINITY;
     for (int r = 0; r < kExactCluster; ++r) gmax = fmaxf(gmax, cluster.map_shared_rank(red, r)[8]);
-    for (int t = t0 + tid; t < t1; t += kExactThreads) ex[t - t0] = exp_rn(fsub(ex[t - t0], gmax));
+    for (int t = t0 + tid; t < t1; t += kExactThreads) ex[t - t0] = exp_libm(fsub(ex[t - t0], gmax));
     cluster.sync();
 
     // 3. every CTA gathers all probabilities' numerators into its own shared
@@ -518,11 +518,12 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
     cudaError_t e = cudaSuccess;
 #define OVF_EXACT(HDV, Q)                                                                                      \
     do {                                                                                                       \
-        static bool attr_set = false;                                                                          \
-        if (!attr_set && smem > 48 * 1024) {                                                                   \
+        static PerDeviceOnce attr_once;                                                                        \
+        const int dev_ = current_device();                                                                     \
+        if (smem > 48 * 1024 && attr_once.pending(dev_)) {                                                     \
             e = cudaFuncSetAttribute(attention_exact_kernel<HDV, Q>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                      (int)attn_exact_smem_bytes(HDV, attn_exact_max_seq(HDV)));                \
-            attr_set = e == cudaSuccess;                                                                       \
+            if (e == cudaSuccess) attr_once.mark(dev_);                                                        \
         }                                                                                                      \
         if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, attention_exact_kernel<HDV, Q>, p);                 \
     } while (0)

@@ -9,9 +9,29 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
+
 #include "../../include/ovf.h"
 
 namespace ovf {
+
+// A per-device "already done" flag for one-time per-device set-up
+// (cudaFuncSetAttribute applies to the current device only).
+struct PerDeviceOnce {
+    std::atomic<bool> done[64] = {};
+    // True when the set-up still has to run on `dev`.
+    bool pending(int dev) const { return dev < 0 || dev >= 64 || !done[dev].load(std::memory_order_acquire); }
+    void mark(int dev) {
+        if (dev >= 0 && dev < 64) done[dev].store(true, std::memory_order_release);
+    }
+};
+
+inline int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+}
+
 
 // ------------------------------------------------------------ host status
 void set_error(const char *fmt, ...);
@@ -248,12 +268,58 @@ __device__ __forceinline__ float rms_scale(float sumsq, int d, float eps) {
     return fdiv(1.0f, sqrtf(fadd(fdiv(sumsq, (float)d), eps)));
 }
 
-// e^x for a float argument, rounded once from the double-precision exp: the
-// correctly rounded result but for rare near-ties.  The reference's
-// MathF.Exp is the host C library's expf, which returns the correctly
-// rounded value for all but a small fraction of inputs, so this agrees with
-// it far more often than the single-precision expf.
-__device__ __forceinline__ float exp_rn(float x) { return __double2float_rn(exp((double)x)); }
+// e^x for a float argument with the bits of the host C library's expf, which
+// is what the reference's MathF.Exp calls on Linux.  glibc (2.27 onwards)
+// and musl use the ARM optimized-routines single-precision exp (Szabolcs
+// Nagy, MIT / Apache-2.0 licence: glibc sysdeps/ieee754/flt-32/e_expf.c,
+// e_exp2f_data.c): in double precision, x*32/ln2 = k + r with k an integer
+// found by the round-to-nearest shift 1.5*2^52, 2^(k/32) built from a
+// 32-entry table tab[i] = bits(2^(i/32)) - (i << 47) plus k << 47, and
+// 2^(r/32) ~= C0 r^3 + C1 r^2 + C2 r + 1 with the published degree-3
+// coefficients; the double result is rounded to float once.  On x86-64 hosts
+// with FMA, glibc selects a build of that code compiled with FMA contraction,
+// so every a*b+c below is one fused multiply-add; compared over every float
+// with |x| < 88 this equals that host expf bit for bit (the unfused build
+// differs on two inputs), and the range tails follow the same code's
+// special cases (overflow to +inf above 0x1.62e42ep6, zero below
+// -0x1.9fe368p6, NaN propagated).
+// Read through the L1 data cache: lanes index it divergently, which the
+// constant cache would serialize.
+__device__ const unsigned long long kExp2Tab32[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+__device__ __forceinline__ float exp_libm(float x) {
+    if (!(fabsf(x) < 88.0f)) {
+        if (x != x) return x + x;
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+    const double shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0, c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0,
+                 c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double xd = (double)x;
+    double kd = __fma_rn(inv_ln2_n, xd, shift);
+    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __fma_rn(inv_ln2_n, xd, -kd);
+    unsigned long long t = __ldg(&kExp2Tab32[ki & 31]);
+    t += ki << 47;
+    const double s = __longlong_as_double((long long)t);
+    const double z = __fma_rn(c0, r, c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __fma_rn(c2, r, 1.0);
+    y = __fma_rn(z, r2, y);
+    y = __dmul_rn(y, s);
+    return __double2float_rn(y);
+}
 
 // Q8_K / Q8_0 element quantizer: clamp(round_half_even(x * inv), -127, 127).
 __device__ __forceinline__ int quant_elem(float x, float inv) {

@@ -775,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                     }
                 }
                 if (p.epi == EPI_SILU_PAIR) {
-                    const float sg = fdiv(1.0f, fadd(1.0f, exp_rn(-y[0])));
+                    const float sg = fdiv(1.0f, fadd(1.0f, exp_libm(-y[0])));
                     p.seg[0].out[row] = fmul(fmul(y[0], sg), y[1]);
                 } else {
                     float *out = p.seg[seg].out;
@@ -1037,13 +1037,13 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
                                   : bps == 4 ? gemv_kernel<false, 4>
                                              : gemv_kernel<false, 8>);
     const int ki = kq ? (bps == 1 ? 0 : 1) : (bps == 1 ? 2 : bps == 2 ? 3 : bps == 4 ? 4 : 5);
-    static bool attr_done[64][6] = {};
-    if (device < 64 && !attr_done[device][ki]) {
+    static PerDeviceOnce attr_once[6];
+    if (attr_once[ki].pending(device)) {
         cudaFuncAttributes fa{};
         OVF_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
         OVF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_optin(device) - (int)fa.sharedSizeBytes));
-        attr_done[device][ki] = true;
+        attr_once[ki].mark(device);
     }
     if (plan_out) *plan_out = GemvPlan{T, stages, warps, grid, smem};
     cudaError_t e = launch_pdl(kern, dim3(grid), dim3(warps * 32), smem, stream, pdl, p);

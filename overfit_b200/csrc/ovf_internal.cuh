@@ -111,6 +111,8 @@ ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float 
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
                         DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,
                         bool pdl);
+ovf_status launch_take_error(int *dev_slot, cudaStream_t st);
+ovf_status launch_exp(const float *x, float *y, int64_t n, cudaStream_t st);
 ovf_status launch_silu_mul(const float *g, const float *u, float *h, int64_t n, cudaStream_t st, bool pdl);
 
 }  // namespace ovf

@@ -15,6 +15,7 @@
 //   GEMV  rmsnorm | lm head -> logits + argmax     final norm, ProjectLogits, TokenSampler.ArgMax
 // The argmax is fed back on the device, so greedy generation replays the
 // graph with no host round trip.
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -59,12 +60,14 @@ struct ovf_model {
     int16_t *bab = nullptr;
     int32_t *btok = nullptr, *bargmax = nullptr;
     int32_t *btok_host = nullptr;  // pinned
+    std::atomic<bool> batch_busy{false};  // one ovf_session_decode_batch at a time per model
 };
 
 struct ovf_session {
     ovf_model *m = nullptr;
     int max_ctx = 0;
     int pos = 0;           // host mirror of DevStep::next_pos
+    bool needs_reset = false;  // a batch call failed after touching this session's state
     int n_logits = 0;      // host mirror of DevStep::n_generated
     cudaStream_t stream = nullptr;
     int kv_dtype = OVF_KV_F32;
@@ -74,6 +77,7 @@ struct ovf_session {
           *gtmp = nullptr, *utmp = nullptr, *logits = nullptr, *rope_cos = nullptr, *rope_sin = nullptr,
           *partial = nullptr;
     int *counters = nullptr, *tokens_log = nullptr;
+    int *err_slot = nullptr;  // device word the error word is moved into after a call
     float *norm_s = nullptr;  // [0]: RMSNorm scale of hidden, [1]: of after
     TraceSlot *trace = nullptr;  // OVF_TRACE=1: per-launch timeline of the last step
     int trace_cap = 0, trace_n = 0;
@@ -1038,6 +1042,7 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     }
     A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
     A((void **)&s->step, sizeof(DevStep));
+    A((void **)&s->err_slot, sizeof(int));
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
     if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
     if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
@@ -1078,13 +1083,34 @@ ovf_status ovf_session_reset(ovf_session *s) {
     OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
     s->pos = 0;
     s->n_logits = 0;
+    s->needs_reset = false;
     return OVF_OK;
 }
 
 int32_t ovf_session_position(const ovf_session *s) { return s ? s->pos : -1; }
 
+// Ends a synchronous call: moves the device error word into `slot` (read and
+// cleared in one atomic step, after the call's kernels), waits for the stream
+// and reports a bounded wait that gave up as OVF_ETIMEDOUT.
+static ovf_status finish_call(cudaStream_t st, int *slot) {
+    ovf_status r = launch_take_error(slot, st);
+    if (r) return r;
+    int code = 0;
+    OVF_CUDA_TRY(cudaMemcpyAsync(&code, slot, sizeof(int), cudaMemcpyDeviceToHost, st));
+    OVF_CUDA_TRY(cudaStreamSynchronize(st));
+    if (code) {
+        set_error("device wait timed out (code %d)", code);
+        return OVF_ETIMEDOUT;
+    }
+    return OVF_OK;
+}
+
 static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host, int32_t *argmax_out) {
     OVF_CHECK_ARG(s, "decode: null session");
+    if (s->needs_reset) {
+        set_error("session state is undefined after a failed batch call; call ovf_session_reset");
+        return OVF_ESTATE;
+    }
     OVF_CHECK_ARG(n >= 0 && (n == 0 || tokens), "decode: bad token array");
     OVF_CHECK_ARG(s->pos + n <= s->max_ctx, "KV cache is full (ContextLength=%d, position %d, %d new tokens)", s->max_ctx,
                   s->pos, n);
@@ -1120,14 +1146,7 @@ static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, 
     if (logits_host)
         OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, s->logits, (size_t)s->m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s->stream));
     if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, &s->step->token, 4, cudaMemcpyDeviceToHost, s->stream));
-    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
-    int code = 0;
-    cudaMemcpyFromSymbol(&code, g_dev_error, sizeof(int));
-    if (code) {
-        set_error("device wait timed out (code %d)", code);
-        return OVF_ETIMEDOUT;
-    }
-    return OVF_OK;
+    return finish_call(s->stream, s->err_slot);
 }
 
 ovf_status ovf_session_decode(ovf_session *s, int32_t token, float *logits_host, int32_t *argmax_out) {
@@ -1150,8 +1169,7 @@ ovf_status ovf_session_generate_greedy(ovf_session *s, int32_t n_steps, int32_t 
         if (r) return r;
     }
     OVF_CUDA_TRY(cudaMemcpyAsync(tokens_out, s->tokens_log + first, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s->stream));
-    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
-    return OVF_OK;
+    return finish_call(s->stream, s->err_slot);
 }
 
 void *ovf_session_stream(const ovf_session *s) { return s ? (void *)s->stream : nullptr; }
@@ -1169,6 +1187,20 @@ ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, con
         OVF_CHECK_ARG(s->pos + 1 <= s->max_ctx, "KV cache is full (ContextLength=%d) in session %d", s->max_ctx, i);
         OVF_CHECK_ARG(tokens[i] >= 0 && tokens[i] < m->cfg.vocab, "token id %d out of range", tokens[i]);
     }
+    for (int i = 0; i < n; ++i)
+        if (sessions[i]->needs_reset) {
+            set_error("decode batch: session %d needs ovf_session_reset after a failed batch call", i);
+            return OVF_ESTATE;
+        }
+    bool idle = false;
+    if (!m->batch_busy.compare_exchange_strong(idle, true)) {
+        set_error("decode batch: another batch call on this model is in flight");
+        return OVF_EBUSY;
+    }
+    struct BusyRelease {
+        std::atomic<bool> &f;
+        ~BusyRelease() { f.store(false); }
+    } busy_release{m->batch_busy};
     DeviceGuard guard(m->device);
     ovf_status r = batch_alloc(m);
     if (r) return r;
@@ -1176,7 +1208,12 @@ ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, con
     const cudaStream_t st = sessions[0]->stream;
     memcpy(m->btok_host, tokens, (size_t)n * 4);
     OVF_CUDA_TRY(cudaMemcpyAsync(m->btok, m->btok_host, (size_t)n * 4, cudaMemcpyHostToDevice, st));
-    if ((r = enqueue_batch_decode(m, sessions, n, st))) return r;
+    if ((r = enqueue_batch_decode(m, sessions, n, st))) {
+        // some sessions may already have appended K/V rows or advanced their
+        // device step: their state no longer matches `pos`
+        for (int i = 0; i < n; ++i) sessions[i]->needs_reset = true;
+        return r;
+    }
     for (int i = 0; i < n; ++i) {
         sessions[i]->pos += 1;
         sessions[i]->n_logits += 1;
@@ -1184,14 +1221,7 @@ ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, con
     if (logits_host)
         OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, m->blogits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
     if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->bargmax, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
-    OVF_CUDA_TRY(cudaStreamSynchronize(st));
-    int code = 0;
-    cudaMemcpyFromSymbol(&code, g_dev_error, sizeof(int));
-    if (code) {
-        set_error("device wait timed out (code %d)", code);
-        return OVF_ETIMEDOUT;
-    }
-    return OVF_OK;
+    return finish_call(st, sessions[0]->err_slot);
 }
 
 }  // extern "C"

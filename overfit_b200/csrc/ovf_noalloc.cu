@@ -15,6 +15,8 @@
 // streams, or two host threads) race with each other.  The array's address
 // is looked up once per device, on that device's first call (see below), so
 // make the first call before any stream capture begins.
+#include <mutex>
+
 #include "ovf_internal.cuh"
 
 namespace ovf {
@@ -27,12 +29,17 @@ static constexpr size_t kNoAllocCounterInts = 256;          // one per KV head
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPartialBytes + kNoAllocCounterInts * 4];
 
 static void *g_noalloc_addr[64] = {nullptr};
+static std::mutex g_noalloc_mu;
 
-// Once per device, with that device current.
+// Once per device, with that device current; host threads making their first
+// call at the same time serialize on the mutex.  The cached address belongs to
+// the device's primary context: after cudaDeviceReset the library (models,
+// sessions and this address alike) must not be used on that device again.
 static ovf_status noalloc_scratch_address(void **out) {
     int dev = 0;
     OVF_CUDA_TRY(cudaGetDevice(&dev));
     OVF_CHECK_ARG(dev >= 0 && dev < 64, "attention (no-alloc): device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (!g_noalloc_addr[dev]) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);

@@ -503,10 +503,32 @@ __global__ void silu_mul_kernel(const float *g, const float *u, float *h, int64_
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
         const float x = g[i];
-        const float sg = fdiv(1.0f, fadd(1.0f, exp_rn(-x)));
+        const float sg = fdiv(1.0f, fadd(1.0f, exp_libm(-x)));
         h[i] = fmul(fmul(x, sg), u[i]);
     }
     pdl_launch_dependents();
+}
+
+// Reads and clears the device error word in one atomic step, ordered on a
+// stream after the work whose waits may have set it.
+__global__ void take_error_kernel(int *out) { *out = atomicExch(&g_dev_error, 0); }
+
+ovf_status launch_take_error(int *dev_slot, cudaStream_t st) {
+    take_error_kernel<<<1, 1, 0, st>>>(dev_slot);
+    return cuda_status(cudaGetLastError(), "take_error");
+}
+
+// MathF.Exp elementwise (exp_libm), for callers and tests of the exp itself.
+__global__ void exp_kernel(const float *x, float *y, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = exp_libm(x[i]);
+}
+
+ovf_status launch_exp(const float *x, float *y, int64_t n, cudaStream_t st) {
+    if (n == 0) return OVF_OK;
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+    exp_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, y, n);
+    return cuda_status(cudaGetLastError(), "exp");
 }
 
 ovf_status launch_silu_mul(const float *g, const float *u, float *h, int64_t n, cudaStream_t st, bool pdl) {

@@ -321,6 +321,17 @@ def rms_normalize(input, gamma, output, eps) -> None:
           "RmsNormalize")
 
 
+def exp(input: torch.Tensor, output: torch.Tensor) -> None:
+    """MathF.Exp elementwise, with the host C library's expf bits."""
+    check(_lib.load().ovf_exp_f32(_ptr(input), _ptr(output), input.numel(), _stream()), "MathF.Exp")
+
+
+def apply_swiglu(gate: torch.Tensor, up: torch.Tensor, output: torch.Tensor) -> None:
+    """ApplySiLU then Multiply (Runtime/CachedFeedForwardBlock.cs:464-472, :309):
+    output = gate * sigmoid(gate) * up."""
+    check(_lib.load().ovf_swiglu(_ptr(gate), _ptr(up), _ptr(output), gate.numel(), _stream()), "ApplySiLU")
+
+
 def rope_apply(vectors: torch.Tensor, cos_row: torch.Tensor, sin_row: torch.Tensor, split_half: bool) -> None:
     """RopeKernel.Apply (Rope/RopeKernel.cs:46-93) on [n_vec x head_dim], in place."""
     n_vec, hd = vectors.shape

@@ -344,7 +344,7 @@ def test_attention_exact_f32(K, orc, H, KVH, hd, seq):
                                           (8, 2, 256, 33)])
 def test_attention_q8_cache_bit_exact(K, orc, H, KVH, hd, seq):
     """Q8 KV cache (Q8KvQuant vectors) attended in ComputeSingleHeadQ8's order
-    vs the restatement with its exp rounded like the GPU's: bit-identical."""
+    vs the restatement: bit-identical."""
     rng = np.random.default_rng(seq * 3 + hd)
     max_ctx = seq + 5
     kf = rng.normal(0, 1, (KVH, max_ctx, hd)).astype(np.float32)
@@ -361,13 +361,9 @@ def test_attention_q8_cache_bit_exact(K, orc, H, KVH, hd, seq):
     K.CachedAttentionKernel.compute_single_head_q8_all(dev(q), dev(kq), dev(ks), dev(vq), dev(vs), out, H, KVH, hd,
                                                        seq, scale)
     got = host(out).reshape(H, hd)
-    orc.set_exp_double_rounded(True)
-    try:
-        G = H // KVH
-        ref = np.stack([orc.attention_single_head_q8(q[h], kq[h // G, :seq], ks[h // G, :seq], vq[h // G, :seq],
-                                                     vs[h // G, :seq], scale) for h in range(H)])
-    finally:
-        orc.set_exp_double_rounded(False)
+    G = H // KVH
+    ref = np.stack([orc.attention_single_head_q8(q[h], kq[h // G, :seq], ks[h // G, :seq], vq[h // G, :seq],
+                                                 vs[h // G, :seq], scale) for h in range(H)])
     np.testing.assert_array_equal(got, ref)
 
 
@@ -394,3 +390,36 @@ def test_attention_close(K, orc, H, KVH, hd, seq):
         rel = np.linalg.norm(got[h] - ref) / max(np.linalg.norm(ref), 1e-30)
         assert rel < 1e-5, (h, rel)
     assert not host(counters).any()  # counters are left zero for the next call
+
+
+# ------------------------------------------------------------ exp and SiLU
+def test_exp_matches_host_expf_exhaustively(K, orc):
+    """The device exp against the host C library's expf (MathF.Exp) on every
+    float32 bit pattern: identical bits, NaNs compared as NaN."""
+    chunk = 1 << 28
+    x = torch.empty(chunk, dtype=torch.float32, device="cuda")
+    y = torch.empty_like(x)
+    for c in range(1 << 32 >> 28):
+        bits = torch.arange(c * chunk, (c + 1) * chunk, dtype=torch.int64, device="cuda")
+        x.copy_((bits - (bits >= (1 << 31)).to(torch.int64) * (1 << 32)).to(torch.int32).view(torch.float32))
+        del bits
+        K.exp(x, y)
+        xh = host(x)
+        got = host(y).view(np.uint32)
+        ref = orc.expf_array(xh).view(np.uint32)
+        nan = np.isnan(xh)
+        bad = np.flatnonzero((got != ref) & ~nan)
+        assert bad.size == 0, (c, xh[bad[:8]], got[bad[:8]], ref[bad[:8]])
+        assert np.isnan(host(y)[nan]).all()
+
+
+def test_swiglu_bit_exact(K, orc):
+    """ApplySiLU(g) * u against the restatement over a wide argument range."""
+    rng = np.random.default_rng(5)
+    g = np.concatenate([rng.normal(0, 3, 1 << 20), rng.uniform(-120, 120, 1 << 16),
+                        [0.0, -0.0, 88.0, -88.0, 89.0, -104.0, 1e-30]]).astype(np.float32)
+    u = rng.normal(0, 1, g.size).astype(np.float32)
+    out = torch.empty(g.size, device="cuda")
+    K.apply_swiglu(dev(g), dev(u), out)
+    ref = orc.silu(g.copy()) * u
+    np.testing.assert_array_equal(host(out), ref)
