@@ -51,6 +51,8 @@ def parse():
                     help="KV cache of the timed session: f16 (the benchmark config) or f32 (the reference's default, "
                          "bit-exact attention)")
     ap.add_argument("--no-f32-line", action="store_true", help="skip the extra F32-KV (exact) measurement")
+    ap.add_argument("--profile-target", default=None, choices=sorted(PROFILE_TARGETS),
+                    help="run only a few launches of one kernel on a small case (for ncu captures) and exit")
     return ap.parse_args()
 
 
@@ -421,8 +423,70 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+# ------------------------------------------------------- profile targets
+def _prof_attn(kv: str):
+    """3 warm-up + 3 timed launches of the exact decode attention at the
+    Llama-3-8B layout (32 query / 8 KV heads, hd 128) over 2048 cached
+    positions."""
+    import torch
+
+    from overfit_b200 import build
+    from overfit_b200.kernels import CachedAttentionKernel as A
+
+    build.build()
+    H, KVH, hd, seq = 32, 8, 128, 2048
+    dt = torch.float16 if kv == "f16" else torch.float32
+    g = torch.Generator(device="cuda").manual_seed(0)
+    kc = torch.randn(KVH, seq, hd, device="cuda", generator=g).to(dt)
+    vc = torch.randn(KVH, seq, hd, device="cuda", generator=g).to(dt)
+    q = torch.randn(H * hd, device="cuda", generator=g)
+    out = torch.empty(H * hd, device="cuda")
+    fn = A.compute_single_head_f16_all if kv == "f16" else A.compute_single_head_all
+    for _ in range(6):
+        fn(q, kc, vc, out, H, KVH, hd, seq, 1.0 / hd ** 0.5)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_target": f"attn_exact_{kv}", "launches": 6}))
+
+
+def _prof_gemv_gateup():
+    """3 warm-up + 3 launches of the fused Q4_K gate/up GEMV (2 x 14336 x
+    4096), rotating over 8 weight pairs (264 MB, larger than L2)."""
+    import torch
+
+    from overfit_b200 import build
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight
+
+    build.build()
+    FF, D = 14336, 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ws = []
+    for _ in range(8):
+        a = GgmlQuant.quantize_q4_k(torch.randn(FF, D, device="cuda", generator=g) * 0.02, D, FF)
+        b = GgmlQuant.quantize_q4_k(torch.randn(FF, D, device="cuda", generator=g) * 0.02, D, FF)
+        ws.append((Q4KWeight(a, D, FF), Q4KWeight(b, D, FF)))
+    x = torch.randn(D, device="cuda", generator=g)
+    gy, uy = torch.empty(FF, device="cuda"), torch.empty(FF, device="cuda")
+    q = torch.empty(D, dtype=torch.int8, device="cuda")
+    s = torch.empty(D // 256, device="cuda")
+    bs = torch.empty(D // 16, dtype=torch.int16, device="cuda")
+    for i in range(6):
+        Q4KDotKernel.project_gate_up_parallel(x, ws[i % 8][0], ws[i % 8][1], gy, uy, q, s, bs)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_target": "gemv_gateup", "launches": 6}))
+
+
+PROFILE_TARGETS = {
+    "attn_exact_f16": lambda: _prof_attn("f16"),
+    "attn_exact_f32": lambda: _prof_attn("f32"),
+    "gemv_gateup": _prof_gemv_gateup,
+}
+
+
 def main():
     args = parse()
+    if args.profile_target:
+        PROFILE_TARGETS[args.profile_target]()
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -158,6 +158,13 @@ int64_t ovf_attention_scratch_bytes(int32_t n_heads, int32_t n_kv_heads, int32_t
 ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const float *v_cache, float *out,
                                      int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
                                      int32_t seq_len, float scale, void *stream);
+/* Runtime/CachedAttentionKernel.cs:36 ComputeSingleHead over fp16 caches
+ * [n_kv_heads x max_ctx x hd] (IEEE binary16, no reference counterpart: the
+ * F32 cache's values rounded to fp16): every value widens exactly to fp32 and
+ * the arithmetic is ComputeSingleHead's, bit for bit. */
+ovf_status ovf_attention_single_head_f16(const float *q, const void *k_cache, const void *v_cache, float *out,
+                                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
+                                         int32_t seq_len, float scale, void *stream);
 /* Runtime/CachedAttentionKernel.cs:139 ComputeSingleHeadQ8 for every query
  * head over a Q8 cache (Q8KvQuant per-vector int8 [n_kv_heads x max_ctx x hd]
  * + fp32 scales [n_kv_heads x max_ctx]), positions [0, seq_len): the
@@ -275,6 +282,43 @@ void *ovf_session_stream(const ovf_session *s);
  * OVF_ESTATE until ovf_session_reset. */
 ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, const int32_t *tokens,
                                     float *logits_host, int32_t *argmax_out);
+
+/* Session options.  OVF_OPT_PREFILL_SINGLE (value 0/1):
+ * CachedLlamaSession.DisableBatchedPrefillForParity (:808) — prompts take
+ * the single-token loop instead of the batched prefill (same results, bit
+ * for bit; for parity checks). */
+#define OVF_OPT_PREFILL_SINGLE 1
+ovf_status ovf_session_set_option(ovf_session *s, int32_t option, int32_t value);
+
+/* CachedLlamaSession.GenerateSpeculative's verify forward
+ * (Runtime/CachedLlamaSession.cs:468-477, PrefillBatchedQuantAllRows +
+ * ProjectLogitsBatched): n (1..64) tokens appended at positions pos.. in one
+ * batched forward, every row projected to logits with one read of the LM
+ * head.  Row j's logits are those a single-token decode of tokens[0..j]
+ * would give, bit for bit; the last row's become the session's logits.
+ * logits_host: [n x vocab] or NULL; argmax_out: [n] (first index of the
+ * max, the greedy acceptance test) or NULL. */
+ovf_status ovf_session_verify(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host,
+                              int32_t *argmax_out);
+/* KeyValueCache.TruncateTo (Runtime/KeyValueCache.cs:246) as
+ * CachedLlamaSession.RollbackTo (:318) uses it: the position becomes length
+ * (0 <= length <= position); rejected draft rows are dropped. */
+ovf_status ovf_session_truncate(ovf_session *s, int32_t length);
+/* Bytes of one side (keys or values) of a prefix snapshot at the current
+ * position: n_layers * n_kv_heads * position * head_dim * element size. */
+int64_t ovf_session_prefix_bytes(const ovf_session *s);
+/* CachedLlamaSession.SavePrefix (:231) -> KeyValueCache.Snapshot
+ * (Runtime/KeyValueCache.cs:264): the live rows packed
+ * [layer][kv_head][position][head_dim] into host buffers of
+ * ovf_session_prefix_bytes each, in the cache's element type (F32; fp16 for
+ * an fp16 cache).  A Q8 cache returns OVF_EUNSUPPORTED, as the reference's
+ * ThrowIfQuantized does. */
+ovf_status ovf_session_save_prefix(const ovf_session *s, void *keys, void *values, int32_t *length_out);
+/* CachedLlamaSession.RestorePrefix (:242) -> KeyValueCache.RestoreFrom
+ * (Runtime/KeyValueCache.cs:296): the packed rows of a snapshot from a
+ * session of the same model and cache type; the position becomes length and
+ * the session holds no logits until the next prefill or decode. */
+ovf_status ovf_session_restore_prefix(ovf_session *s, const void *keys, const void *values, int32_t length);
 
 #ifdef __cplusplus
 }

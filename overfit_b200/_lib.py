@@ -21,6 +21,7 @@ OVF_ETIMEDOUT = -5
 OVF_ESTATE = -6
 OVF_EUNSUPPORTED = -7
 OVF_EBUSY = -8
+OPT_PREFILL_SINGLE = 1
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 8, 12, 14
 TENSORS_PER_LAYER = 14
@@ -75,6 +76,7 @@ SIGNATURES = {
     "ovf_attention_decode": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P, P, P]),
     "ovf_attention_decode_noalloc": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_attention_single_head": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
+    "ovf_attention_single_head_f16": (I32, [P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_attention_single_head_q8": (I32, [P, P, P, P, P, P, I32, I32, I32, I32, I32, F, P]),
     "ovf_model_create": (I32, [I32, P, P, I32, P]),
     "ovf_model_destroy": (I32, [P]),
@@ -89,6 +91,12 @@ SIGNATURES = {
     "ovf_session_generate_greedy": (I32, [P, I32, P]),
     "ovf_session_stream": (P, [P]),
     "ovf_session_decode_batch": (I32, [P, I32, P, P, P]),
+    "ovf_session_set_option": (I32, [P, I32, I32]),
+    "ovf_session_verify": (I32, [P, P, I32, P, P]),
+    "ovf_session_truncate": (I32, [P, I32]),
+    "ovf_session_prefix_bytes": (I64, [P]),
+    "ovf_session_save_prefix": (I32, [P, P, P, P]),
+    "ovf_session_restore_prefix": (I32, [P, P, P, I32]),
 }
 
 _lib = None

@@ -308,6 +308,25 @@ ovf_status ovf_attention_single_head(const float *q, const float *k_cache, const
     return launch_attention_exact(p, seq_len, S(stream), false);
 }
 
+ovf_status ovf_attention_single_head_f16(const float *q, const void *k_cache, const void *v_cache, float *out,
+                                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx,
+                                         int32_t seq_len, float scale, void *stream) {
+    OVF_CHECK_ARG(q && k_cache && v_cache && out, "ComputeSingleHead (fp16 cache): null buffer");
+    OVF_CHECK_ARG(seq_len >= 1 && seq_len <= max_ctx, "ComputeSingleHead (fp16 cache): seq_len must be in [1, max_ctx]");
+    AttnParams p{};
+    p.q = q;
+    p.kc = (__half *)k_cache;
+    p.vc = (__half *)v_cache;
+    p.out = out;
+    p.H = n_heads;
+    p.KVH = n_kv_heads;
+    p.hd = head_dim;
+    p.max_ctx = max_ctx;
+    p.seq_len_host = seq_len;
+    p.scale = scale;
+    return launch_attention_exact(p, seq_len, S(stream), false, OVF_KV_F16);
+}
+
 ovf_status ovf_attention_single_head_q8(const float *q, const int8_t *k_cache, const float *k_scales,
                                         const int8_t *v_cache, const float *v_scales, float *out, int32_t n_heads,
                                         int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx, int32_t seq_len,
@@ -328,7 +347,7 @@ ovf_status ovf_attention_single_head_q8(const float *q, const int8_t *k_cache, c
     p.max_ctx = max_ctx;
     p.seq_len_host = seq_len;
     p.scale = scale;
-    return launch_attention_exact(p, seq_len, S(stream), false, true);
+    return launch_attention_exact(p, seq_len, S(stream), false, OVF_KV_Q8);
 }
 
 }  // extern "C"

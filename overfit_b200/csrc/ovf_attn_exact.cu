@@ -64,13 +64,17 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 int attn_exact_max_seq(int) { return kExactMaxSeq; }
 
-// Q8 = true: the reference's Q8 KV cache (KvCacheDType.Q8, per-vector int8
-// + one fp32 scale, Runtime/Q8KvQuant.cs) attended in ComputeSingleHeadQ8's
-// order (Runtime/CachedAttentionKernel.cs:139-235): score = DotF32I8(q, kQ)
-// * keyScale * scale, out[d] += (p * invSum * valueScale) * vQ[d].
-template <int HD, bool Q8>
+// KT = OVF_KV_Q8: the reference's Q8 KV cache (KvCacheDType.Q8, per-vector
+// int8 + one fp32 scale, Runtime/Q8KvQuant.cs) attended in
+// ComputeSingleHeadQ8's order (Runtime/CachedAttentionKernel.cs:139-235):
+// score = DotF32I8(q, kQ) * keyScale * scale, out[d] += (p * invSum *
+// valueScale) * vQ[d].  KT = OVF_KV_F16: the cache holds K/V rounded to fp16
+// (half the bytes of F32) and every value read widens exactly to fp32, so the
+// arithmetic is ComputeSingleHead's on the rounded cache.
+template <int HD, int KT>
 __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactThreads)
     attention_exact_kernel(const AttnParams p) {
+    constexpr bool Q8 = KT == OVF_KV_Q8, F16 = KT == OVF_KV_F16, RAW = Q8 || F16;
     extern __shared__ __align__(16) float esm[];
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
@@ -88,9 +92,11 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     const float *vf = reinterpret_cast<const float *>(p.vc) + (size_t)g * p.max_ctx * HD;
     const int8_t *k8 = reinterpret_cast<const int8_t *>(p.kc) + (size_t)g * p.max_ctx * HD;
     const int8_t *v8 = reinterpret_cast<const int8_t *>(p.vc) + (size_t)g * p.max_ctx * HD;
+    const __half *k16 = p.kc + (size_t)g * p.max_ctx * HD;
+    const __half *v16 = p.vc + (size_t)g * p.max_ctx * HD;
     const float *ksc = Q8 ? p.ks + (size_t)g * p.max_ctx : nullptr;
     const float *vsc = Q8 ? p.vs + (size_t)g * p.max_ctx : nullptr;
-    constexpr int EB = Q8 ? 1 : 4;  // bytes per cached element
+    constexpr int EB = Q8 ? 1 : F16 ? 2 : 4;  // bytes per cached element
 
     // the next projections' weights do not depend on this kernel: pull them
     // into L2 while the (latency-bound) attention runs
@@ -131,18 +137,21 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     // global reads stay coalesced along d)
     // (Q8: raw int8 rows [kVBlock][DPC], 4-byte pieces)
     constexpr int NE = kVBlock * DPC / kExactThreads;
-    constexpr int NE8 = (kVBlock * DPC / 4 + kExactThreads - 1) / kExactThreads;
+    constexpr int NE8 = (kVBlock * DPC * EB / 4 + kExactThreads - 1) / kExactThreads;
     auto stage_values = [&](int blk) {
         if (blk < nblk) {
             float *dst = vbuf + (blk % NBUF) * kVRow * DPC;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
-            if (Q8) {
-                int8_t *d8 = reinterpret_cast<int8_t *>(dst);
+            if (RAW) {
+                // raw rows [kVBlock][DPC] of EB-byte elements, 4-byte pieces
+                constexpr int PPR = DPC * EB / 4;  // pieces per row
+                char *d8 = reinterpret_cast<char *>(dst);
+                const char *src = Q8 ? reinterpret_cast<const char *>(v8) : reinterpret_cast<const char *>(v16);
 #pragma unroll
                 for (int j = 0; j < NE8; ++j) {
-                    const int i = tid + j * kExactThreads, t = i / (DPC / 4), q4 = i % (DPC / 4);
-                    if (i < kVBlock * DPC / 4 && t < n)
-                        cp_async4(d8 + t * DPC + 4 * q4, v8 + (size_t)(tb + t) * HD + d0 + 4 * q4);
+                    const int i = tid + j * kExactThreads, t = i / PPR, q4 = i % PPR;
+                    if (i < kVBlock * PPR && t < n)
+                        cp_async4(d8 + (t * DPC) * EB + 4 * q4, src + ((size_t)(tb + t) * HD + d0) * EB + 4 * q4);
                 }
             } else {
 #pragma unroll
@@ -169,6 +178,15 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
         const float *c = p.rope_cos + (size_t)pos * (HD / 2), *s = p.rope_sin + (size_t)pos * (HD / 2);
         rope_rotate(qs, HD, c, s, p.split_half, tid, kExactThreads);
         if (has_new) rope_rotate(kn, HD, c, s, p.split_half, tid, kExactThreads);
+        __syncthreads();
+    }
+    if (F16 && has_new) {
+        // the cache keeps the rotated key and the value rounded to fp16; the
+        // current token is attended from the same rounded values
+        for (int i = tid; i < HD; i += kExactThreads) {
+            kn[i] = __half2float(__float2half_rn(kn[i]));
+            vn[i] = __half2float(__float2half_rn(vn[i]));
+        }
         __syncthreads();
     }
     if (Q8 && has_new) {
@@ -211,6 +229,13 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
                 p.ks[(size_t)g * p.max_ctx + pos] = red[10];
                 p.vs[(size_t)g * p.max_ctx + pos] = red[11];
             }
+        } else if (F16) {
+            __half *kw = p.kc + ((size_t)g * p.max_ctx + pos) * HD;
+            __half *vw = p.vc + ((size_t)g * p.max_ctx + pos) * HD;
+            for (int i = tid; i < HD; i += kExactThreads) {
+                kw[i] = __float2half_rn(kn[i]);
+                vw[i] = __float2half_rn(vn[i]);
+            }
         } else {
             float *kw = reinterpret_cast<float *>(p.kc) + ((size_t)g * p.max_ctx + pos) * HD;
             float *vw = reinterpret_cast<float *>(p.vc) + ((size_t)g * p.max_ctx + pos) * HD;
@@ -240,6 +265,15 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
                 const int8_t *kr = (has_new && t == pos) ? kq8n : k8 + (size_t)(ok ? t : t0) * HD;
 #pragma unroll
                 for (int i = 0; i < HD / 16; ++i) kv[u][i] = (float)kr[16 * i + c];
+            } else if (F16) {
+                if (has_new && t == pos) {
+#pragma unroll
+                    for (int i = 0; i < HD / 16; ++i) kv[u][i] = kn[16 * i + c];
+                } else {
+                    const __half *kr = k16 + (size_t)(ok ? t : t0) * HD;
+#pragma unroll
+                    for (int i = 0; i < HD / 16; ++i) kv[u][i] = __half2float(kr[16 * i + c]);
+                }
             } else {
                 const float *kr = (has_new && t == pos) ? kn : kf + (size_t)(ok ? t : t0) * HD;
 #pragma unroll
@@ -359,6 +393,25 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
     for (int blk = 0; blk < nblk; ++blk) {
         cp_async_wait<NBUF - 1>();  // block blk has landed (this thread's part)
         __syncthreads();
+        if (F16 && tid < DPC && !bad) {
+            __half *vb16 = reinterpret_cast<__half *>(vbuf + (blk % NBUF) * kVRow * DPC) + tid;
+            const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
+            if (has_new && pos >= tb && pos < tb + n) vb16[(pos - tb) * DPC] = __float2half_rn(vn[d0 + tid]);
+            const float *pb = eall + tb;
+            int i = 0;
+#pragma unroll 1
+            for (; i + 16 <= n; i += 16) {
+                float pv[16], vv[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    pv[j] = pb[i + j];
+                    vv[j] = __half2float(vb16[(i + j) * DPC]);
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) acc = fadd(acc, fmul(pv[j], vv[j]));
+            }
+            for (; i < n; ++i) acc = fadd(acc, fmul(pb[i], __half2float(vb16[i * DPC])));
+        }
         if (Q8 && tid < DPC && !bad) {
             int8_t *vb8 = reinterpret_cast<int8_t *>(vbuf + (blk % NBUF) * kVRow * DPC) + tid;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
@@ -378,7 +431,7 @@ __global__ void __cluster_dims__(kExactCluster, 1, 1) __launch_bounds__(kExactTh
             }
             for (; i < n; ++i) acc = fadd(acc, fmul(pb[i], (float)vb8[i * DPC]));
         }
-        if (!Q8 && tid < DPC && !bad) {
+        if (!RAW && tid < DPC && !bad) {
             float *vb = vbuf + (blk % NBUF) * kVRow * DPC + tid * kVRow;
             const int tb = blk * kVBlock, n = min(kVBlock, seq - tb);
             // the current token's value was not in the cache when staged
@@ -497,7 +550,9 @@ ovf_status launch_kv_append_rows(const AttnParams &p, const float *k, const floa
 
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }
 
-ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8) {
+ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, int kv_dtype) {
+    const bool q8 = kv_dtype == OVF_KV_Q8;
+    OVF_CHECK_ARG(kv_dtype == OVF_KV_F32 || q8 || kv_dtype == OVF_KV_F16, "attention: unknown KV type %d", kv_dtype);
     OVF_CHECK_ARG(attn_exact_supported(p.hd), "attention: head_dim %d unsupported (32, 64, 128 or 256)", p.hd);
     OVF_CHECK_ARG(p.H > 0 && p.KVH > 0 && p.H % p.KVH == 0, "attention: n_heads must be a multiple of n_kv_heads");
     OVF_CHECK_ARG(!q8 || (p.ks && p.vs), "attention: Q8 cache without its scales");
@@ -528,11 +583,18 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
         if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, attention_exact_kernel<HDV, Q>, p);                 \
     } while (0)
     switch (p.hd) {
-        case 32: if (q8) OVF_EXACT(32, true); else OVF_EXACT(32, false); break;
-        case 64: if (q8) OVF_EXACT(64, true); else OVF_EXACT(64, false); break;
-        case 128: if (q8) OVF_EXACT(128, true); else OVF_EXACT(128, false); break;
-        default: if (q8) OVF_EXACT(256, true); else OVF_EXACT(256, false); break;
+#define OVF_EXACT_KT(HDV)                                                                                      \
+    do {                                                                                                       \
+        if (kv_dtype == OVF_KV_Q8) OVF_EXACT(HDV, OVF_KV_Q8);                                                  \
+        else if (kv_dtype == OVF_KV_F16) OVF_EXACT(HDV, OVF_KV_F16);                                           \
+        else OVF_EXACT(HDV, OVF_KV_F32);                                                                       \
+    } while (0)
+        case 32: OVF_EXACT_KT(32); break;
+        case 64: OVF_EXACT_KT(64); break;
+        case 128: OVF_EXACT_KT(128); break;
+        default: OVF_EXACT_KT(256); break;
     }
+#undef OVF_EXACT_KT
 #undef OVF_EXACT
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "attention_exact_kernel launch");
 }

@@ -89,10 +89,11 @@ ovf_status launch_attention(const AttnParams &p, cudaStream_t st, bool pdl);
 // ovf_attn_cluster.cu: cluster-merged variant used by the decode session.
 bool attn_cluster_supported(int G, int hd);
 ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool pdl);
-// ovf_attn_exact.cu: F32 cache, the reference's operation order (bit-exact).
+// ovf_attn_exact.cu: F32 / Q8 / fp16 caches in the reference's operation order (bit-exact on the cached values).
 bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);
-ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, bool q8 = false);
+ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl,
+                                  int kv_dtype = OVF_KV_F32);
 // RoPE + append of `rows` keys/values ([rows][KVH*hd] each) at positions
 // pos0 .. pos0+rows-1 into the cache of `p` (kv_dtype: OVF_KV_*), exactly as
 // the attention kernels append the token they decode.

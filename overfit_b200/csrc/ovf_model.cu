@@ -68,6 +68,7 @@ struct ovf_session {
     int max_ctx = 0;
     int pos = 0;           // host mirror of DevStep::next_pos
     bool needs_reset = false;  // a batch call failed after touching this session's state
+    bool prefill_single = false;  // DisableBatchedPrefillForParity
     int n_logits = 0;      // host mirror of DevStep::n_generated
     cudaStream_t stream = nullptr;
     int kv_dtype = OVF_KV_F32;
@@ -93,6 +94,9 @@ struct ovf_session {
     int8_t *paq = nullptr;
     int16_t *pab = nullptr;
     int32_t *ptok = nullptr;
+    // speculative verify: per-row logits and argmax of one verify batch
+    float *vlogits = nullptr;
+    int32_t *vargmax = nullptr;
     std::vector<void *> allocs;
 };
 
@@ -407,13 +411,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         }
         a.trace = tslot("attn");
         a.no_kv_prefetch = env_flag("OVF_ATTN_NOPF") ? 1 : 0;
-        if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
-            if ((r = launch_attention_exact(a, s->max_ctx, st, true, s->kv_dtype == OVF_KV_Q8))) return r;
-        } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
-            if ((r = launch_attention_cluster(a, st, true))) return r;
-        } else if ((r = launch_attention(a, st, true))) {
-            return r;
-        }
+        if ((r = launch_attention_exact(a, s->max_ctx, st, true, s->kv_dtype))) return r;
         prof_mark(st, "attn");
         {
             // Wo: per-head Q8_0 (G = hd/32 blocks per head), heads summed in
@@ -672,7 +670,7 @@ ovf_status rows_wo_ffn(const ovf_model *m, const DevLayer &L, const RowBufs &b, 
 // Enqueues the batched prefill of tokens [0, n) (already in s->ptok) at
 // positions s->pos ..; the last row's logits and argmax land where a decode
 // step's would.
-ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
+ovf_status enqueue_prefill_batched(ovf_session *s, int n, bool all_rows = false) {
     ovf_model *m = s->m;
     const ovf_model_config &c = m->cfg;
     const cudaStream_t st = s->stream;
@@ -698,44 +696,30 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
             if ((r = quantize_rows_for(ar, L.wv, s->pn, M, D, &fam, st))) return r;
             if ((r = project_rows(ar, L.wv, L.bv, s->pv, M, st))) return r;
             const size_t esz = s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
-            const bool exact = s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8;
-            const bool cluster = !exact && attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK");
-            // exact and cluster kernels: append every row's key/value first,
-            // then one launch attends all rows (each causal at its position)
-            const bool multi = (exact || cluster) && !env_flag("OVF_PREFILL_ATTN_PER_ROW");
-            for (int i = 0; i < (multi ? 1 : M); ++i) {
+            {
+                // every row's key and value are appended first, then one launch
+                // attends all rows (each causal at its own position)
                 AttnParams a{};
-                a.q = s->pq + (size_t)i * QD;
-                a.k_new = multi ? nullptr : s->pk + (size_t)i * KD;
-                a.v_new = multi ? nullptr : s->pv + (size_t)i * KD;
-                a.rows = multi ? M : 1;
+                a.q = s->pq;
+                a.rows = M;
                 a.kc = (__half *)((char *)s->kc + (size_t)l * KVH * s->max_ctx * hd * esz);
                 a.vc = (__half *)((char *)s->vc + (size_t)l * KVH * s->max_ctx * hd * esz);
                 if (s->kv_dtype == OVF_KV_Q8) {
                     a.ks = s->ks + (size_t)l * KVH * s->max_ctx;
                     a.vs = s->vs + (size_t)l * KVH * s->max_ctx;
                 }
-                a.out = s->patt + (size_t)i * QD;
+                a.out = s->patt;
                 a.rope_cos = s->rope_cos;
                 a.rope_sin = s->rope_sin;
-                a.pos_dev = nullptr;
-                a.seq_len_host = base + r0 + i + 1;
-                a.partial = s->partial;
-                a.counters = s->counters;
+                a.seq_len_host = base + r0 + 1;
                 a.split_half = c.rope_split_half;
                 a.H = H;
                 a.KVH = KVH;
                 a.hd = hd;
                 a.max_ctx = s->max_ctx;
                 a.scale = 1.0f / sqrtf((float)hd);
-                if (multi && (r = launch_kv_append_rows(a, s->pk, s->pv, M, base + r0, s->kv_dtype, st))) return r;
-                if (exact) {
-                    if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype == OVF_KV_Q8))) return r;
-                } else if (cluster) {
-                    if ((r = launch_attention_cluster(a, st, false))) return r;
-                } else if ((r = launch_attention(a, st, false))) {
-                    return r;
-                }
+                if ((r = launch_kv_append_rows(a, s->pk, s->pv, M, base + r0, s->kv_dtype, st))) return r;
+                if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) return r;
             }
             // Wo (Q8_0) per head, heads in order on the bias, + residual
             fam = 0;
@@ -753,6 +737,20 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n) {
             if ((r = quantize_rows_for(ar, L.down, s->ph, M, FF, &fam, st))) return r;
             if ((r = project_rows(ar, L.down, nullptr, s->px, M, st, 0, s->pa))) return r;
         }
+    }
+    if (all_rows) {
+        // every row of the (single) chunk to logits: final norm per row, the
+        // LM head over all rows with one read of its weights, argmax per row
+        // (CachedGptStack.ProjectLogitsBatched); the last row's logits and
+        // argmax become the session's, as after a decode step
+        int fam = 0;
+        if ((r = launch_rmsnorm_rows(s->px, m->final_norm, s->pn, n, D, c.eps, nullptr, st))) return r;
+        if ((r = quantize_rows_for(ar, m->lm_head, s->pn, n, D, &fam, st))) return r;
+        if ((r = project_rows(ar, m->lm_head, nullptr, s->vlogits, n, st))) return r;
+        if ((r = launch_argmax_rows(s->vlogits, n, c.vocab, s->vargmax, st))) return r;
+        OVF_CUDA_TRY(cudaMemcpyAsync(s->logits, s->vlogits + (size_t)(n - 1) * c.vocab, (size_t)c.vocab * 4,
+                                     cudaMemcpyDeviceToDevice, st));
+        return launch_batch_finish(s->step, base + n - 1, base + n, s->vargmax + n - 1, s->tokens_log, st);
     }
     // final norm + logits + argmax of the last prompt row
     const float *last = s->px + (size_t)(last_rows - 1) * D;
@@ -849,13 +847,7 @@ ovf_status enqueue_batch_decode(ovf_model *m, ovf_session *const *ss, int n, cud
             a.hd = hd;
             a.max_ctx = s->max_ctx;
             a.scale = 1.0f / sqrtf((float)hd);
-            if (s->kv_dtype == OVF_KV_F32 || s->kv_dtype == OVF_KV_Q8) {
-                if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype == OVF_KV_Q8))) return r;
-            } else if (attn_cluster_supported(H / KVH, hd) && !getenv("OVF_ATTN_SPLITK")) {
-                if ((r = launch_attention_cluster(a, st, false))) return r;
-            } else if ((r = launch_attention(a, st, false))) {
-                return r;
-            }
+            if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) return r;
         }
         if ((r = rows_wo_ffn(m, L, rb, n, st))) return r;
     }
@@ -997,11 +989,9 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     OVF_CHECK_ARG(max_ctx > 0 && max_ctx <= (1 << 20), "ovf_session_create: bad max_ctx");
     OVF_CHECK_ARG(kv_dtype == OVF_KV_F32 || kv_dtype == OVF_KV_Q8 || kv_dtype == OVF_KV_F16,
                   "ovf_session_create: unknown KV dtype %d", kv_dtype);
-    if (kv_dtype != OVF_KV_F16) {
-        OVF_CHECK_ARG(attn_exact_supported(m->cfg.head_dim), "ovf_session_create: head_dim %d unsupported",
-                      m->cfg.head_dim);
-        OVF_CHECK_ARG(max_ctx <= attn_exact_max_seq(m->cfg.head_dim), "ovf_session_create: max_ctx too large");
-    }
+    OVF_CHECK_ARG(attn_exact_supported(m->cfg.head_dim), "ovf_session_create: head_dim %d unsupported",
+                  m->cfg.head_dim);
+    OVF_CHECK_ARG(max_ctx <= attn_exact_max_seq(m->cfg.head_dim), "ovf_session_create: max_ctx too large");
     DeviceGuard guard(m->device);
     ovf_session *s = new ovf_session();
     s->m = m;
@@ -1120,7 +1110,7 @@ static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, 
     DeviceGuard guard(s->m->device);
     OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
     int done = 0;
-    if (n >= kPrefillThreshold && !env_flag("OVF_PREFILL_SINGLE")) {
+    if (n >= kPrefillThreshold && !s->prefill_single) {
         // the batched path (n <= max_ctx <= pinned_cap)
         ovf_status r = prefill_alloc(s);
         if (r) return r;
@@ -1222,6 +1212,136 @@ ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, con
         OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, m->blogits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, st));
     if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, m->bargmax, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
     return finish_call(st, sessions[0]->err_slot);
+}
+
+ovf_status ovf_session_set_option(ovf_session *s, int32_t option, int32_t value) {
+    OVF_CHECK_ARG(s, "set_option: null session");
+    switch (option) {
+        case OVF_OPT_PREFILL_SINGLE: s->prefill_single = value != 0; return OVF_OK;
+        default: OVF_CHECK_ARG(false, "set_option: unknown option %d", option);
+    }
+}
+
+// ------------------------------------------------ speculative verify / KV
+// CachedLlamaSession.GenerateSpeculativeCore's verify forward (:468-477):
+// the rows [t0, drafts...] through the batched stack at positions pos..,
+// every row to logits.  Each row's arithmetic is a decode step's, so row j's
+// logits equal those a single-token decode of tokens[0..j] would give.
+constexpr int kVerifyMax = 64;
+
+ovf_status ovf_session_verify(ovf_session *s, const int32_t *tokens, int32_t n, float *logits_host,
+                              int32_t *argmax_out) {
+    OVF_CHECK_ARG(s && tokens && n >= 1, "verify: bad arguments");
+    OVF_CHECK_ARG(n <= kVerifyMax, "verify: at most %d rows per call, got %d", kVerifyMax, n);
+    if (s->needs_reset) {
+        set_error("session state is undefined after a failed batch call; call ovf_session_reset");
+        return OVF_ESTATE;
+    }
+    OVF_CHECK_ARG(s->pos + n <= s->max_ctx, "KV cache is full (ContextLength=%d, position %d, %d new tokens)",
+                  s->max_ctx, s->pos, n);
+    for (int i = 0; i < n; ++i)
+        OVF_CHECK_ARG(tokens[i] >= 0 && tokens[i] < s->m->cfg.vocab, "token id %d out of range", tokens[i]);
+    DeviceGuard guard(s->m->device);
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    ovf_status r = prefill_alloc(s);
+    if (r) return r;
+    if (!s->vlogits) {
+        if ((r = dalloc(s->allocs, (void **)&s->vlogits, (size_t)kVerifyMax * s->m->cfg.vocab * 4))) return r;
+        if ((r = dalloc(s->allocs, (void **)&s->vargmax, (size_t)kVerifyMax * 4))) return r;
+    }
+    memcpy(s->pinned_tok, tokens, (size_t)n * 4);
+    OVF_CUDA_TRY(cudaMemcpyAsync(s->ptok, s->pinned_tok, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream));
+    if ((r = enqueue_prefill_batched(s, n, true))) {
+        s->needs_reset = true;
+        return r;
+    }
+    s->pos += n;
+    s->n_logits += 1;
+    if (logits_host)
+        OVF_CUDA_TRY(cudaMemcpyAsync(logits_host, s->vlogits, (size_t)n * s->m->cfg.vocab * 4, cudaMemcpyDeviceToHost,
+                                     s->stream));
+    if (argmax_out) OVF_CUDA_TRY(cudaMemcpyAsync(argmax_out, s->vargmax, (size_t)n * 4, cudaMemcpyDeviceToHost, s->stream));
+    return finish_call(s->stream, s->err_slot);
+}
+
+// KeyValueCache.TruncateTo (Runtime/KeyValueCache.cs:246-258) as
+// CachedLlamaSession.RollbackTo (:318) uses it: positions [length, pos) are
+// dropped; their stale rows are overwritten before they are read again.
+ovf_status ovf_session_truncate(ovf_session *s, int32_t length) {
+    OVF_CHECK_ARG(s, "TruncateTo: null session");
+    OVF_CHECK_ARG(length >= 0 && length <= s->pos, "TruncateTo %d must be in [0, CurrentLength=%d]", length, s->pos);
+    DeviceGuard guard(s->m->device);
+    ovf_status r = launch_set_step_pos(s->step, length > 0 ? length - 1 : 0, length, s->stream);
+    if (r) return r;
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    s->pos = length;
+    return OVF_OK;
+}
+
+static size_t kv_elem_bytes(const ovf_session *s) {
+    return s->kv_dtype == OVF_KV_F32 ? 4 : s->kv_dtype == OVF_KV_Q8 ? 1 : 2;
+}
+
+int64_t ovf_session_prefix_bytes(const ovf_session *s) {
+    if (!s) return -1;
+    const ovf_model_config &c = s->m->cfg;
+    return (int64_t)c.n_layers * c.n_kv_heads * s->pos * c.head_dim * (int64_t)kv_elem_bytes(s);
+}
+
+// KeyValueCache.Snapshot (Runtime/KeyValueCache.cs:264-289) via
+// CachedLlamaSession.SavePrefix (:231): the live rows [0, pos) of every
+// (layer, KV head), packed [layer][kv_head][pos][head_dim] into the caller's
+// host buffers (ovf_session_prefix_bytes each).  F32 (the reference's only
+// snapshot type) and fp16 caches; a Q8 cache is rejected as the reference's
+// ThrowIfQuantized does.
+ovf_status ovf_session_save_prefix(const ovf_session *s, void *keys, void *values, int32_t *length_out) {
+    OVF_CHECK_ARG(s && keys && values && length_out, "SavePrefix: null argument");
+    if (s->kv_dtype == OVF_KV_Q8) {
+        set_error("Snapshot is not supported for a quantized (Q8) KV cache");
+        return OVF_EUNSUPPORTED;
+    }
+    DeviceGuard guard(s->m->device);
+    const ovf_model_config &c = s->m->cfg;
+    const size_t esz = kv_elem_bytes(s), run = (size_t)s->pos * c.head_dim * esz,
+                 pitch = (size_t)s->max_ctx * c.head_dim * esz, lh = (size_t)c.n_layers * c.n_kv_heads;
+    *length_out = s->pos;
+    if (run == 0) return OVF_OK;
+    OVF_CUDA_TRY(cudaMemcpy2DAsync(keys, run, s->kc, pitch, run, lh, cudaMemcpyDeviceToHost, s->stream));
+    OVF_CUDA_TRY(cudaMemcpy2DAsync(values, run, s->vc, pitch, run, lh, cudaMemcpyDeviceToHost, s->stream));
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    return OVF_OK;
+}
+
+// KeyValueCache.RestoreFrom (Runtime/KeyValueCache.cs:296-327) via
+// CachedLlamaSession.RestorePrefix (:242): rows [0, length) of every
+// (layer, KV head) from a packed prefix of the same model and cache type;
+// the session's position becomes `length` (a copy, not a forward pass) and it
+// holds no logits until the next prefill / decode.
+ovf_status ovf_session_restore_prefix(ovf_session *s, const void *keys, const void *values, int32_t length) {
+    OVF_CHECK_ARG(s && (length == 0 || (keys && values)), "RestorePrefix: null argument");
+    if (s->kv_dtype == OVF_KV_Q8) {
+        set_error("RestoreFrom is not supported for a quantized (Q8) KV cache");
+        return OVF_EUNSUPPORTED;
+    }
+    OVF_CHECK_ARG(length >= 0 && length <= s->max_ctx, "Snapshot length %d exceeds cache MaxLength %d", length,
+                  s->max_ctx);
+    DeviceGuard guard(s->m->device);
+    const ovf_model_config &c = s->m->cfg;
+    const size_t esz = kv_elem_bytes(s), run = (size_t)length * c.head_dim * esz,
+                 pitch = (size_t)s->max_ctx * c.head_dim * esz, lh = (size_t)c.n_layers * c.n_kv_heads;
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    OVF_CUDA_TRY(cudaMemsetAsync(s->step, 0, sizeof(DevStep), s->stream));
+    if (run) {
+        OVF_CUDA_TRY(cudaMemcpy2DAsync(s->kc, pitch, keys, run, run, lh, cudaMemcpyHostToDevice, s->stream));
+        OVF_CUDA_TRY(cudaMemcpy2DAsync(s->vc, pitch, values, run, run, lh, cudaMemcpyHostToDevice, s->stream));
+    }
+    ovf_status r = launch_set_step_pos(s->step, length > 0 ? length - 1 : 0, length, s->stream);
+    if (r) return r;
+    OVF_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    s->pos = length;
+    s->n_logits = 0;
+    s->needs_reset = false;
+    return OVF_OK;
 }
 
 }  // extern "C"

@@ -155,6 +155,9 @@ class CudaLlamaSession:
         self._h = h
         self._logits = np.zeros(engine.cfg["vocab"], np.float32)
         self._have_logits = False
+        self._last_argmax = -1
+        self._spec_ema = 0.0      # committed tokens per verify (EMA); starts gated
+        self._spec_countdown = 0  # the first gated step probes
 
     @property
     def vocabulary_size(self) -> int:
@@ -175,7 +178,7 @@ class CudaLlamaSession:
         """CachedLlamaSession.Prefill; returns the greedy next token and keeps
         the last logits.  Prompts of 16 tokens or more take the batched path
         (PrefillBatchedQuant, bit-identical to the single-token loop, which
-        OVF_PREFILL_SINGLE=1 forces)."""
+        ``disable_batched_prefill_for_parity`` forces)."""
         toks = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32))
         if toks.size == 0:
             return -1
@@ -183,6 +186,7 @@ class CudaLlamaSession:
         check(_lib.load().ovf_session_prefill(self._h, toks.ctypes.data, toks.size, self._logits.ctypes.data,
                                               C.byref(am)), "Prefill")
         self._have_logits = True
+        self._last_argmax = am.value
         return am.value
 
     def decode(self, token: int, want_logits: bool = True) -> int:
@@ -191,6 +195,7 @@ class CudaLlamaSession:
         ptr = self._logits.ctypes.data if want_logits else None
         check(_lib.load().ovf_session_decode(self._h, int(token), ptr, C.byref(am)), "DecodeToken")
         self._have_logits = want_logits
+        self._last_argmax = am.value
         return am.value
 
     def generate_greedy(self, n_steps: int) -> np.ndarray:
@@ -202,6 +207,102 @@ class CudaLlamaSession:
         check(_lib.load().ovf_session_generate_greedy(self._h, n_steps, out.ctypes.data), "GenerateNextToken")
         self._have_logits = False
         return out
+
+    @property
+    def disable_batched_prefill_for_parity(self) -> bool:
+        """CachedLlamaSession.DisableBatchedPrefillForParity (:808)."""
+        return getattr(self, "_prefill_single", False)
+
+    @disable_batched_prefill_for_parity.setter
+    def disable_batched_prefill_for_parity(self, on: bool) -> None:
+        check(_lib.load().ovf_session_set_option(self._h, _lib.OPT_PREFILL_SINGLE, int(bool(on))), "set_option")
+        self._prefill_single = bool(on)
+
+    # ---------------------------------------------- speculative decoding
+    def verify(self, tokens, want_logits: bool = False):
+        """The speculative verify forward (GenerateSpeculativeCore :468-477):
+        appends `tokens` in one batched forward and returns the argmax of
+        every row (and the [n, vocab] logits when asked)."""
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        n = toks.size
+        am = np.empty(n, np.int32)
+        lg = np.empty((n, self.engine.cfg["vocab"]), np.float32) if want_logits else None
+        check(_lib.load().ovf_session_verify(self._h, toks.ctypes.data, n, None if lg is None else lg.ctypes.data,
+                                             am.ctypes.data), "Verify")
+        self._have_logits = False
+        return (am, lg) if want_logits else am
+
+    def rollback_to(self, length: int) -> None:
+        """CachedLlamaSession.RollbackTo (:318) -> KeyValueCache.TruncateTo."""
+        check(_lib.load().ovf_session_truncate(self._h, int(length)), "TruncateTo")
+        self._have_logits = False
+
+    def generate_speculative(self, history, max_draft: int = 4, ngram_min: int = 1, ngram_max: int = 3) -> list:
+        """Greedy GenerateSpeculative (Runtime/CachedLlamaSession.cs:335-530):
+        t0 = argmax of the current logits; prompt-lookup drafts from
+        history + [t0]; one batched verify of [t0, drafts...]; drafts are
+        accepted while they equal the verify row's argmax; the rejected
+        drafts' rows are rolled back and the correction (or bonus) token is
+        decoded so the session holds its logits.  Returns the committed tokens
+        (>= 1): greedy output identical to single-token steps.  The adaptive
+        gate (EMA of committed tokens per verify, probe every 64 steps) follows
+        the reference."""
+        if self.current_position == 0:
+            raise OverfitRuntimeError("Session is empty. Call Reset with a prompt first.")
+        if max_draft <= 0:
+            raise ValueError("maxDraft must be positive")
+        t0 = int(np.argmax(self.get_last_logits())) if self._have_logits else self._last_argmax
+        gated = self._spec_ema < 3.0
+        probe = False
+        if gated:
+            if self._spec_countdown > 0:
+                self._spec_countdown -= 1
+            else:
+                probe = True
+                self._spec_countdown = 64
+        draft = []
+        if not gated or probe:
+            draft = prompt_lookup_draft(list(history) + [t0], max_draft, ngram_min, ngram_max)
+        base = self.current_position
+        if not draft or base + 1 + len(draft) + 1 > self.max_context_length:
+            self._last_argmax = self.decode(t0)
+            return [t0]
+        am = self.verify([t0] + draft)
+        committed, accepted, correction = [t0], 0, -1
+        for j, d in enumerate(draft):
+            if int(am[j]) == d:
+                committed.append(d)
+                accepted += 1
+            else:
+                correction = int(am[j])
+                break
+        if correction < 0:
+            correction = int(am[len(draft)])
+        self.rollback_to(base + 1 + accepted)
+        committed.append(correction)
+        self._last_argmax = self.decode(correction)
+        self._spec_ema = 0.5 * len(committed) + 0.5 * self._spec_ema
+        return committed
+
+    # ---------------------------------------------------- prefix KV reuse
+    def save_prefix(self) -> dict:
+        """CachedLlamaSession.SavePrefix (:231): the live KV rows packed
+        [layer][kv_head][position][head_dim] (F32, or fp16 for an fp16 cache)."""
+        nbytes = int(_lib.load().ovf_session_prefix_bytes(self._h))
+        k = np.empty(max(nbytes, 1), np.uint8)
+        v = np.empty(max(nbytes, 1), np.uint8)
+        n = C.c_int32()
+        check(_lib.load().ovf_session_save_prefix(self._h, k.ctypes.data, v.ctypes.data, C.byref(n)), "SavePrefix")
+        return dict(keys=k[:nbytes], values=v[:nbytes], length=n.value, kv=self.kv_cache_dtype)
+
+    def restore_prefix(self, prefix: dict) -> None:
+        """CachedLlamaSession.RestorePrefix (:242): a copy, not a forward pass."""
+        if prefix["kv"] != self.kv_cache_dtype:
+            raise ValueError("Snapshot shape does not match this cache")
+        check(_lib.load().ovf_session_restore_prefix(self._h, prefix["keys"].ctypes.data,
+                                                     prefix["values"].ctypes.data, int(prefix["length"])),
+              "RestorePrefix")
+        self._have_logits = False
 
     @property
     def stream_handle(self) -> int:
@@ -223,6 +324,25 @@ class CudaLlamaSession:
             self.close()
         except Exception:
             pass
+
+
+def prompt_lookup_draft(history, max_draft: int, ngram_min: int = 1, ngram_max: int = 3) -> list:
+    """PromptLookupDrafter.Draft (Runtime/PromptLookupDrafter.cs:24-74): the
+    longest suffix n-gram (ngram_max down to ngram_min) matched against its
+    most recent earlier occurrence; proposes the tokens that followed it."""
+    if max_draft <= 0:
+        return []
+    if ngram_min <= 0:
+        raise ValueError("ngramMin must be positive")
+    ngram_max = max(ngram_max, ngram_min)
+    n_hist = len(history)
+    for n in range(min(ngram_max, n_hist - 1), ngram_min - 1, -1):
+        suffix = history[n_hist - n:]
+        for i in range(n_hist - n - 1, -1, -1):
+            if history[i:i + n] == suffix:
+                follow = i + n
+                return list(history[follow:follow + min(max_draft, n_hist - follow)])
+    return []
 
 
 # ------------------------------------------------------------- synthetic

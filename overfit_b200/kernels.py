@@ -356,6 +356,17 @@ class CachedAttentionKernel:
                                                     _stream()), "ComputeSingleHead")
 
     @staticmethod
+    def compute_single_head_f16_all(query, k_cache, v_cache, output, n_heads, n_kv_heads, head_dim, seq_len,
+                                    scale) -> None:
+        """ComputeSingleHead for every query head over fp16 caches
+        [n_kv_heads, max_ctx, hd] (float16 tensors): the reference's order on
+        the widened values (bit-identical)."""
+        max_ctx = k_cache.shape[1]
+        check(_lib.load().ovf_attention_single_head_f16(_ptr(query), _ptr(k_cache), _ptr(v_cache), _ptr(output),
+                                                        n_heads, n_kv_heads, head_dim, max_ctx, seq_len, float(scale),
+                                                        _stream()), "ComputeSingleHead")
+
+    @staticmethod
     def compute_single_head_q8_all(query, k_q, k_scales, v_q, v_scales, output, n_heads, n_kv_heads, head_dim,
                                    seq_len, scale) -> None:
         """ComputeSingleHeadQ8 (Runtime/CachedAttentionKernel.cs:139-200) for

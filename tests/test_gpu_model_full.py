@@ -11,8 +11,12 @@ with the reference's own exp (the host C library's expf, MathF.Exp).
   config's full prompt; the CPU restatement then needs minutes).
 
 Bar (north star): logits within 1e-2 relative L2 at every step and identical
-greedy tokens for 32 steps.  The F32 sessions are also required to be
-bit-identical, which is what the GPU path is built to be.
+greedy tokens for 32 steps.  Every session is also required to be
+bit-identical (the fp16 cache against the restatement with its cache rounded
+to fp16), which is what the GPU path is built to be: random-init models of
+this depth amplify a single differently rounded value into percent-level
+logit differences within a few hundred tokens, so only the reference's exact
+operation order holds the bar.
 
 Weights are N(0, 0.02) drawn on the device and quantized by the library's
 device encoders (bit-identical to the restatement's), then handed to both
@@ -99,6 +103,6 @@ def test_llama3_8b_shape_parity(E, orc, llama8b, kv):
     if kv == "f16":
         ref.set_kv_fp16(True)
     prompt = np.random.default_rng(2048).integers(0, cfg["vocab"], PROMPT_8B)
-    errs = run_parity(sess, ref, prompt, 32, exact=(kv == "f32"))
+    errs = run_parity(sess, ref, prompt, 32, exact=True)
     print(f"llama3-8b {kv} KV: max rel L2 {max(errs):.3g} over {len(errs)} steps")
     sess.close()
