@@ -445,7 +445,13 @@ def _prof_attn(kv: str):
     for _ in range(6):
         fn(q, kc, vc, out, H, KVH, hd, seq, 1.0 / hd ** 0.5)
     torch.cuda.synchronize()
-    print(json.dumps({"profile_target": f"attn_exact_{kv}", "launches": 6}))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        fn(q, kc, vc, out, H, KVH, hd, seq, 1.0 / hd ** 0.5)
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_target": f"attn_exact_{kv}", "launches": 26, "us_per_launch": e0.elapsed_time(e1) * 50}))
 
 
 def _prof_gemv_gateup():

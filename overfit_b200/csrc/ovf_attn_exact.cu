@@ -548,6 +548,16 @@ ovf_status launch_kv_append_rows(const AttnParams &p, const float *k, const floa
     return cuda_status(cudaGetLastError(), "kv_append_rows");
 }
 
+// OVF_ATTN_NO_GROUP=1 keeps every launch on the per-head kernel (same
+// results; for comparisons).
+static bool getenv_flag_cached_no_group() {
+    static const bool v = [] {
+        const char *e = getenv("OVF_ATTN_NO_GROUP");
+        return e && e[0] == '1';
+    }();
+    return v;
+}
+
 bool attn_exact_supported(int hd) { return hd == 32 || hd == 64 || hd == 128 || hd == 256; }
 
 ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStream_t st, bool pdl, int kv_dtype) {
@@ -558,6 +568,9 @@ ovf_status launch_attention_exact(const AttnParams &p, int seq_len_max, cudaStre
     OVF_CHECK_ARG(!q8 || (p.ks && p.vs), "attention: Q8 cache without its scales");
     OVF_CHECK_ARG(seq_len_max >= 1 && seq_len_max <= attn_exact_max_seq(p.hd),
                   "attention: sequence length %d outside [1, %d]", seq_len_max, attn_exact_max_seq(p.hd));
+    if (!getenv_flag_cached_no_group() &&
+        attn_group_supported(p.H, p.KVH, p.hd, kv_dtype, seq_len_max, smem_optin(current_device())))
+        return launch_attention_group(p, seq_len_max, st, pdl, kv_dtype);
     const size_t smem = (size_t)attn_exact_smem_bytes(p.hd, seq_len_max);
     cudaLaunchConfig_t cfg = {};
     OVF_CHECK_ARG(p.rows <= 1 || (p.k_new == nullptr && !p.pos_dev && p.rows <= 65535), "attention: bad row batch");

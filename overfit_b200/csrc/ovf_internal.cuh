@@ -89,6 +89,9 @@ ovf_status launch_attention(const AttnParams &p, cudaStream_t st, bool pdl);
 // ovf_attn_cluster.cu: cluster-merged variant used by the decode session.
 bool attn_cluster_supported(int G, int hd);
 ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool pdl);
+// ovf_attn_group.cu: F32 / fp16 caches, one cluster per KV head (exact order).
+bool attn_group_supported(int H, int KVH, int hd, int kv_dtype, int seq_cap, int smem_optin_bytes);
+ovf_status launch_attention_group(const AttnParams &p, int seq_cap, cudaStream_t st, bool pdl, int kv_dtype);
 // ovf_attn_exact.cu: F32 / Q8 / fp16 caches in the reference's operation order (bit-exact on the cached values).
 bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);

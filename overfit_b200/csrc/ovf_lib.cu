@@ -7,6 +7,7 @@
 #include "ovf_batched.cu"
 #include "ovf_ops.cu"
 #include "ovf_attn_cluster.cu"
+#include "ovf_attn_group.cu"
 #include "ovf_attn_exact.cu"
 #include "ovf_model.cu"
 #include "ovf_noalloc.cu"
