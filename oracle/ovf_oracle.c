@@ -523,8 +523,10 @@ void orc_q8_0_project_batched(const float *x, int64_t rows, const int8_t *wq, co
  * sequential over i. */
 void orc_f32_project_input_major(const float *x, const float *w, int64_t k, int64_t n, float *y) {
     for (int64_t e = 0; e < n; e++) y[e] = 0.0f;
-    for (int64_t i = 0; i < k; i++)
+    for (int64_t i = 0; i < k; i++) {
+        if (x[i] == 0.0f) continue; /* ProjectChunk skips zero inputs (:255-260) */
         for (int64_t e = 0; e < n; e++) y[e] = y[e] + x[i] * w[i * n + e];
+    }
 }
 
 /* ------------------------------------------------------------------ */

@@ -52,15 +52,6 @@ int64_t attn_exact_smem_bytes(int hd, int seq_len) {
     return (int64_t)(3 * hd + 16 + hd / 2 + bufs * kVRow * dpc + chunk + ((seq_len + 3) & ~3)) * 4 + 16;
 }
 
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gsrc) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 int attn_exact_max_seq(int) { return kExactMaxSeq; }
 

@@ -32,21 +32,43 @@ namespace ovf {
 
 namespace gcg = cooperative_groups;
 
+#ifdef OVF_PHASE_PROBE
+__device__ unsigned long long g_phase[16];
+#define OVF_PHASE(i) \
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) g_phase[i] = clock64()
+#else
+#define OVF_PHASE(i)
+#endif
+
 static constexpr int kGrpCluster = 16;
 static constexpr int kGrpThreads = 256;
-static constexpr int kGrpMaxHeads = 8;  // query heads per KV head held in registers while scoring
 
 struct GroupLayout {
-    int chunk_cap, sp_cap;  // per-CTA slice capacity and padded sequence capacity (multiples of 4)
-    int64_t floats;
+    int chunk_cap, sp_cap;  // per-CTA slice capacity and padded row stride (floats)
+    int64_t o_sc, o_eall, o_reg2, o_vraw, floats;  // offsets (floats) and total
 };
 
-__host__ __device__ inline GroupLayout group_layout(int G, int hd, int seq_cap) {
+// Shared memory (floats): qs [G][hd] | kn, vn [hd] | red [264] | exp table
+// [64] | sc [G][chunk] | eall [G][sp] | reg2: the key rows [chunk][hd] while
+// scoring, then vt [hd/16][sp] (fp32, or fp16 for an fp16 cache) | vraw
+// (fp16 cache only): the value columns [sp][hd/16] as cached.  About
+// 48 bytes per position for Llama-3-8B heads, so two CTAs fit an SM at a
+// 2K context and a 16-CTA cluster packs into a GPC.
+__host__ __device__ inline GroupLayout group_layout(int G, int hd, int seq_cap, int eb) {
     GroupLayout L;
     L.chunk_cap = (((seq_cap + kGrpCluster - 1) / kGrpCluster) + 3) & ~3;
-    L.sp_cap = (seq_cap + 3) & ~3;
+    // rows of the [heads][t] and [d][t] arrays start 4 banks apart (stride
+    // = 4 mod 32 floats), so lanes reading 8 rows at one t with 16-byte loads
+    // hit 32 distinct banks
+    L.sp_cap = (((seq_cap + 3) & ~3) + 31) / 32 * 32 + 4;
     const int dpc = hd / kGrpCluster;
-    L.floats = (int64_t)G * hd + 2 * hd + 128 + (int64_t)G * L.chunk_cap + (int64_t)G * L.sp_cap + (int64_t)dpc * L.sp_cap;
+    const int64_t kraw = ((int64_t)L.chunk_cap * hd * eb / 4 + 3) & ~int64_t(3);
+    const int64_t vt = (int64_t)dpc * L.sp_cap * eb / 4;
+    L.o_sc = (int64_t)G * hd + 2 * hd + 264 + 64;
+    L.o_eall = L.o_sc + (int64_t)G * L.chunk_cap;
+    L.o_reg2 = L.o_eall + (int64_t)G * L.sp_cap;
+    L.o_vraw = L.o_reg2 + (kraw > vt ? kraw : vt);
+    L.floats = L.o_vraw + (eb == 2 ? (((int64_t)L.sp_cap * dpc * eb / 4 + 3) & ~int64_t(3)) : 0);
     return L;
 }
 
@@ -95,53 +117,79 @@ __device__ __forceinline__ void load_cols(const void *src, float *dst) {
     }
 }
 
-template <int HD, int KT>
+// Async copy of n (4, 8 or a multiple of 16) bytes, 16 at a time.
+__device__ __forceinline__ void cp_async_n(char *dst, const char *src, int n) {
+    if (n >= 16) {
+        for (int o = 0; o < n; o += 16) cp_async16(dst + o, src + o);
+    } else if (n == 8) {
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    } else {
+        cp_async4(dst, src);
+    }
+}
+
+template <int HD, int KT, int GT>
 __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const AttnParams p, int seq_cap) {
     constexpr bool F16 = KT == OVF_KV_F16;
     constexpr int CL = kGrpCluster, DPC = HD / CL, NT = kGrpThreads, EB = F16 ? 2 : 4;
+    constexpr int G = GT;  // query heads of the KV head
     extern __shared__ __align__(16) float gsm[];
     gcg::cluster_group cluster = gcg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int g = blockIdx.x / CL, row = blockIdx.y;
-    const int G = p.H / p.KVH;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const GroupLayout GL = group_layout(G, HD, seq_cap);
+    const GroupLayout GL = group_layout(G, HD, seq_cap, EB);
     const int cc = GL.chunk_cap, spc = GL.sp_cap;
     float *qs = gsm;               // [G][HD]
     float *kn = qs + G * HD;       // [HD] current key (rotated)
     float *vn = kn + HD;           // [HD] current value
-    float *red = vn + HD;          // [128]: warp maxima [8][8] | local max [64..72) | max [96..104) | inv [80..88) | bad [88..96)
-    float *sc = red + 128;         // [G][cc] own slice: scores, then exponentials
-    float *eall = sc + G * cc;     // [G][spc] all exponentials, then probabilities
-    float *vt = eall + G * spc;    // [DPC][spc] this CTA's value columns, transposed
+    float *red = vn + HD;          // [264]: warp maxima [8][8] | inv [80..88) | bad [88..96) | max [96..104) |
+                                   //        every rank's maxima [128 + rank * G + h] | mbarrier at [256]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 256);
+    unsigned long long *etab = reinterpret_cast<unsigned long long *>(red + 264);
+    float *sc = gsm + GL.o_sc;     // [G][cc] own slice: scores, then exponentials
+    float *eall = gsm + GL.o_eall; // [G][spc] all exponentials, then probabilities
+    char *kraw = reinterpret_cast<char *>(gsm + GL.o_reg2);  // key rows [t0, t1) while scoring
+    float *vt = gsm + GL.o_reg2;   // then: [DPC][spc] this CTA's value columns, transposed (fp32 cache)
+    __half *vt16 = reinterpret_cast<__half *>(gsm + GL.o_reg2);  // (fp16 cache: fp16)
+    char *vraw = reinterpret_cast<char *>(gsm + GL.o_vraw);  // fp16 cache: [spc][DPC] value columns as cached
     const char *kbase = reinterpret_cast<const char *>(p.kc) + (size_t)g * p.max_ctx * HD * EB;
     const char *vbase = reinterpret_cast<const char *>(p.vc) + (size_t)g * p.max_ctx * HD * EB;
     const int d0 = rank * DPC;
 
     if (tid == 0) trace_mark(p.trace, TR_START);
+    if (tid < 32) etab[tid] = kExp2Tab32[tid];
     if (tid == 0 && p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
-    if (tid == 0 && p.pos_dev && !p.no_kv_prefetch) {
-        // the cache rows before this token do not depend on the previous
-        // kernel: pull this CTA's key slice into L2 now (the position read
-        // here may be the previous step's; it only bounds the hint)
-        const int sp = *(volatile const int *)p.pos_dev + 1;
-        const int ch = (((sp + CL - 1) / CL) + 3) & ~3;
-        const int a = min(sp, rank * ch), b = min(sp, a + ch);
-        if (b > a) {
-            L2Prefetch kv{};
-            kv.ptr[0] = kbase + (size_t)a * HD * EB;
-            kv.bytes[0] = (int64_t)(b - a) * HD * EB;
-            kv.n = 1;
-            prefetch_l2_slice(kv, 0, 1);
-        }
-    }
+    OVF_PHASE(0);
     pdl_wait();
     if (tid == 0) trace_mark(p.trace, TR_WAITED);
     const int pos = p.pos_dev ? *p.pos_dev : p.seq_len_host - 1 + row;
     const int seq = pos + 1;
     const int chunk = (((seq + CL - 1) / CL) + 3) & ~3;
     const int t0 = min(seq, rank * chunk), t1 = min(seq, t0 + chunk);
+    const int own = t1 - t0;
     const bool has_new = p.k_new != nullptr;
+    // the cached rows arrive by asynchronous copies while the prologue runs:
+    // the CTA's key rows [t0, t1) (contiguous), then its value columns
+    // [d0, d0 + DPC) of every earlier position
+    {
+        const char *src = kbase + (size_t)t0 * HD * EB;
+        const int n16 = own * HD * EB / 16;
+        for (int i = tid; i < n16; i += NT) cp_async16(kraw + 16 * i, src + 16 * (size_t)i);
+        cp_async_commit();
+    }
+    // the exponentials of every slice arrive by bulk copies from the owners:
+    // G rows of own_pad(r) floats from each rank r
+    if (tid == 0) {
+        uint32_t expect = 0;
+        for (int r = 0; r < CL; ++r) {
+            const int a = min(seq, r * chunk), b = min(seq, a + chunk);
+            expect += (uint32_t)(G * ((b - a + 3) & ~3) * 4);
+        }
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, expect);
+    }
 
     for (int i = tid; i < G * HD; i += NT) qs[i] = p.q[((size_t)row * p.H + (size_t)g * G) * HD + i];
     if (has_new)
@@ -182,19 +230,22 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
         }
     }
     pdl_launch_dependents();
+    OVF_PHASE(1);
 
     // 1. scores of [t0, t1) for every head of the group
     const int c = lane & 15, hw = lane >> 4;
-    float qreg[kGrpMaxHeads][HD / 16];
+    float qreg[G][HD / 16];
 #pragma unroll
-    for (int h = 0; h < kGrpMaxHeads; ++h)
+    for (int h = 0; h < G; ++h)
 #pragma unroll
-        for (int i = 0; i < HD / 16; ++i) qreg[h][i] = h < G ? qs[h * HD + 16 * i + c] : 0.0f;
-    float lmax[kGrpMaxHeads];
+        for (int i = 0; i < HD / 16; ++i) qreg[h][i] = qs[h * HD + 16 * i + c];
+    float lmax[G];
 #pragma unroll
-    for (int h = 0; h < kGrpMaxHeads; ++h) lmax[h] = -INFINITY;
+    for (int h = 0; h < G; ++h) lmax[h] = -INFINITY;
+    cp_async_wait<0>();  // this thread's key copies
+    __syncthreads();
     constexpr int KPI = 2 * (NT / 32);  // keys per step (a half-warp each)
-    constexpr int U = 4;                // keys per half-warp in flight
+    constexpr int U = G <= 4 ? 4 : 2;   // keys per half-warp per step
     for (int tb = t0; tb < t1; tb += U * KPI) {
         float kv[U][HD / 16];
 #pragma unroll
@@ -205,184 +256,251 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
 #pragma unroll
                 for (int i = 0; i < HD / 16; ++i) kv[u][i] = kn[16 * i + c];
             } else if (F16) {
-                const __half *kr = reinterpret_cast<const __half *>(kbase) + (size_t)tt * HD;
+                const __half *kr = reinterpret_cast<const __half *>(kraw) + (size_t)(tt - t0) * HD;
 #pragma unroll
                 for (int i = 0; i < HD / 16; ++i) kv[u][i] = __half2float(kr[16 * i + c]);
             } else {
-                const float *kr = reinterpret_cast<const float *>(kbase) + (size_t)tt * HD;
+                const float *kr = reinterpret_cast<const float *>(kraw) + (size_t)(tt - t0) * HD;
 #pragma unroll
                 for (int i = 0; i < HD / 16; ++i) kv[u][i] = kr[16 * i + c];
             }
         }
+        // all (key, head) dots first, then each fold round over all of them:
+        // the shuffles of independent dots overlap
+        float v[U][G];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                float a = 0.0f;
+#pragma unroll
+                for (int i = 0; i < HD / 16; ++i) a = fadd(a, fmul(qreg[h][i], kv[u][i]));
+                v[u][h] = a;
+            }
+        // v[j] = acc0[j] + acc1[j], then ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7))
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int h = 0; h < G; ++h) v[u][h] = fadd(v[u][h], __shfl_xor_sync(0xFFFFFFFFu, v[u][h], 8));
+#pragma unroll
+        for (int o = 1; o <= 4; o <<= 1)
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int h = 0; h < G; ++h) v[u][h] = fadd(v[u][h], __shfl_xor_sync(0xFFFFFFFFu, v[u][h], o));
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int t = tb + u * KPI + 2 * warp + hw;
+            if (c == 0 && t < t1) {
 #pragma unroll
-            for (int h = 0; h < kGrpMaxHeads; ++h) {
-                if (h < G) {
-                    float a = 0.0f;
-#pragma unroll
-                    for (int i = 0; i < HD / 16; ++i) a = fadd(a, fmul(qreg[h][i], kv[u][i]));
-                    // v[j] = acc0[j] + acc1[j], then ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7))
-                    float v = fadd(a, __shfl_xor_sync(0xFFFFFFFFu, a, 8));
-                    v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
-                    v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
-                    v = fadd(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
-                    const float s = fmul(v, p.scale);
-                    if (c == 0 && t < t1) {
-                        sc[h * cc + (t - t0)] = s;
-                        lmax[h] = s > lmax[h] ? s : lmax[h];
-                    }
+                for (int h = 0; h < G; ++h) {
+                    const float sv = fmul(v[u][h], p.scale);
+                    sc[h * cc + (t - t0)] = sv;
+                    lmax[h] = sv > lmax[h] ? sv : lmax[h];
                 }
             }
         }
     }
+    OVF_PHASE(2);
+    if (F16) {
+        // the value columns [d0, d0 + DPC) of every earlier position arrive
+        // while the maxima and exponentials are formed
+        const int nv = has_new ? pos : seq;  // the decoded token's row is not cached yet
+        for (int t = tid; t < nv; t += NT)
+            cp_async_n(vraw + (size_t)t * DPC * EB, vbase + ((size_t)t * HD + d0) * EB, DPC * EB);
+        cp_async_commit();
+    }
     // 2. per-head maxima over the cluster (max is order-free)
 #pragma unroll
-    for (int h = 0; h < kGrpMaxHeads; ++h) {
+    for (int h = 0; h < G; ++h) {
         float m = lmax[h];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
         if (lane == 0) red[warp * 8 + h] = m;
     }
     __syncthreads();
-    if (tid < G) {
-        float m = red[tid];
-        for (int w = 1; w < NT / 32; ++w) m = fmaxf(m, red[w * 8 + tid]);
-        red[64 + tid] = m;
+    if (tid < G * CL) {
+        // this CTA's maximum of head h, pushed to every rank's table
+        const int r = tid / G, h = tid - r * G;
+        float m = red[h];
+        for (int w = 1; w < NT / 32; ++w) m = fmaxf(m, red[w * 8 + h]);
+        cluster.map_shared_rank(red, r)[128 + rank * G + h] = m;
     }
+    OVF_PHASE(3);
     cluster.sync();
+    OVF_PHASE(4);
     if (tid < G) {
         float m = -INFINITY;
-        for (int r = 0; r < CL; ++r) m = fmaxf(m, cluster.map_shared_rank(red, r)[64 + tid]);
+#pragma unroll
+        for (int r = 0; r < CL; ++r) m = fmaxf(m, red[128 + r * G + tid]);
         red[96 + tid] = m;
     }
     __syncthreads();
-    const int own = t1 - t0;
-    for (int i = tid; i < G * own; i += NT) {
-        const int h = i / own, t = i - h * own;
-        sc[h * cc + t] = exp_libm(fsub(sc[h * cc + t], red[96 + h]));
+    // the slice's exponentials, one per thread, then one bulk copy per
+    // (rank, head) of them into every CTA's eall (t0 is a multiple of 4; a
+    // last partial quad only fills positions past the sequence)
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+        for (int t = tid; t < own; t += NT) sc[h * cc + t] = exp_libm(fsub(sc[h * cc + t], red[96 + h]), etab);
+    fence_proxy_async_smem();  // the writes above are read by the bulk-copy engine
+    __syncthreads();
+    const int own_pad = (own + 3) & ~3;
+    if (tid < CL * G && own_pad > 0) {
+        const int r = tid / G, h = tid - r * G;
+        bulk_s2cluster(mapa_shared(smem_u32(eall + h * spc + t0), (uint32_t)r), sc + h * cc, (uint32_t)own_pad * 4,
+                       mapa_shared(smem_u32(bar), (uint32_t)r));
     }
-    cluster.sync();
-
-    // 3. all heads' exponentials into this CTA, 16 bytes per remote load
+    OVF_PHASE(5);
+    // meanwhile: this CTA's value columns, transposed to vt[d][t] over the
+    // dead key rows, four positions per thread (fp16 cache: from the copies
+    // already in shared memory, kept in fp16; fp32 cache: from the cache)
+    cp_async_wait<0>();
+    __syncthreads();
     const int nq = (seq + 3) >> 2;
-    for (int base = 0; base < G * nq; base += 4 * NT) {
-        float4 tmp[4];
-        int dst[4];
+    for (int q = tid; q < nq; q += NT) {
+        float v[4][DPC];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int i = base + j * NT + tid;
-            dst[j] = -1;
-            if (i < G * nq) {
-                const int h = i / nq, t = 4 * (i - h * nq), r = t / chunk;
-                tmp[j] = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(sc, r) + h * cc + (t - r * chunk));
-                dst[j] = h * spc + t;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            if (dst[j] >= 0) *reinterpret_cast<float4 *>(eall + dst[j]) = tmp[j];
-    }
-    __syncthreads();
-
-    if (warp == 0) {
-        // sumExp chains, one lane per head, in position order
-        if (lane < G) {
-            const float *e = eall + lane * spc;
-            float sum = 0.0f;
-            int t = 0;
-            const int s32 = seq & ~31;
-            if (s32 > 0) {
-                float4 a[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) a[j] = reinterpret_cast<const float4 *>(e)[j];
-                for (; t < s32; t += 32) {
-                    float4 b[8];
-                    const int tn = t + 32 < s32 ? t + 32 : t;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) b[j] = reinterpret_cast<const float4 *>(e + tn)[j];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        sum = fadd(sum, a[j].x);
-                        sum = fadd(sum, a[j].y);
-                        sum = fadd(sum, a[j].z);
-                        sum = fadd(sum, a[j].w);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) a[j] = b[j];
-                }
-            }
-            for (; t < seq; ++t) sum = fadd(sum, e[t]);
-            const bool bad = !(sum > 0.0f) || isinf(sum);
-            red[80 + lane] = bad ? 0.0f : fdiv(1.0f, sum);
-            red[88 + lane] = bad ? 1.0f : 0.0f;
-        }
-    } else {
-        // meanwhile: this CTA's value columns [d0, d0 + DPC), transposed to
-        // vt[d][t] and widened to fp32
-        for (int t = tid - 32; t < seq; t += NT - 32) {
-            float v[DPC];
+            const int t = 4 * q + j;
             if (has_new && t == pos) {
 #pragma unroll
-                for (int d = 0; d < DPC; ++d) v[d] = vn[d0 + d];
+                for (int d = 0; d < DPC; ++d) v[j][d] = vn[d0 + d];
+            } else if (t < seq) {
+                if (F16) load_cols<DPC, true>(vraw + (size_t)t * DPC * EB, v[j]);
+                else load_cols<DPC, false>(vbase + ((size_t)t * HD + d0) * EB, v[j]);
             } else {
-                load_cols<DPC, F16>(vbase + ((size_t)t * HD + d0) * EB, v);
-            }
 #pragma unroll
-            for (int d = 0; d < DPC; ++d) vt[d * spc + t] = v[d];
+                for (int d = 0; d < DPC; ++d) v[j][d] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < DPC; ++d) {
+            if (F16) {
+                // exact: every value came from an fp16
+                __half2 lo = __floats2half2_rn(v[0][d], v[1][d]), hi = __floats2half2_rn(v[2][d], v[3][d]);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t *>(&lo);
+                u.y = *reinterpret_cast<uint32_t *>(&hi);
+                *reinterpret_cast<uint2 *>(vt16 + (size_t)d * spc + 4 * q) = u;
+            } else {
+                *reinterpret_cast<float4 *>(vt + d * spc + 4 * q) = make_float4(v[0][d], v[1][d], v[2][d], v[3][d]);
+            }
+        }
+    }
+    mbar_wait_sleep_bounded(bar, 0);  // every slice's exponentials have landed
+    __syncthreads();
+    OVF_PHASE(8);
+
+    if (warp == 0 && lane < G) {
+        // sumExp chains, one lane per head, in position order
+        const float *e = eall + lane * spc;
+        float sum = 0.0f;
+        int t = 0;
+        const int s32 = seq & ~31;
+        if (s32 > 0) {
+            float4 a[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = reinterpret_cast<const float4 *>(e)[j];
+            for (; t < s32; t += 32) {
+                float4 b[8];
+                const int tn = t + 32 < s32 ? t + 32 : t;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) b[j] = reinterpret_cast<const float4 *>(e + tn)[j];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    sum = fadd(sum, a[j].x);
+                    sum = fadd(sum, a[j].y);
+                    sum = fadd(sum, a[j].z);
+                    sum = fadd(sum, a[j].w);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a[j] = b[j];
+            }
+        }
+        for (; t < seq; ++t) sum = fadd(sum, e[t]);
+        const bool bad = !(sum > 0.0f) || isinf(sum);
+        red[80 + lane] = bad ? 0.0f : fdiv(1.0f, sum);
+        red[88 + lane] = bad ? 1.0f : 0.0f;
+    }
+    OVF_PHASE(9);
+    __syncthreads();
+    OVF_PHASE(10);
+    // p_t = e_t * invSum (the reference's probability), all threads
+    for (int h = 0; h < G; ++h) {
+        const float inv = red[80 + h];
+        float4 *e4 = reinterpret_cast<float4 *>(eall + h * spc);
+        for (int q = tid; q < nq; q += NT) {
+            float4 v = e4[q];
+            v.x = fmul(v.x, inv);
+            v.y = fmul(v.y, inv);
+            v.z = fmul(v.z, inv);
+            v.w = fmul(v.w, inv);
+            e4[q] = v;
         }
     }
     __syncthreads();
-    // p_t = e_t * invSum (the reference's probability), all threads
-    for (int i = tid; i < G * nq * 4; i += NT) {
-        const int h = i / (nq * 4), t = i - h * nq * 4;
-        if (t < seq) eall[h * spc + t] = fmul(eall[h * spc + t], red[80 + h]);
-    }
-    __syncthreads();
-
+    OVF_PHASE(11);
     // 4. output chains: lane (h, d) sums p_t * v_t[d] over t in order
     if (tid < G * DPC) {
         const int h = tid / DPC, d = tid - h * DPC;
         float acc = 0.0f;
         if (red[88 + h] == 0.0f) {
-            const float *pp = eall + h * spc, *vv = vt + d * spc;
+            const float *pp = eall + h * spc;
+            const size_t vrow = (size_t)d * spc;
+            // four values of dimension d at positions t..t+3 (t a multiple of 4)
+            auto v4 = [&](int t) -> float4 {
+                if (F16) {
+                    const uint2 u = *reinterpret_cast<const uint2 *>(vt16 + vrow + t);
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+                    return make_float4(a.x, a.y, b.x, b.y);
+                }
+                return *reinterpret_cast<const float4 *>(vt + vrow + t);
+            };
             const int s16 = seq & ~15;
             int t = 0;
             if (s16 > 0) {
-                float4 pa[4], va[4];
+                // the products of a block are formed while the previous
+                // block's adds run; each add then waits only on the last one
+                float pr[16];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    pa[j] = reinterpret_cast<const float4 *>(pp)[j];
-                    va[j] = reinterpret_cast<const float4 *>(vv)[j];
+                    const float4 a = reinterpret_cast<const float4 *>(pp)[j];
+                    const float4 b = v4(4 * j);
+                    pr[4 * j] = fmul(a.x, b.x);
+                    pr[4 * j + 1] = fmul(a.y, b.y);
+                    pr[4 * j + 2] = fmul(a.z, b.z);
+                    pr[4 * j + 3] = fmul(a.w, b.w);
                 }
                 for (; t < s16; t += 16) {
-                    float4 pb[4], vb[4];
                     const int tn = t + 16 < s16 ? t + 16 : t;
+                    float nx[16];
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        pb[j] = reinterpret_cast<const float4 *>(pp + tn)[j];
-                        vb[j] = reinterpret_cast<const float4 *>(vv + tn)[j];
+                        const float4 a = reinterpret_cast<const float4 *>(pp + tn)[j];
+                        const float4 b = v4(tn + 4 * j);
+                        nx[4 * j] = fmul(a.x, b.x);
+                        nx[4 * j + 1] = fmul(a.y, b.y);
+                        nx[4 * j + 2] = fmul(a.z, b.z);
+                        nx[4 * j + 3] = fmul(a.w, b.w);
                     }
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        acc = fadd(acc, fmul(pa[j].x, va[j].x));
-                        acc = fadd(acc, fmul(pa[j].y, va[j].y));
-                        acc = fadd(acc, fmul(pa[j].z, va[j].z));
-                        acc = fadd(acc, fmul(pa[j].w, va[j].w));
-                    }
+                    for (int j = 0; j < 16; ++j) acc = fadd(acc, pr[j]);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        pa[j] = pb[j];
-                        va[j] = vb[j];
-                    }
+                    for (int j = 0; j < 16; ++j) pr[j] = nx[j];
                 }
             }
-            for (; t < seq; ++t) acc = fadd(acc, fmul(pp[t], vv[t]));
+            for (; t < seq; ++t) {
+                const float4 b = v4(t & ~3);
+                const float vv = (t & 3) == 0 ? b.x : (t & 3) == 1 ? b.y : (t & 3) == 2 ? b.z : b.w;
+                acc = fadd(acc, fmul(pp[t], vv));
+            }
         }
         p.out[((size_t)row * p.H + (size_t)g * G + h) * HD + d0 + d] = acc;
     }
+    OVF_PHASE(12);
     cluster.sync();  // no CTA leaves while another may still read its shared memory
+    OVF_PHASE(13);
     if (tid == 0) trace_mark(p.trace, TR_END);
 }
 
@@ -393,19 +511,21 @@ bool attn_group_supported(int H, int KVH, int hd, int kv_dtype, int seq_cap, int
     if (hd != 32 && hd != 64 && hd != 128) return false;
     if (KVH <= 0 || H % KVH != 0) return false;
     const int G = H / KVH;
-    if (G > kGrpMaxHeads || G * (hd / kGrpCluster) > kGrpThreads) return false;
-    return group_layout(G, hd, seq_cap).floats * 4 <= smem_optin_bytes;
+    if (G * (hd / kGrpCluster) > kGrpThreads) return false;
+    const bool inst = G == 1 || G == 4 || G == 8 || (G == 2 && hd != 32) || (G == 7 && hd != 128);
+    if (!inst) return false;
+    return group_layout(G, hd, seq_cap, kv_dtype == OVF_KV_F16 ? 2 : 4).floats * 4 <= smem_optin_bytes;
 }
 
-template <int HD, int KT>
+template <int HD, int KT, int GT>
 static cudaError_t launch_group_inst(const AttnParams &p, int seq_cap, size_t smem, cudaStream_t st, bool pdl) {
     static PerDeviceOnce attr_once;
     const int dev = current_device();
     if (attr_once.pending(dev)) {
-        cudaError_t e = cudaFuncSetAttribute(attention_group_kernel<HD, KT>,
+        cudaError_t e = cudaFuncSetAttribute(attention_group_kernel<HD, KT, GT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin(dev));
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(attention_group_kernel<HD, KT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            e = cudaFuncSetAttribute(attention_group_kernel<HD, KT, GT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
         attr_once.mark(dev);
     }
@@ -423,24 +543,23 @@ static cudaError_t launch_group_inst(const AttnParams &p, int seq_cap, size_t sm
     attrs[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attrs;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, attention_group_kernel<HD, KT>, p, seq_cap);
+    return cudaLaunchKernelEx(&cfg, attention_group_kernel<HD, KT, GT>, p, seq_cap);
 }
 
 ovf_status launch_attention_group(const AttnParams &p, int seq_cap, cudaStream_t st, bool pdl, int kv_dtype) {
     const int G = p.H / p.KVH;
-    const size_t smem = (size_t)group_layout(G, p.hd, seq_cap).floats * 4;
+    const size_t smem = (size_t)group_layout(G, p.hd, seq_cap, kv_dtype == OVF_KV_F16 ? 2 : 4).floats * 4;
     OVF_CHECK_ARG(p.rows <= 1 || (p.k_new == nullptr && !p.pos_dev && p.rows <= 65535), "attention: bad row batch");
     cudaError_t e = cudaErrorInvalidValue;
     const bool f16 = kv_dtype == OVF_KV_F16;
-    switch (p.hd) {
-        case 32: e = f16 ? launch_group_inst<32, OVF_KV_F16>(p, seq_cap, smem, st, pdl)
-                         : launch_group_inst<32, OVF_KV_F32>(p, seq_cap, smem, st, pdl); break;
-        case 64: e = f16 ? launch_group_inst<64, OVF_KV_F16>(p, seq_cap, smem, st, pdl)
-                         : launch_group_inst<64, OVF_KV_F32>(p, seq_cap, smem, st, pdl); break;
-        case 128: e = f16 ? launch_group_inst<128, OVF_KV_F16>(p, seq_cap, smem, st, pdl)
-                          : launch_group_inst<128, OVF_KV_F32>(p, seq_cap, smem, st, pdl); break;
-        default: break;
-    }
+#define OVF_GRP(HDV, GV)                                                                                      \
+    if (p.hd == HDV && G == GV)                                                                               \
+        e = f16 ? launch_group_inst<HDV, OVF_KV_F16, GV>(p, seq_cap, smem, st, pdl)                           \
+                : launch_group_inst<HDV, OVF_KV_F32, GV>(p, seq_cap, smem, st, pdl);
+    OVF_GRP(128, 1) OVF_GRP(128, 2) OVF_GRP(128, 4) OVF_GRP(128, 8)
+    OVF_GRP(64, 1) OVF_GRP(64, 2) OVF_GRP(64, 4) OVF_GRP(64, 7) OVF_GRP(64, 8)
+    OVF_GRP(32, 1) OVF_GRP(32, 4) OVF_GRP(32, 7) OVF_GRP(32, 8)
+#undef OVF_GRP
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "attention_group_kernel launch");
 }
 

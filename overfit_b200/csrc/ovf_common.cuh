@@ -96,6 +96,23 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// 1-D bulk copy from this CTA's shared memory to a CTA of the cluster
+// (addresses from mapa_shared), completion signalled on that CTA's mbarrier.
+// 16-byte aligned addresses, bytes a non-zero multiple of 16.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -268,6 +285,17 @@ __device__ __forceinline__ float rms_scale(float sumsq, int d, float eps) {
     return fdiv(1.0f, sqrtf(fadd(fdiv(sumsq, (float)d), eps)));
 }
 
+// cp.async (Ampere-style asynchronous copies into shared memory).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // e^x for a float argument with the bits of the host C library's expf, which
 // is what the reference's MathF.Exp calls on Linux.  glibc (2.27 onwards)
 // and musl use the ARM optimized-routines single-precision exp (Szabolcs
@@ -295,7 +323,10 @@ __device__ const unsigned long long kExp2Tab32[32] = {
     0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
 
-__device__ __forceinline__ float exp_libm(float x) {
+// `tab`: the 32-entry table above, or a copy of it in shared memory (a
+// kernel that exponentiates on its critical path copies it at its start: the
+// global table's first read costs an L2 round trip).
+__device__ __forceinline__ float exp_libm(float x, const unsigned long long *tab) {
     if (!(fabsf(x) < 88.0f)) {
         if (x != x) return x + x;
         if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
@@ -310,7 +341,7 @@ __device__ __forceinline__ float exp_libm(float x) {
     const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
     kd = __dsub_rn(kd, shift);
     const double r = __fma_rn(inv_ln2_n, xd, -kd);
-    unsigned long long t = __ldg(&kExp2Tab32[ki & 31]);
+    unsigned long long t = tab[ki & 31];
     t += ki << 47;
     const double s = __longlong_as_double((long long)t);
     const double z = __fma_rn(c0, r, c1);
@@ -320,6 +351,8 @@ __device__ __forceinline__ float exp_libm(float x) {
     y = __dmul_rn(y, s);
     return __double2float_rn(y);
 }
+
+__device__ __forceinline__ float exp_libm(float x) { return exp_libm(x, kExp2Tab32); }
 
 // Q8_K / Q8_0 element quantizer: clamp(round_half_even(x * inv), -127, 127).
 __device__ __forceinline__ int quant_elem(float x, float inv) {

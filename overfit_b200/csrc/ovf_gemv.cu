@@ -478,7 +478,7 @@ __device__ __forceinline__ uint32_t copy_span(uint8_t *dst, const uint8_t *src, 
 // releases those stores) announces the transaction count, pass 1 issues the
 // copies.
 __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L, const GroupRef &g, uint8_t *stage,
-                                            uint64_t *bar, uint64_t pol) {
+                                            uint64_t *bar, uint64_t pol, size_t eoff_w = 0, size_t eoff_s = 0) {
     const int parts = p.pair ? 2 : 1;
     uint32_t bytes = 0;
     for (int pass = 0; pass < 2; ++pass) {
@@ -486,11 +486,12 @@ __device__ __forceinline__ void issue_stage(const GemvParams &p, const Layout &L
         for (int part = 0; part < parts && g.nr > 0; ++part) {
             const GemvSeg &sg = p.seg[p.pair ? part : g.seg];
             const size_t rb = (size_t)row_bytes(sg.type, p.K);
-            bytes += copy_span(stage + part * L.part_bytes, sg.w, (size_t)g.r0 * rb, (size_t)g.nr * rb,
+            bytes += copy_span(stage + part * L.part_bytes, sg.w + eoff_w, (size_t)g.r0 * rb, (size_t)g.nr * rb,
                                (size_t)sg.rows * rb, bar, pol, bulk);
             if (!is_kquant(sg.type)) {
                 const size_t sb = (size_t)(p.K / 8);
-                bytes += copy_span(stage + L.s_region + part * L.s_part, reinterpret_cast<const uint8_t *>(sg.ws),
+                bytes += copy_span(stage + L.s_region + part * L.s_part,
+                                   reinterpret_cast<const uint8_t *>(sg.ws) + eoff_s,
                                    (size_t)g.r0 * sb, (size_t)g.nr * sb, (size_t)sg.rows * sb, bar, pol, bulk);
             }
         }
@@ -658,15 +659,28 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     }
     __syncthreads();
     uint64_t pol = 0;
-    // Weights do not depend on the previous kernel: start streaming now.
+    // Weights do not depend on the previous kernel: start streaming now
+    // (a routed expert's weights only once the routing is known).
+    const bool routed = p.expert_sel != nullptr;
     if (warp == kProducerWarp && lane == 0) {
         pol = l2_evict_first_policy();
-        for (int it = 0; it < p.stages && it < items; ++it)
-            issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)it * L.stage_bytes, &B.full[it],
-                        pol);
+        if (!routed)
+            for (int it = 0; it < p.stages && it < items; ++it)
+                issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)it * L.stage_bytes, &B.full[it],
+                            pol);
     }
 
     pdl_wait();
+    size_t eoff_w = 0, eoff_s = 0;
+    if (routed) {
+        const int e = p.expert_sel[p.expert_slot];
+        eoff_w = (size_t)e * (size_t)p.expert_wstride;
+        eoff_s = (size_t)e * (size_t)p.expert_sstride;
+        if (warp == kProducerWarp && lane == 0)
+            for (int it = 0; it < p.stages && it < items; ++it)
+                issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)it * L.stage_bytes, &B.full[it],
+                            pol, eoff_w, eoff_s);
+    }
     if (tid == 0) trace_mark(p.trace, TR_WAITED);
     if (p.fill_sentinel) {
         // mark the buffer a later residual launch of this step will write
@@ -698,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             if (*B.abort_flag) break;
             fence_proxy_async_smem();
             issue_stage(p, L, locate(p, tcta + it * tgrid), ring + (size_t)s * L.stage_bytes, &B.full[s],
-                        pol);
+                        pol, eoff_w, eoff_s);
         }
         if (p.pf.n) prefetch_l2_slice(p.pf, blockIdx.x, gridDim.x);
         trace_mark(p.trace, TR_END);
@@ -947,6 +961,9 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
                       "gemv: an output RMSNorm needs a single-segment residual launch");
     if (p.act_mode == ACT_F32_RMSNORM) OVF_CHECK_ARG(p.norm_scale != nullptr, "gemv: RMSNorm input without its scale");
     if (p.epi == EPI_LOGITS_ARGMAX) OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
+    if (p.expert_sel)
+        OVF_CHECK_ARG(p.expert_wstride % 16 == 0 && p.expert_sstride % 16 == 0 && p.expert_slot >= 0 && !p.norm_out,
+                      "gemv: routed expert weights need 16-byte strides and no output norm");
 
     int device = 0;
     OVF_CUDA_TRY(cudaGetDevice(&device));

@@ -81,6 +81,10 @@ struct GemvParams {
     int fill_n;
     DevStep *step;       // EPI_LOGITS_ARGMAX
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
+    const int *expert_sel;  // routed expert: segment weights are offset by expert_sel[expert_slot] * stride
+    int expert_slot;        // (read after griddepcontrol.wait; no weight is staged before it)
+    int64_t expert_wstride;  // bytes between experts' quants
+    int64_t expert_sstride;  // bytes between experts' Q8_0 scales
     L2Prefetch pf;       // weights of a later launch to pull into L2 once this one's are issued
     TraceSlot *trace;    // OVF_TRACE timeline slot, or null
 };

@@ -115,6 +115,17 @@ ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float 
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
                         DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,
                         bool pdl);
+// ovf_moe.cu: router, combine, row gather/scatter of the MoE FFN.
+ovf_status launch_moe_route(const float *x, int ld_x, const float *gamma, const float *norm_scale, const float *R,
+                            int rows, int D, int E, int K, int normalize, int32_t *sel, float *w, cudaStream_t st,
+                            bool pdl);
+ovf_status launch_moe_combine(const float *after, const float *y, const float *w, int K, int D, float *hidden,
+                              float *norm_out, float eps, cudaStream_t st, bool pdl);
+ovf_status launch_moe_combine_rows(const float *a, const float *slot, const float *w, int K, int rows, int D, float *out,
+                                   cudaStream_t st);
+ovf_status launch_gather_rows(const float *src, const int32_t *rows, int n, int width, float *dst, cudaStream_t st);
+ovf_status launch_scatter_slots(const float *src, const int32_t *rows, const int32_t *slots, int n, int K, int width,
+                                float *dst, cudaStream_t st);
 ovf_status launch_take_error(int *dev_slot, cudaStream_t st);
 ovf_status launch_exp(const float *x, float *y, int64_t n, cudaStream_t st);
 ovf_status launch_silu_mul(const float *g, const float *u, float *h, int64_t n, cudaStream_t st, bool pdl);

@@ -40,7 +40,45 @@ struct DevLayer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     DevWeight wq, wk, wv, wo, gate, up, down;
     float *bq = nullptr, *bk = nullptr, *bv = nullptr, *bo = nullptr;
+    // MoE (n_experts > 0): F32 router [d_model][n_experts] (input-major, as
+    // GgufLlamaLoader.cs:770-786 transposes ffn_gate_inp); gate/up/down hold
+    // the experts' matrices back to back, `*_stride` bytes apart
+    float *router = nullptr;
+    int64_t gu_wstride = 0, gu_sstride = 0, d_wstride = 0, d_sstride = 0;
 };
+
+// MoE scratch of a batch of rows (allocated on first use): the routing
+// [rows][k], per-expert row lists, the gathered inputs, one expert's outputs
+// and every row's k expert outputs [rows][k][d_model].
+struct MoeRows {
+    int cap = 0;
+    int32_t *sel = nullptr, *idx = nullptr;  // idx: rows [E][cap] then slots [E][cap]
+    float *w = nullptr, *gx = nullptr, *eo = nullptr, *slot = nullptr;
+    int32_t *host = nullptr;  // pinned: sel [cap][k] | rows/slots [2][E][cap]
+};
+
+// Bytes of one expert's quants and Q8_0 scales in a stacked expert weight.
+void expert_strides(const DevWeight &w, int64_t rows_e, int64_t *wstride, int64_t *sstride) {
+    if (w.type == OVF_TYPE_Q8_0) {
+        *wstride = rows_e * w.cols;
+        *sstride = rows_e * (w.cols / 32) * 4;
+    } else {
+        *wstride = rows_e * (w.cols / 256) * (w.type == OVF_TYPE_Q4_K ? 144 : 210);
+        *sstride = 0;
+    }
+}
+
+// One expert of a stacked expert weight as a weight of its own.
+DevWeight expert_view(const DevWeight &w, int64_t rows_e, int e) {
+    int64_t ws = 0, ss = 0;
+    expert_strides(w, rows_e, &ws, &ss);
+    DevWeight v = w;
+    v.data = w.data + (size_t)e * ws;
+    v.scales = w.scales ? reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(w.scales) + (size_t)e * ss) : nullptr;
+    v.rows = rows_e;
+    v.owns = false;
+    return v;
+}
 
 }  // namespace
 
@@ -61,6 +99,7 @@ struct ovf_model {
     int32_t *btok = nullptr, *bargmax = nullptr;
     int32_t *btok_host = nullptr;  // pinned
     std::atomic<bool> batch_busy{false};  // one ovf_session_decode_batch at a time per model
+    MoeRows bmoe;                          // MoE scratch of the batch rows
 };
 
 struct ovf_session {
@@ -79,6 +118,8 @@ struct ovf_session {
           *partial = nullptr;
     int *counters = nullptr, *tokens_log = nullptr;
     int *err_slot = nullptr;  // device word the error word is moved into after a call
+    int32_t *msel = nullptr;  // MoE decode: selected experts [k], their weights [k],
+    float *mw = nullptr, *mh = nullptr, *meo = nullptr;  // SwiGLU rows [k][d_ff], expert outputs [k][d_model]
     float *norm_s = nullptr;  // [0]: RMSNorm scale of hidden, [1]: of after
     TraceSlot *trace = nullptr;  // OVF_TRACE=1: per-launch timeline of the last step
     int trace_cap = 0, trace_n = 0;
@@ -94,6 +135,7 @@ struct ovf_session {
     int8_t *paq = nullptr;
     int16_t *pab = nullptr;
     int32_t *ptok = nullptr;
+    MoeRows pmoe;  // MoE scratch of the prefill rows
     // speculative verify: per-row logits and argmax of one verify batch
     float *vlogits = nullptr;
     int32_t *vargmax = nullptr;
@@ -108,6 +150,24 @@ ovf_status dalloc(std::vector<void *> &list, void **p, size_t bytes) {
     if (e != cudaSuccess) return cuda_status(e, "cudaMalloc");
     list.push_back(*p);
     return OVF_OK;
+}
+
+ovf_status moe_rows_alloc(const ovf_model_config &c, int cap, std::vector<void *> &allocs, MoeRows *mr) {
+    if (mr->cap >= cap) return OVF_OK;
+    const size_t K = c.n_experts_used, E = c.n_experts, D = c.d_model;
+    ovf_status st = OVF_OK;
+    auto A = [&](void **p, size_t bytes) {
+        if (!st) st = dalloc(allocs, p, bytes);
+    };
+    A((void **)&mr->sel, cap * K * 4);
+    A((void **)&mr->idx, 2 * E * cap * 4);
+    A((void **)&mr->w, cap * K * 4);
+    A((void **)&mr->gx, cap * D * 4);
+    A((void **)&mr->eo, cap * D * 4);
+    A((void **)&mr->slot, cap * K * D * 4);
+    if (!st) st = cuda_status(cudaMallocHost(&mr->host, (cap * K + 2 * E * cap) * 4), "cudaMallocHost");
+    if (!st) mr->cap = cap;
+    return st;
 }
 
 int64_t tensor_bytes(int type, int64_t rows, int64_t cols) {
@@ -317,6 +377,57 @@ static void trace_report(ovf_session *s) {
                 x.second.gap / x.second.n);
 }
 
+// MoE FFN of one decode token (MoeFeedForwardBlock.Decode, :79-138): the
+// router on the device, then for each of the k selected experts a fused
+// gate/up GEMV (SiLU*up) and a down GEMV whose weights are picked by the
+// expert index the router left in device memory (no host round trip, so the
+// step stays one CUDA graph), then the weighted sum in top-k order, the
+// residual, and the next RMSNorm's scale.
+template <class Slot>
+ovf_status enqueue_moe_ffn(ovf_session *s, const DevLayer &L, cudaStream_t st, Slot tslot) {
+    const ovf_model_config &c = s->m->cfg;
+    const int D = c.d_model, FF = c.d_ff, K = c.n_experts_used;
+    ovf_status r = launch_moe_route(s->after, D, L.ffn_norm, &s->norm_s[1], L.router, 1, D, c.n_experts, K,
+                                    c.normalize_experts, s->msel, s->mw, st, true);
+    if (r) return r;
+    for (int j = 0; j < K; ++j) {
+        GemvParams p{};
+        p.nseg = 2;
+        p.pair = 1;
+        p.seg[0] = seg_of(L.gate, nullptr, s->mh + (size_t)j * FF);
+        p.seg[1] = seg_of(L.up, nullptr, s->mh + (size_t)j * FF);
+        p.seg[0].rows = p.seg[1].rows = FF;
+        p.K = D;
+        p.act_mode = ACT_F32_RMSNORM;
+        p.x = s->after;
+        p.gamma = L.ffn_norm;
+        p.norm_scale = &s->norm_s[1];
+        p.eps = c.eps;
+        p.epi = EPI_SILU_PAIR;
+        p.expert_sel = s->msel;
+        p.expert_slot = j;
+        p.expert_wstride = L.gu_wstride;
+        p.expert_sstride = L.gu_sstride;
+        p.trace = tslot("gateup");
+        if ((r = gemv_launch(p, st, true))) return r;
+        GemvParams q{};
+        q.nseg = 1;
+        q.seg[0] = seg_of(L.down, nullptr, s->meo + (size_t)j * D);
+        q.seg[0].rows = D;
+        q.K = FF;
+        q.act_mode = ACT_F32;
+        q.x = s->mh + (size_t)j * FF;
+        q.epi = EPI_STORE;
+        q.expert_sel = s->msel;
+        q.expert_slot = j;
+        q.expert_wstride = L.d_wstride;
+        q.expert_sstride = L.d_sstride;
+        q.trace = tslot("down");
+        if ((r = gemv_launch(q, st, true))) return r;
+    }
+    return launch_moe_combine(s->after, s->meo, s->mw, K, D, s->hidden, &s->norm_s[0], c.eps, st, true);
+}
+
 // Enqueues one token's kernels on s->stream.
 ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     ovf_model *m = s->m;
@@ -431,6 +542,10 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.trace = tslot("wo");
             if ((r = gemv_launch(p, st, true))) return r;
             prof_mark(st, "wo");
+        }
+        if (c.n_experts > 0) {
+            if ((r = enqueue_moe_ffn(s, L, st, tslot))) return r;
+            continue;
         }
         if (L.gate.type == L.up.type) {
             GemvParams p{};
@@ -596,6 +711,7 @@ ovf_status prefill_alloc(ovf_session *s) {
     A((void **)&s->pab, R * KM / 16 * 2);
     A((void **)&s->ptok, (size_t)(s->max_ctx + 1) * 4);
     A((void **)&s->pscale, 16);
+    if (!st && c.n_experts > 0) st = moe_rows_alloc(c, kPrefillRows, s->allocs, &s->pmoe);
     if (!st) s->pf_rows = kPrefillRows;
     return st;
 }
@@ -624,6 +740,7 @@ ovf_status project_rows(const ActRows &ar, const DevWeight &w, const float *bias
                                   rows, st, group, resid);
 }
 
+
 // Row buffers of one batch of hidden states ([rows][width] each).
 struct RowBufs {
     ActRows ar;
@@ -647,24 +764,73 @@ ovf_status rows_norm_qkv(const ovf_model *m, const DevLayer &L, const RowBufs &b
 
 // Wo (Q8_0, heads in order on the bias) + residual x -> a; RMSNorm(a) ->
 // n; gate/up; SiLU*up -> h; down + residual a -> x.
-ovf_status rows_wo_ffn(const ovf_model *m, const DevLayer &L, const RowBufs &b, int M, cudaStream_t st) {
+// SwiGLU of rows x ([M][D], normalized) through gate/up/down -> y ([M][D]),
+// optionally + resid.
+ovf_status rows_swiglu(const DevWeight &gate, const DevWeight &up, const DevWeight &down, const RowBufs &b,
+                       const float *x, float *y, const float *resid, int M, int D, int FF, cudaStream_t st) {
+    int fam = 0;
+    ovf_status r;
+    if ((r = quantize_rows_for(b.ar, gate, x, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, gate, nullptr, b.g, M, st))) return r;
+    if ((r = quantize_rows_for(b.ar, up, x, M, D, &fam, st))) return r;
+    if ((r = project_rows(b.ar, up, nullptr, b.u, M, st))) return r;
+    if ((r = launch_silu_mul(b.g, b.u, b.h, (int64_t)M * FF, st, false))) return r;
+    fam = 0;
+    if ((r = quantize_rows_for(b.ar, down, b.h, M, FF, &fam, st))) return r;
+    return project_rows(b.ar, down, nullptr, y, M, st, 0, resid);
+}
+
+// The FFN of M rows: b.a holds the residual stream after attention, b.n its
+// RMSNorm; the result (+ residual) lands in b.x.  Dense: one SwiGLU.  MoE
+// (MoeFeedForwardBlock.DecodeBatched, :140-243): route every row, group the
+// rows per expert (host round trip for the counts), run each used expert's
+// SwiGLU once over its rows, stash each output at the row's top-k slot and
+// sum the slots in top-k order, so every row equals a single-token decode.
+ovf_status rows_ffn(const ovf_model *m, const DevLayer &L, const RowBufs &b, MoeRows *mr, int M, cudaStream_t st) {
     const ovf_model_config &c = m->cfg;
-    const int D = c.d_model, QD = c.n_heads * c.head_dim, hd = c.head_dim, FF = c.d_ff;
+    const int D = c.d_model, FF = c.d_ff;
+    if (c.n_experts == 0) return rows_swiglu(L.gate, L.up, L.down, b, b.n, b.x, b.a, M, D, FF, st);
+    const int E = c.n_experts, K = c.n_experts_used, R = mr->cap;
+    ovf_status r;
+    if ((r = launch_moe_route(b.n, D, nullptr, nullptr, L.router, M, D, E, K, c.normalize_experts, mr->sel, mr->w, st,
+                              false)))
+        return r;
+    int32_t *hsel = mr->host, *hrows = mr->host + (size_t)R * K, *hslots = hrows + (size_t)E * R;
+    OVF_CUDA_TRY(cudaMemcpyAsync(hsel, mr->sel, (size_t)M * K * 4, cudaMemcpyDeviceToHost, st));
+    OVF_CUDA_TRY(cudaStreamSynchronize(st));
+    std::vector<int> count(E, 0);
+    for (int e = 0; e < E; ++e)
+        for (int n = 0; n < M; ++n)
+            for (int j = 0; j < K; ++j)
+                if (hsel[(size_t)n * K + j] == e) {
+                    hrows[(size_t)e * R + count[e]] = n;
+                    hslots[(size_t)e * R + count[e]] = j;
+                    ++count[e];
+                    break;
+                }
+    OVF_CUDA_TRY(cudaMemcpyAsync(mr->idx, hrows, (size_t)2 * E * R * 4, cudaMemcpyHostToDevice, st));
+    for (int e = 0; e < E; ++e) {
+        if (!count[e]) continue;
+        const int32_t *rows = mr->idx + (size_t)e * R, *slots = mr->idx + (size_t)E * R + (size_t)e * R;
+        if ((r = launch_gather_rows(b.n, rows, count[e], D, mr->gx, st))) return r;
+        if ((r = rows_swiglu(expert_view(L.gate, FF, e), expert_view(L.up, FF, e), expert_view(L.down, D, e), b, mr->gx,
+                             mr->eo, nullptr, count[e], D, FF, st)))
+            return r;
+        if ((r = launch_scatter_slots(mr->eo, rows, slots, count[e], K, D, mr->slot, st))) return r;
+    }
+    return launch_moe_combine_rows(b.a, mr->slot, mr->w, K, M, D, b.x, st);
+}
+
+ovf_status rows_wo_ffn(const ovf_model *m, const DevLayer &L, const RowBufs &b, MoeRows *mr, int M, cudaStream_t st) {
+    const ovf_model_config &c = m->cfg;
+    const int D = c.d_model, QD = c.n_heads * c.head_dim, hd = c.head_dim;
     int fam = 0;
     ovf_status r;
     if ((r = quantize_rows_for(b.ar, L.wo, b.att, M, QD, &fam, st))) return r;
     const int g = hd / 32 < QD / 32 ? hd / 32 : 0;
     if ((r = project_rows(b.ar, L.wo, L.bo, b.a, M, st, g, b.x))) return r;
     if ((r = launch_rmsnorm_rows(b.a, L.ffn_norm, b.n, M, D, c.eps, nullptr, st))) return r;
-    fam = 0;
-    if ((r = quantize_rows_for(b.ar, L.gate, b.n, M, D, &fam, st))) return r;
-    if ((r = project_rows(b.ar, L.gate, nullptr, b.g, M, st))) return r;
-    if ((r = quantize_rows_for(b.ar, L.up, b.n, M, D, &fam, st))) return r;
-    if ((r = project_rows(b.ar, L.up, nullptr, b.u, M, st))) return r;
-    if ((r = launch_silu_mul(b.g, b.u, b.h, (int64_t)M * FF, st, false))) return r;
-    fam = 0;
-    if ((r = quantize_rows_for(b.ar, L.down, b.h, M, FF, &fam, st))) return r;
-    return project_rows(b.ar, L.down, nullptr, b.x, M, st, 0, b.a);
+    return rows_ffn(m, L, b, mr, M, st);
 }
 
 // Enqueues the batched prefill of tokens [0, n) (already in s->ptok) at
@@ -678,6 +844,7 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n, bool all_rows = false)
     const int QD = H * hd, KD = KVH * hd;
     const int base = s->pos;
     const ActRows ar{s->paq, s->pas, s->pab};
+    const RowBufs pb{ar, s->px, s->pa, s->pn, s->pq, s->pk, s->pv, s->patt, s->pg, s->pu, s->ph};
     ovf_status r = OVF_OK;
     int last_rows = 0;
     for (int r0 = 0; r0 < n; r0 += s->pf_rows) {
@@ -721,21 +888,8 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n, bool all_rows = false)
                 if ((r = launch_kv_append_rows(a, s->pk, s->pv, M, base + r0, s->kv_dtype, st))) return r;
                 if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) return r;
             }
-            // Wo (Q8_0) per head, heads in order on the bias, + residual
-            fam = 0;
-            if ((r = quantize_rows_for(ar, L.wo, s->patt, M, QD, &fam, st))) return r;
-            const int g = hd / 32 < QD / 32 ? hd / 32 : 0;
-            if ((r = project_rows(ar, L.wo, L.bo, s->pa, M, st, g, s->px))) return r;
-            if ((r = launch_rmsnorm_rows(s->pa, L.ffn_norm, s->pn, M, D, c.eps, nullptr, st))) return r;
-            fam = 0;
-            if ((r = quantize_rows_for(ar, L.gate, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(ar, L.gate, nullptr, s->pg, M, st))) return r;
-            if ((r = quantize_rows_for(ar, L.up, s->pn, M, D, &fam, st))) return r;
-            if ((r = project_rows(ar, L.up, nullptr, s->pu, M, st))) return r;
-            if ((r = launch_silu_mul(s->pg, s->pu, s->ph, (int64_t)M * FF, st, false))) return r;
-            fam = 0;
-            if ((r = quantize_rows_for(ar, L.down, s->ph, M, FF, &fam, st))) return r;
-            if ((r = project_rows(ar, L.down, nullptr, s->px, M, st, 0, s->pa))) return r;
+            // Wo (Q8_0) per head, heads in order on the bias, + residual; FFN
+            if ((r = rows_wo_ffn(m, L, pb, &s->pmoe, M, st))) return r;
         }
     }
     if (all_rows) {
@@ -808,6 +962,7 @@ ovf_status batch_alloc(ovf_model *m) {
     A((void **)&m->btok, R * 4);
     A((void **)&m->bargmax, R * 4);
     if (!st && !m->btok_host) st = cuda_status(cudaMallocHost(&m->btok_host, R * 4), "cudaMallocHost");
+    if (!st && c.n_experts > 0) st = moe_rows_alloc(c, kBatchMax, m->allocs, &m->bmoe);
     if (!st) m->b_rows = kBatchMax;
     return st;
 }
@@ -849,7 +1004,7 @@ ovf_status enqueue_batch_decode(ovf_model *m, ovf_session *const *ss, int n, cud
             a.scale = 1.0f / sqrtf((float)hd);
             if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) return r;
         }
-        if ((r = rows_wo_ffn(m, L, rb, n, st))) return r;
+        if ((r = rows_wo_ffn(m, L, rb, &m->bmoe, n, st))) return r;
     }
     // final norm, LM head rows, argmax per row
     if ((r = launch_rmsnorm_rows(m->bx, m->final_norm, m->bn, n, D, c.eps, nullptr, st))) return r;
@@ -890,7 +1045,10 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
                   "ovf_model_create: config dimensions must be positive");
     OVF_CHECK_ARG(c.n_heads % c.n_kv_heads == 0, "ovf_model_create: n_heads must be a multiple of n_kv_heads");
     OVF_CHECK_ARG(c.head_dim % 32 == 0 && c.head_dim <= 256, "ovf_model_create: head_dim must be a multiple of 32, <= 256");
-    OVF_CHECK_ARG(c.n_experts == 0, "ovf_model_create: mixture-of-experts layers are not supported by this build");
+    OVF_CHECK_ARG(c.n_experts >= 0 && c.n_experts <= 64, "ovf_model_create: n_experts must be in [0, 64]");
+    OVF_CHECK_ARG(c.n_experts == 0 || (c.n_experts_used >= 1 && c.n_experts_used <= 8 &&
+                                       c.n_experts_used <= c.n_experts),
+                  "ovf_model_create: n_experts_used must be in [1, min(8, n_experts)]");
     OVF_CHECK_ARG(n_tensors == c.n_layers * OVF_TENSORS_PER_LAYER + 3, "ovf_model_create: expected %d tensors, got %d",
                   c.n_layers * OVF_TENSORS_PER_LAYER + 3, n_tensors);
     int ndev = 0;
@@ -916,9 +1074,36 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
         if (!st) st = upload_vec(m, lt[7], KD, &L.bv, "attn_v.bias");
         if (!st) st = upload_vec(m, lt[8], D, &L.bo, "attn_output.bias");
         if (!st) st = upload_vec(m, lt[9], D, &L.ffn_norm, "ffn_norm");
-        if (!st) st = upload_matrix(m, lt[10], c.d_ff, D, false, &L.gate, "ffn_gate");
-        if (!st) st = upload_matrix(m, lt[11], c.d_ff, D, false, &L.up, "ffn_up");
-        if (!st) st = upload_matrix(m, lt[12], D, c.d_ff, false, &L.down, "ffn_down");
+        const int64_t E = c.n_experts > 0 ? c.n_experts : 1;
+        if (!st) st = upload_matrix(m, lt[10], E * c.d_ff, D, false, &L.gate, "ffn_gate");
+        if (!st) st = upload_matrix(m, lt[11], E * c.d_ff, D, false, &L.up, "ffn_up");
+        if (!st) st = upload_matrix(m, lt[12], E * D, c.d_ff, false, &L.down, "ffn_down");
+        if (!st && c.n_experts > 0) {
+            // Mixtral: ffn_gate_inp as the input-major F32 router; experts stacked
+            ovf_tensor rt = lt[13];
+            if (!rt.data || rt.type != OVF_TYPE_F32 || rt.rows != D || rt.cols != c.n_experts) {
+                set_error("layer %d: MoE router must be F32 [d_model x n_experts] (input-major)", l);
+                st = OVF_EINVAL;
+            } else {
+                ovf_tensor flat{OVF_TYPE_F32, rt.data, 1, D * c.n_experts};
+                st = upload_vec(m, flat, D * c.n_experts, &L.router, "ffn_gate_inp");
+            }
+            if (!st && (L.gate.type != L.up.type)) {
+                set_error("layer %d: MoE gate and up experts must share a type", l);
+                st = OVF_EINVAL;
+            }
+            if (!st) {
+                expert_strides(L.gate, c.d_ff, &L.gu_wstride, &L.gu_sstride);
+                expert_strides(L.down, D, &L.d_wstride, &L.d_sstride);
+                if (L.gu_wstride % 16 || L.gu_sstride % 16 || L.d_wstride % 16 || L.d_sstride % 16) {
+                    set_error("layer %d: expert matrices must be multiples of 16 bytes", l);
+                    st = OVF_EINVAL;
+                }
+                // a decode step streams n_experts_used of the n_experts
+                m->weight_bytes -= (int64_t)(c.n_experts - c.n_experts_used) *
+                                   (2 * (L.gu_wstride + L.gu_sstride) + L.d_wstride + L.d_sstride);
+            }
+        }
         if (!st && (!L.attn_norm || !L.ffn_norm)) {
             set_error("layer %d: norms are required", l);
             st = OVF_EINVAL;
@@ -973,6 +1158,7 @@ ovf_status ovf_model_destroy(ovf_model *m) {
     if (!m) return OVF_OK;
     DeviceGuard guard(m->device);
     if (m->btok_host) cudaFreeHost(m->btok_host);
+    if (m->bmoe.host) cudaFreeHost(m->bmoe.host);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return OVF_OK;
@@ -1033,6 +1219,12 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     A((void **)&s->tokens_log, (size_t)(max_ctx + 1) * 4);
     A((void **)&s->step, sizeof(DevStep));
     A((void **)&s->err_slot, sizeof(int));
+    if (c.n_experts > 0) {
+        A((void **)&s->msel, (size_t)c.n_experts_used * 4);
+        A((void **)&s->mw, (size_t)c.n_experts_used * 4);
+        A((void **)&s->mh, (size_t)c.n_experts_used * c.d_ff * 4);
+        A((void **)&s->meo, (size_t)c.n_experts_used * D * 4);
+    }
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
     if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
     if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
@@ -1061,6 +1253,7 @@ ovf_status ovf_session_destroy(ovf_session *s) {
     if (s->graph_nologits) cudaGraphExecDestroy(s->graph_nologits);
     for (void *p : s->allocs) cudaFree(p);
     if (s->pinned_tok) cudaFreeHost(s->pinned_tok);
+    if (s->pmoe.host) cudaFreeHost(s->pmoe.host);
     if (s->stream) cudaStreamDestroy(s->stream);
     delete s;
     return OVF_OK;

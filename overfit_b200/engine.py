@@ -48,6 +48,24 @@ def tensor_of(entry) -> tuple:
     return (t, np.ascontiguousarray(data), rows, cols)
 
 
+def moe_layer_entries(layer: dict) -> dict:
+    """A Mixtral layer (``router`` [d_model x n_experts] F32 input-major,
+    ``experts`` = [{gate, up, down}] in file formats) as the tensor table
+    wants it: the experts' matrices back to back in one entry per kind."""
+    if "experts" not in layer:
+        return layer
+    out = dict(layer)
+    r = np.ascontiguousarray(layer["router"], dtype=np.float32)
+    out["router"] = (TYPE_F32, r.reshape(-1), r.shape[0], r.shape[1])
+    for k in ("gate", "up", "down"):
+        parts = [tensor_of(ex[k]) for ex in layer["experts"]]
+        t = parts[0][0]
+        if any(p[0] != t for p in parts):
+            raise ValueError(f"experts' {k} matrices must share a type")
+        out[k] = (t, np.concatenate([p[1].reshape(-1) for p in parts]), sum(p[2] for p in parts), parts[0][3])
+    return out
+
+
 def tensor_table(cfg: dict, model_file: dict):
     """Builds the ovf_tensor table (include/ovf.h) and the list of arrays it
     points into (keep it alive until ovf_model_create returns)."""
@@ -55,6 +73,7 @@ def tensor_table(cfg: dict, model_file: dict):
     table = (Tensor * (nl * TENSORS_PER_LAYER + 3))()
     keep = []
     for l, layer in enumerate(model_file["layers"]):
+        layer = moe_layer_entries(layer)
         for j, key in enumerate(LAYER_KEYS):
             t, data, rows, cols = tensor_of(layer.get(key))
             if data is not None:

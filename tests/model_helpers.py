@@ -13,6 +13,9 @@ Q4KM = dict(wq=orc.Q4_K, wk=orc.Q4_K, wv=orc.Q6_K, wo=orc.Q4_K, gate=orc.Q4_K, u
 
 TINY_LLAMA = dict(n_layers=2, d_model=512, n_heads=8, n_kv_heads=2, head_dim=64, d_ff=1024, vocab=2000,
                   theta=500000.0, eps=1e-6, rope_split_half=0, tied=False, qkv_bias=False, scheme="q4_k_m")
+TINY_MIXTRAL = dict(n_layers=2, d_model=512, n_heads=8, n_kv_heads=2, head_dim=64, d_ff=512, vocab=1000,
+                    theta=1000000.0, eps=1e-6, rope_split_half=0, tied=False, qkv_bias=False, scheme="q4_k_m",
+                    n_experts=4, n_experts_used=2, normalize_experts=1)
 TINY_QWEN = dict(n_layers=2, d_model=224, n_heads=7, n_kv_heads=1, head_dim=32, d_ff=608, vocab=1500,
                  theta=1000000.0, eps=1e-6, rope_split_half=1, tied=True, qkv_bias=True, scheme="q8_0")
 
@@ -35,11 +38,20 @@ def make_model_file(cfg: dict, seed: int, std: float = 0.02) -> dict:
         return rng.normal(0, std, size=n).astype(np.float32)
 
     layers = []
+    E = cfg.get("n_experts", 0)
     for _ in range(cfg["n_layers"]):
         L = dict(attn_norm=(1 + rng.normal(0, 0.1, D)).astype(np.float32),
                  ffn_norm=(1 + rng.normal(0, 0.1, D)).astype(np.float32),
                  wq=mat(H * hd, D, "wq"), wk=mat(KVH * hd, D, "wk"), wv=mat(KVH * hd, D, "wv"),
-                 wo=mat(D, H * hd, "wo"), gate=mat(FF, D, "gate"), up=mat(FF, D, "up"), down=mat(D, FF, "down"))
+                 wo=mat(D, H * hd, "wo"))
+        if E:
+            # Mixtral: ffn_gate_inp as the loader hands it to the engine,
+            # input-major F32 [d_model x n_experts]; experts in file formats
+            L["router"] = rng.normal(0, std * 5, size=(D, E)).astype(np.float32)
+            L["experts"] = [dict(gate=mat(FF, D, "gate"), up=mat(FF, D, "up"), down=mat(D, FF, "down"))
+                            for _ in range(E)]
+        else:
+            L.update(gate=mat(FF, D, "gate"), up=mat(FF, D, "up"), down=mat(D, FF, "down"))
         if cfg.get("qkv_bias"):
             L.update(bq=vec(H * hd), bk=vec(KVH * hd), bv=vec(KVH * hd))
         layers.append(L)
@@ -64,8 +76,14 @@ def oracle_weights(model_file: dict) -> dict:
     layers = []
     for L in model_file["layers"]:
         o = dict(attn_norm=L["attn_norm"], ffn_norm=L["ffn_norm"])
-        for k in ("wq", "wk", "wv", "gate", "up", "down"):
+        for k in ("wq", "wk", "wv"):
             o[k] = _resident(L[k])
+        if "experts" in L:
+            o["router"] = np.ascontiguousarray(L["router"], dtype=np.float32).reshape(-1)
+            o["experts"] = [{k: _resident(ex[k]) for k in ("gate", "up", "down")} for ex in L["experts"]]
+        else:
+            for k in ("gate", "up", "down"):
+                o[k] = _resident(L[k])
         o["wo"] = _resident(L["wo"], force_q8=True)
         for b in ("bq", "bk", "bv", "bo"):
             o[b] = L.get(b)
