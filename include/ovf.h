@@ -229,6 +229,31 @@ typedef struct {
 ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const ovf_tensor *tensors,
                             int32_t n_tensors, ovf_model **out);
 ovf_status ovf_model_destroy(ovf_model *m);
+
+/* Tensor parallelism over `world` GPUs (one process per GPU), the north
+ * star's split of Llama-family models: rank r holds query heads
+ * [r*H/world, (r+1)*H/world) with their KV heads (Q/K/V rows, attn_output
+ * columns, its share of the KV cache), FFN rows [r*F/world, ...) of gate/up
+ * and the same columns of down, and vocabulary rows of the LM head; the
+ * embedding and norms are replicated.  Every rank passes the FULL tensor
+ * table; the library uploads only its shard (shard-aware upload of the
+ * loader's slices, GgufLlamaLoader.cs:45-531).  The per-head outputs
+ * (CachedMultiHeadAttention.cs:221-298), the down projection's super-block
+ * terms and the logits are exchanged over NVLink through peer memory, and
+ * every rank adds them in the reference's order, so the results are
+ * bit-identical to one GPU.  Requires n_kv_heads, d_ff/256 and vocab
+ * divisible by world (world <= 8); no MoE.  After creation, exchange the
+ * ranks' OVF_TP_HANDLE_BYTES handles (ovf_model_tp_export) between the
+ * processes and call ovf_model_tp_connect with all of them in rank order.
+ * Sessions then run in lockstep: every rank makes the same calls in the
+ * same order (a rank that stops makes the others' next step fail with
+ * OVF_ETIMEDOUT after about a second).  Prompts take the single-token loop;
+ * batch decode and speculative verify return OVF_EUNSUPPORTED. */
+#define OVF_TP_HANDLE_BYTES 64
+ovf_status ovf_model_create_tp(int32_t device, const ovf_model_config *cfg, const ovf_tensor *tensors,
+                               int32_t n_tensors, int32_t rank, int32_t world, ovf_model **out);
+ovf_status ovf_model_tp_export(ovf_model *m, void *handle_out);
+ovf_status ovf_model_tp_connect(ovf_model *m, const void *handles);
 /* Device bytes of resident weights (for bandwidth accounting). */
 int64_t ovf_model_weight_bytes(const ovf_model *m);
 

@@ -22,6 +22,7 @@ OVF_ESTATE = -6
 OVF_EUNSUPPORTED = -7
 OVF_EBUSY = -8
 OPT_PREFILL_SINGLE = 1
+TP_HANDLE_BYTES = 64
 
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 8, 12, 14
 TENSORS_PER_LAYER = 14
@@ -92,6 +93,9 @@ SIGNATURES = {
     "ovf_session_stream": (P, [P]),
     "ovf_session_decode_batch": (I32, [P, I32, P, P, P]),
     "ovf_session_set_option": (I32, [P, I32, I32]),
+    "ovf_model_create_tp": (I32, [I32, P, P, I32, I32, I32, P]),
+    "ovf_model_tp_export": (I32, [P, P]),
+    "ovf_model_tp_connect": (I32, [P, P]),
     "ovf_session_verify": (I32, [P, P, I32, P, P]),
     "ovf_session_truncate": (I32, [P, I32]),
     "ovf_session_prefix_bytes": (I64, [P]),

@@ -55,7 +55,7 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Device-side error word (per device, per library instance).  Kernels set it
 // when a bounded wait gives up; the host reads it with ovf_device_error.
-enum : int { DEVERR_NONE = 0, DEVERR_MBAR_TIMEOUT = 1, DEVERR_COUNTER = 2 };
+enum : int { DEVERR_NONE = 0, DEVERR_MBAR_TIMEOUT = 1, DEVERR_COUNTER = 2, DEVERR_TP_TIMEOUT = 3 };
 // Defined once: the library is a single translation unit (csrc/ovf_lib.cu).
 __device__ int g_dev_error = 0;
 

@@ -742,6 +742,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                 __syncwarp();
                 if (!valid) continue;
                 const float *tb = tbuf + (size_t)j * T * nb;
+                if (p.epi == EPI_TERMS_TP) {
+                    // every block term of the row to every rank, block-major
+                    const float *tr = tb + (size_t)slot * nb;
+                    for (int m = 0; m < nb; ++m) {
+                        const float v = tr[m];
+                        const size_t o = (size_t)(p.tp_index0 + m) * p.tp_rows + row;
+                        for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][o] = v;
+                    }
+                    continue;
+                }
                 float y[2] = {0.0f, 0.0f};
                 for (int k = 0; k < (p.pair ? 2 : 1); ++k) {
                     const float *tr = tb + (size_t)(slot + k * half) * nb;
@@ -751,7 +761,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                         // head-ordered sum: each group of G blocks summed in
                         // order, the group sums added in order on the bias
                         float acc = hb ? bv : 0.0f, grp = 0.0f;
-                        int gp = 0;
+                        int gp = 0, gi = 0;
+                        const bool to_ranks = p.epi == EPI_GROUPS_TP;
                         int m = 0;
                         for (; m + 8 <= nb; m += 8) {
                             float v[8];
@@ -761,16 +772,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                             for (int q = 0; q < 8; ++q) {
                                 grp = gp == 0 ? fadd(0.0f, v[q]) : fadd(grp, v[q]);
                                 if (++gp == G) {
+                                    if (to_ranks) {
+                                        const size_t o = (size_t)(p.tp_index0 + gi) * p.tp_rows + row;
+                                        for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][o] = grp;
+                                    }
                                     acc = fadd(acc, grp);
                                     gp = 0;
+                                    ++gi;
                                 }
                             }
                         }
                         for (; m < nb; ++m) {
                             grp = gp == 0 ? fadd(0.0f, tr[m]) : fadd(grp, tr[m]);
                             if (++gp == G) {
+                                if (to_ranks) {
+                                    const size_t o = (size_t)(p.tp_index0 + gi) * p.tp_rows + row;
+                                    for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][o] = grp;
+                                }
                                 acc = fadd(acc, grp);
                                 gp = 0;
+                                ++gi;
                             }
                         }
                         y[k] = acc;
@@ -785,13 +806,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                             for (int q = 0; q < 8; ++q) sum = fadd(sum, v[q]);
                         }
                         for (; m < nb; ++m) sum = fadd(sum, tr[m]);
+                        if (p.epi == EPI_GROUPS_TP) {  // one group: the whole row
+                            const size_t o = (size_t)p.tp_index0 * p.tp_rows + row;
+                            for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][o] = sum;
+                        }
                         y[k] = hb ? fadd(bv, sum) : sum;
                     }
                 }
                 if (p.epi == EPI_SILU_PAIR) {
                     const float sg = fdiv(1.0f, fadd(1.0f, exp_libm(-y[0])));
                     p.seg[0].out[row] = fmul(fmul(y[0], sg), y[1]);
-                } else {
+                } else if (p.epi == EPI_LOGITS_TP) {
+                    const int grow = p.tp_index0 + row;
+                    for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][grow] = y[0];
+                    const unsigned long long kk = argmax_key(y[0], grow);
+                    best = kk > best ? kk : best;
+                } else if (p.epi != EPI_GROUPS_TP) {
                     float *out = p.seg[seg].out;
                     if (p.epi == EPI_RESIDUAL) out[row] = fadd(res, y[0]);
                     else out[row] = y[0];
@@ -803,6 +833,29 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&B.tfree[j]);
+        }
+        if (p.epi >= EPI_GROUPS_TP) __threadfence_system();  // the peers' copies before the kernel ends
+        if (p.epi == EPI_LOGITS_TP) {
+            // warp max -> one global atomic per CTA; the last CTA to finish
+            // publishes this rank's winning key to every rank
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+                best = other > best ? other : best;
+            }
+            if (lane == 0) {
+                if (best) atomicMax(&p.step->argmax_key, best);
+                __threadfence();
+                const int ticket = atomicAdd(&p.step->done_ctas, 1);
+                if (ticket == (int)gridDim.x - 1) {
+                    __threadfence();
+                    const unsigned long long k = atomicAdd(&p.step->argmax_key, 0ull);
+                    for (int w = 0; w < p.tp_world; ++w) p.tp_keys[w][p.tp_rank] = k;
+                    p.step->argmax_key = 0ull;
+                    p.step->done_ctas = 0;
+                    __threadfence_system();
+                }
+            }
         }
         if (p.epi == EPI_LOGITS_ARGMAX) {
             // warp max -> one global atomic per CTA; the last CTA to finish
@@ -960,7 +1013,15 @@ ovf_status gemv_launch(GemvParams p, cudaStream_t stream, bool pdl, GemvPlan *pl
         OVF_CHECK_ARG(p.epi == EPI_RESIDUAL && p.nseg == 1,
                       "gemv: an output RMSNorm needs a single-segment residual launch");
     if (p.act_mode == ACT_F32_RMSNORM) OVF_CHECK_ARG(p.norm_scale != nullptr, "gemv: RMSNorm input without its scale");
-    if (p.epi == EPI_LOGITS_ARGMAX) OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
+    if (p.epi == EPI_LOGITS_ARGMAX || p.epi == EPI_LOGITS_TP)
+        OVF_CHECK_ARG(p.step != nullptr, "gemv: argmax epilogue without step state");
+    if (p.epi >= EPI_GROUPS_TP) {
+        OVF_CHECK_ARG(p.tp_world >= 1 && p.tp_world <= 8 && p.nseg == 1 && !p.pair && !p.norm_out,
+                      "gemv: tensor-parallel epilogue needs one segment and 1..8 ranks");
+        for (int w = 0; w < p.tp_world; ++w)
+            OVF_CHECK_ARG(p.tp_dst[w] && (p.epi != EPI_LOGITS_TP || p.tp_keys[w]), "gemv: missing exchange buffer");
+        if (p.epi == EPI_GROUPS_TP) OVF_CHECK_ARG(!kq && p.q8_group > 0, "gemv: head outputs need grouped Q8_0");
+    }
     if (p.expert_sel)
         OVF_CHECK_ARG(p.expert_wstride % 16 == 0 && p.expert_sstride % 16 == 0 && p.expert_slot >= 0 && !p.norm_out,
                       "gemv: routed expert weights need 16-byte strides and no output norm");

@@ -25,6 +25,11 @@ enum EpiMode : int {
     EPI_RESIDUAL = 1,       // out[row] = resid[row] + (bias + sum)
     EPI_SILU_PAIR = 2,      // seg0 = gate, seg1 = up: out[row] = silu(gate)*up
     EPI_LOGITS_ARGMAX = 3,  // out[row] = sum; greedy argmax tracked in DevStep
+    // tensor-parallel epilogues: results go to the exchange buffer of every
+    // rank (tp_dst[w], w < tp_world) instead of out
+    EPI_GROUPS_TP = 4,      // Q8_0 groups (heads): dst[(tp_index0 + group) * tp_rows + row] = group sum
+    EPI_TERMS_TP = 5,       // every block's term: dst[(tp_index0 + block) * tp_rows + row]
+    EPI_LOGITS_TP = 6,      // dst[tp_index0 + row] = sum; the rank's argmax key goes to tp_keys[w][tp_rank]
 };
 
 // Device-resident per-session step state (greedy loop without host syncs).
@@ -83,6 +88,9 @@ struct GemvParams {
     int *tokens_out;     // EPI_LOGITS_ARGMAX: generated token log (optional)
     const int *expert_sel;  // routed expert: segment weights are offset by expert_sel[expert_slot] * stride
     int expert_slot;        // (read after griddepcontrol.wait; no weight is staged before it)
+    float *tp_dst[8];       // EPI_*_TP: every rank's exchange buffer (peer pointers)
+    unsigned long long *tp_keys[8];  // EPI_LOGITS_TP: every rank's argmax key table
+    int tp_world, tp_rank, tp_index0, tp_rows;
     int64_t expert_wstride;  // bytes between experts' quants
     int64_t expert_sstride;  // bytes between experts' Q8_0 scales
     L2Prefetch pf;       // weights of a later launch to pull into L2 once this one's are issued

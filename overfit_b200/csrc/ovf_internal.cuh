@@ -114,7 +114,18 @@ ovf_status launch_batch_finish(DevStep *step, int cur, int next, const int32_t *
 ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float *s, int split_half, cudaStream_t st);
 ovf_status launch_embed(const DevStep *step, int type, const void *w, const float *q8s, int d, float *hidden,
                         DevStep *step_mut, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st,
-                        bool pdl);
+                        bool pdl, unsigned *epoch = nullptr);
+// ovf_tp.cu: tensor-parallel exchange (flags in every rank's arena).
+struct TpExchange {
+    unsigned *flags_peer[8];  // every rank's flag table [slots][world]
+    const unsigned *flags_own;
+    const unsigned *epoch;    // this rank's step epoch (bumped by the embedding kernel)
+    int world, rank, slot;
+};
+ovf_status launch_tp_sum_combine(const TpExchange &x, const float *recv, int n, const float *bias, const float *resid,
+                                 float *out, float *norm_out, int D, float eps, cudaStream_t st, bool pdl);
+ovf_status launch_tp_lm_finish(const TpExchange &x, const unsigned long long *keys, DevStep *step, int32_t *tokens_log,
+                               cudaStream_t st, bool pdl);
 // ovf_moe.cu: router, combine, row gather/scatter of the MoE FFN.
 ovf_status launch_moe_route(const float *x, int ld_x, const float *gamma, const float *norm_scale, const float *R,
                             int rows, int D, int E, int K, int normalize, int32_t *sel, float *w, cudaStream_t st,

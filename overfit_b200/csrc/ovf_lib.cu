@@ -7,6 +7,7 @@
 #include "ovf_batched.cu"
 #include "ovf_ops.cu"
 #include "ovf_moe.cu"
+#include "ovf_tp.cu"
 #include "ovf_attn_cluster.cu"
 #include "ovf_attn_group.cu"
 #include "ovf_attn_exact.cu"

@@ -100,6 +100,14 @@ struct ovf_model {
     int32_t *btok_host = nullptr;  // pinned
     std::atomic<bool> batch_busy{false};  // one ovf_session_decode_batch at a time per model
     MoeRows bmoe;                          // MoE scratch of the batch rows
+    // tensor parallelism (world > 1): this rank's share of heads, FFN rows
+    // and vocabulary; the exchange arena (IPC-exported) and the peers'
+    int tp_rank = 0, tp_world = 1;
+    int h_loc = 0, kvh_loc = 0, ff_loc = 0, v_loc = 0, nb_down = 0;  // nb_down: down blocks of all ranks
+    char *arena = nullptr;
+    size_t arena_bytes = 0, off_heads = 0, off_terms = 0, off_logits = 0, off_keys = 0, off_flags = 0, off_epoch = 0;
+    char *peer[8] = {};
+    bool tp_ready = false;
 };
 
 struct ovf_session {
@@ -180,6 +188,44 @@ int64_t tensor_bytes(int type, int64_t rows, int64_t cols) {
     }
 }
 
+int64_t host_row_bytes(int type, int64_t cols) {
+    switch (type) {
+        case OVF_TYPE_F32: return cols * 4;
+        case OVF_TYPE_Q8_0: return cols / 32 * 34;
+        case OVF_TYPE_Q4_K: return cols / 256 * 144;
+        case OVF_TYPE_Q6_K: return cols / 256 * 210;
+        default: return -1;
+    }
+}
+
+// Rows [r0, r0 + n) of a host tensor (a view, no copy).
+ovf_tensor host_rows(const ovf_tensor &t, int64_t r0, int64_t n) {
+    ovf_tensor v = t;
+    if (t.data) v.data = static_cast<const char *>(t.data) + r0 * host_row_bytes(t.type, t.cols);
+    v.rows = n;
+    return v;
+}
+
+// Columns [k0, k0 + kn) of every row of a host tensor, gathered into `buf`
+// (k0, kn multiples of the block length).
+ovf_tensor host_cols(const ovf_tensor &t, int64_t k0, int64_t kn, std::vector<uint8_t> &buf) {
+    const int64_t rb = host_row_bytes(t.type, t.cols), ob = host_row_bytes(t.type, k0), nb = host_row_bytes(t.type, kn);
+    buf.resize((size_t)(t.rows * nb));
+    for (int64_t r = 0; r < t.rows; ++r)
+        memcpy(buf.data() + r * nb, static_cast<const char *>(t.data) + r * rb + ob, (size_t)nb);
+    ovf_tensor v{t.type, buf.data(), t.rows, kn};
+    return v;
+}
+
+// A slice [i0, i0 + n) of an F32 vector tensor.
+ovf_tensor host_vec_slice(const ovf_tensor &t, int64_t i0, int64_t n) {
+    ovf_tensor v = t;
+    if (t.data) v.data = static_cast<const float *>(t.data) + i0;
+    v.rows = 1;
+    v.cols = n;
+    return v;
+}
+
 // Uploads an f32 vector (norm / bias).
 ovf_status upload_vec(ovf_model *m, const ovf_tensor &t, int64_t n, float **out, const char *what) {
     *out = nullptr;
@@ -233,6 +279,38 @@ ovf_status upload_matrix(ovf_model *m, const ovf_tensor &t, int64_t rows, int64_
     }
     cudaFree(staging);
     if (e != cudaSuccess) return cuda_status(e, what);
+    return st;
+}
+
+// Tensor parallelism: the columns [c0, c0 + cn) (this rank's heads) of
+// attn_output after the loader's Q8_0 re-quantization of the whole matrix
+// (GgufLlamaLoader.cs:977-995: per-head Q8_0 blocks never cross a head).
+ovf_status upload_wo_local(ovf_model *m, const ovf_tensor &t, int64_t rows, int64_t cols, int64_t c0, int64_t cn,
+                           DevWeight *w) {
+    DevWeight full;
+    std::vector<void *> keep;
+    std::swap(keep, m->allocs);
+    const int64_t before = m->weight_bytes;
+    ovf_status st = upload_matrix(m, t, rows, cols, true, &full, "attn_output");
+    std::swap(keep, m->allocs);  // `keep` now holds the full matrix's buffers
+    m->weight_bytes = before;
+    if (!st) {
+        w->type = OVF_TYPE_Q8_0;
+        w->rows = rows;
+        w->cols = cn;
+        st = dalloc(m->allocs, (void **)&w->data, (size_t)(rows * cn));
+        if (!st) st = dalloc(m->allocs, (void **)&w->scales, (size_t)(rows * cn / 32 * 4));
+        if (!st)
+            st = cuda_status(cudaMemcpy2D(w->data, (size_t)cn, full.data + c0, (size_t)cols, (size_t)cn, (size_t)rows,
+                                          cudaMemcpyDeviceToDevice),
+                             "attn_output slice");
+        if (!st)
+            st = cuda_status(cudaMemcpy2D(w->scales, (size_t)(cn / 32 * 4), full.scales + c0 / 32, (size_t)(cols / 32 * 4),
+                                          (size_t)(cn / 32 * 4), (size_t)rows, cudaMemcpyDeviceToDevice),
+                             "attn_output scales slice");
+        m->weight_bytes += rows * cn + rows * cn / 8;
+    }
+    for (void *q : keep) cudaFree(q);
     return st;
 }
 
@@ -428,12 +506,33 @@ ovf_status enqueue_moe_ffn(ovf_session *s, const DevLayer &L, cudaStream_t st, S
     return launch_moe_combine(s->after, s->meo, s->mw, K, D, s->hidden, &s->norm_s[0], c.eps, st, true);
 }
 
+// Tensor parallelism: the exchange slot `slot` of the model's arena.
+TpExchange tp_exchange(const ovf_model *m, int slot) {
+    TpExchange x{};
+    for (int w = 0; w < m->tp_world; ++w) x.flags_peer[w] = reinterpret_cast<unsigned *>(m->peer[w] + m->off_flags);
+    x.flags_own = reinterpret_cast<const unsigned *>(m->arena + m->off_flags);
+    x.epoch = reinterpret_cast<const unsigned *>(m->arena + m->off_epoch);
+    x.world = m->tp_world;
+    x.rank = m->tp_rank;
+    x.slot = slot;
+    return x;
+}
+
+// Every rank's exchange buffer at byte offset `off` + `elem` floats.
+void tp_dsts(const ovf_model *m, size_t off, size_t elem, GemvParams *p) {
+    for (int w = 0; w < m->tp_world; ++w) p->tp_dst[w] = reinterpret_cast<float *>(m->peer[w] + off) + elem;
+    p->tp_world = m->tp_world;
+    p->tp_rank = m->tp_rank;
+}
+
 // Enqueues one token's kernels on s->stream.
 ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     ovf_model *m = s->m;
     const ovf_model_config &c = m->cfg;
     const cudaStream_t st = s->stream;
-    const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim;
+    const bool tp = m->tp_world > 1;
+    // this rank's heads (all of them on one GPU)
+    const int D = c.d_model, H = m->h_loc, KVH = m->kvh_loc, hd = c.head_dim;
     s->trace_n = 0;
     auto tslot = [&](const char *label) -> TraceSlot * {
         if (!s->trace || s->trace_n >= s->trace_cap) return nullptr;
@@ -442,7 +541,8 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
     };
     if (s->trace) OVF_CUDA_TRY(cudaMemsetAsync(s->trace, 0, (size_t)s->trace_cap * sizeof(TraceSlot), st));
     ovf_status r = launch_embed(s->step, m->embed.type, m->embed.data, m->embed.scales, D, s->hidden, s->step,
-                                &s->norm_s[0], c.eps, tslot("embed"), st, true);
+                                &s->norm_s[0], c.eps, tslot("embed"), st, true,
+                                tp ? reinterpret_cast<unsigned *>(m->arena + m->off_epoch) : nullptr);
     prof_mark(st, "embed");
     if (r) return r;
     for (int l = 0; l < c.n_layers; ++l) {
@@ -463,7 +563,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.norm_scale = &s->norm_s[0];
             p.eps = c.eps;
             p.epi = EPI_STORE;
-            p.fill_sentinel = s->after;  // Wo's norm CTA watches `after` being written
+            p.fill_sentinel = tp ? nullptr : s->after;  // Wo's norm CTA watches `after` being written
             p.fill_n = D;
             p.trace = tslot("qkv");
             if ((r = gemv_launch(p, st, true))) return r;
@@ -483,7 +583,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.norm_scale = &s->norm_s[0];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
-                if (i == 0) {
+                if (i == 0 && !tp) {
                     p.fill_sentinel = s->after;
                     p.fill_n = D;
                 }
@@ -534,13 +634,29 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.q8_group = hd / 32;
             p.act_mode = ACT_F32;
             p.x = s->attn;
-            p.epi = EPI_RESIDUAL;
-            p.resid = s->hidden;
-            p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
+            if (tp) {
+                // this rank's heads' outputs into every rank's exchange buffer
+                p.seg[0].bias = nullptr;
+                p.epi = EPI_GROUPS_TP;
+                tp_dsts(m, m->off_heads, (size_t)l * c.n_heads * D, &p);
+                p.tp_index0 = m->tp_rank * H;
+                p.tp_rows = D;
+            } else {
+                p.epi = EPI_RESIDUAL;
+                p.resid = s->hidden;
+                p.norm_out = &s->norm_s[1];  // RMSNorm scale of `after` for the FFN
+            }
             if (l2_prefetch_mode() & 4) add_prefetch(p.pf, L.down);
             p.eps = c.eps;
             p.trace = tslot("wo");
             if ((r = gemv_launch(p, st, true))) return r;
+            if (tp) {
+                // after = hidden + (((bias + y_0) + y_1) + ...), every head in order
+                const float *recv = reinterpret_cast<const float *>(m->arena + m->off_heads) + (size_t)l * c.n_heads * D;
+                if ((r = launch_tp_sum_combine(tp_exchange(m, 2 * l), recv, c.n_heads, L.bo, s->hidden, s->after,
+                                               &s->norm_s[1], D, c.eps, st, true)))
+                    return r;
+            }
             prof_mark(st, "wo");
         }
         if (c.n_experts > 0) {
@@ -560,7 +676,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
             p.norm_scale = &s->norm_s[1];
             p.eps = c.eps;
             p.epi = EPI_SILU_PAIR;
-            p.fill_sentinel = s->hidden;  // the down projection's norm CTA watches `hidden`
+            p.fill_sentinel = tp ? nullptr : s->hidden;  // the down projection's norm CTA watches `hidden`
             p.fill_n = D;
             if ((l2_prefetch_mode() & 8) && l + 1 < c.n_layers) {
                 const DevLayer &N = m->layers[l + 1];
@@ -585,7 +701,7 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 p.norm_scale = &s->norm_s[1];
                 p.eps = c.eps;
                 p.epi = EPI_STORE;
-                if (i == 0) {
+                if (i == 0 && !tp) {
                     p.fill_sentinel = s->hidden;
                     p.fill_n = D;
                 }
@@ -593,22 +709,37 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
                 if ((r = gemv_launch(p, st, true))) return r;
                 prof_mark(st, "gateup");
             }
-            if ((r = launch_silu_mul(s->gtmp, s->utmp, s->h, c.d_ff, st, true))) return r;
+            if ((r = launch_silu_mul(s->gtmp, s->utmp, s->h, m->ff_loc, st, true))) return r;
             prof_mark(st, "gateup");
         }
         {
             GemvParams p{};
             p.nseg = 1;
             p.seg[0] = seg_of(L.down, nullptr, s->hidden);
-            p.K = c.d_ff;
+            p.K = m->ff_loc;
             p.act_mode = ACT_F32;
             p.x = s->h;
-            p.epi = EPI_RESIDUAL;
-            p.resid = s->after;
-            p.norm_out = &s->norm_s[0];  // RMSNorm scale of the new hidden: next layer / final norm
+            if (tp) {
+                // this rank's block terms of every row into every rank's buffer
+                p.epi = EPI_TERMS_TP;
+                tp_dsts(m, m->off_terms, (size_t)l * m->nb_down * D, &p);
+                p.tp_index0 = m->tp_rank * (m->nb_down / m->tp_world);
+                p.tp_rows = D;
+            } else {
+                p.epi = EPI_RESIDUAL;
+                p.resid = s->after;
+                p.norm_out = &s->norm_s[0];  // RMSNorm scale of the new hidden: next layer / final norm
+            }
             p.eps = c.eps;
             p.trace = tslot("down");
             if ((r = gemv_launch(p, st, true))) return r;
+            if (tp) {
+                // hidden = after + (((0 + t_0) + t_1) + ...), every block in order
+                const float *recv = reinterpret_cast<const float *>(m->arena + m->off_terms) + (size_t)l * m->nb_down * D;
+                if ((r = launch_tp_sum_combine(tp_exchange(m, 2 * l + 1), recv, m->nb_down, nullptr, s->after,
+                                               s->hidden, &s->norm_s[0], D, c.eps, st, true)))
+                    return r;
+            }
             prof_mark(st, "down");
         }
     }
@@ -625,8 +756,24 @@ ovf_status enqueue_step(ovf_session *s, bool with_logits) {
         p.epi = EPI_LOGITS_ARGMAX;
         p.step = s->step;
         p.tokens_out = s->tokens_log;
+        if (tp) {
+            // this rank's vocabulary rows into every rank's logits, keys published
+            p.epi = EPI_LOGITS_TP;
+            tp_dsts(m, m->off_logits, 0, &p);
+            for (int w = 0; w < m->tp_world; ++w)
+                p.tp_keys[w] = reinterpret_cast<unsigned long long *>(m->peer[w] + m->off_keys);
+            p.tp_index0 = m->tp_rank * m->v_loc;
+        }
         p.trace = tslot("lmhead");
         if ((r = gemv_launch(p, st, true))) return r;
+        if (tp) {
+            if ((r = launch_tp_lm_finish(tp_exchange(m, 2 * c.n_layers),
+                                         reinterpret_cast<const unsigned long long *>(m->arena + m->off_keys), s->step,
+                                         s->tokens_log, st, true)))
+                return r;
+            OVF_CUDA_TRY(cudaMemcpyAsync(s->logits, m->arena + m->off_logits, (size_t)c.vocab * 4,
+                                         cudaMemcpyDeviceToDevice, st));
+        }
         prof_mark(st, "lmhead");
     }
     return OVF_OK;
@@ -1036,8 +1183,34 @@ struct DeviceGuard {
 
 extern "C" {
 
-ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const ovf_tensor *t, int32_t n_tensors,
-                            ovf_model **out) {
+// The exchange arena of a tensor-parallel rank: per layer the head outputs
+// [n_heads][d_model] and the down terms [d_ff/256][d_model] of every rank,
+// the logits [vocab], the ranks' argmax keys, the flags [2 * n_layers + 1]
+// [world] and this rank's step epoch.
+static ovf_status tp_arena_alloc(ovf_model *m) {
+    const ovf_model_config &c = m->cfg;
+    const DevLayer &L0 = m->layers[0];
+    m->nb_down = L0.down.type == OVF_TYPE_Q8_0 ? c.d_ff / 32 : c.d_ff / 256;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = (o + bytes + 255) & ~size_t(255);
+        return at;
+    };
+    m->off_heads = take((size_t)c.n_layers * c.n_heads * c.d_model * 4);
+    m->off_terms = take((size_t)c.n_layers * m->nb_down * c.d_model * 4);
+    m->off_logits = take((size_t)c.vocab * 4);
+    m->off_keys = take((size_t)m->tp_world * 8);
+    m->off_flags = take((size_t)(2 * c.n_layers + 1) * m->tp_world * 4);
+    m->off_epoch = take(16);
+    m->arena_bytes = o;
+    ovf_status st = dalloc(m->allocs, (void **)&m->arena, o);
+    if (!st) st = cuda_status(cudaMemset(m->arena, 0, o), "arena memset");
+    return st;
+}
+
+static ovf_status model_create(int32_t device, const ovf_model_config *cfg, const ovf_tensor *t, int32_t n_tensors,
+                               int32_t rank, int32_t world, ovf_model **out) {
     OVF_CHECK_ARG(cfg && t && out, "ovf_model_create: null argument");
     const ovf_model_config &c = *cfg;
     OVF_CHECK_ARG(c.n_layers > 0 && c.d_model > 0 && c.n_heads > 0 && c.n_kv_heads > 0 && c.head_dim > 0 &&
@@ -1054,30 +1227,79 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
     int ndev = 0;
     OVF_CUDA_TRY(cudaGetDeviceCount(&ndev));
     OVF_CHECK_ARG(device >= 0 && device < ndev, "ovf_model_create: device %d not present", device);
+    OVF_CHECK_ARG(world >= 1 && world <= 8 && rank >= 0 && rank < world, "ovf_model_create: bad rank %d of %d", rank,
+                  world);
+    const bool tp = world > 1;
+    if (tp) {
+        OVF_CHECK_ARG(c.n_experts == 0, "tensor parallelism: MoE models are split by experts, not heads");
+        OVF_CHECK_ARG(c.n_kv_heads % world == 0, "tensor parallelism: %d KV heads do not split over %d ranks",
+                      c.n_kv_heads, world);
+        OVF_CHECK_ARG(c.d_ff % world == 0 && (c.d_ff / world) % 256 == 0,
+                      "tensor parallelism: d_ff %d must split into multiples of 256", c.d_ff);
+        OVF_CHECK_ARG(c.vocab % world == 0, "tensor parallelism: vocab %d must split evenly", c.vocab);
+    }
     DeviceGuard guard(device);
     ovf_model *m = new ovf_model();
     m->device = device;
     m->cfg = c;
+    m->tp_rank = rank;
+    m->tp_world = world;
+    m->h_loc = c.n_heads / world;
+    m->kvh_loc = c.n_kv_heads / world;
+    m->ff_loc = c.d_ff / world;
+    m->v_loc = c.vocab / world;
     m->layers.resize(c.n_layers);
-    const int64_t D = c.d_model, QD = (int64_t)c.n_heads * c.head_dim, KD = (int64_t)c.n_kv_heads * c.head_dim;
+    const int64_t D = c.d_model, hd = c.head_dim, QD = (int64_t)c.n_heads * hd, KD = (int64_t)c.n_kv_heads * hd;
+    const int64_t QDl = (int64_t)m->h_loc * hd, KDl = (int64_t)m->kvh_loc * hd, FFl = m->ff_loc;
+    const int64_t q0 = (int64_t)rank * QDl, k0 = (int64_t)rank * KDl, f0 = (int64_t)rank * FFl;
     ovf_status st = OVF_OK;
+    std::vector<uint8_t> colbuf;
     for (int l = 0; l < c.n_layers && !st; ++l) {
         const ovf_tensor *lt = t + (size_t)l * OVF_TENSORS_PER_LAYER;
         DevLayer &L = m->layers[l];
         if (!st) st = upload_vec(m, lt[0], D, &L.attn_norm, "attn_norm");
-        if (!st) st = upload_matrix(m, lt[1], QD, D, false, &L.wq, "attn_q");
-        if (!st) st = upload_matrix(m, lt[2], KD, D, false, &L.wk, "attn_k");
-        if (!st) st = upload_matrix(m, lt[3], KD, D, false, &L.wv, "attn_v");
-        if (!st) st = upload_matrix(m, lt[4], D, QD, true, &L.wo, "attn_output");
-        if (!st) st = upload_vec(m, lt[5], QD, &L.bq, "attn_q.bias");
-        if (!st) st = upload_vec(m, lt[6], KD, &L.bk, "attn_k.bias");
-        if (!st) st = upload_vec(m, lt[7], KD, &L.bv, "attn_v.bias");
+        if (!tp) {
+            if (!st) st = upload_matrix(m, lt[1], QD, D, false, &L.wq, "attn_q");
+            if (!st) st = upload_matrix(m, lt[2], KD, D, false, &L.wk, "attn_k");
+            if (!st) st = upload_matrix(m, lt[3], KD, D, false, &L.wv, "attn_v");
+            if (!st) st = upload_matrix(m, lt[4], D, QD, true, &L.wo, "attn_output");
+            if (!st) st = upload_vec(m, lt[5], QD, &L.bq, "attn_q.bias");
+            if (!st) st = upload_vec(m, lt[6], KD, &L.bk, "attn_k.bias");
+            if (!st) st = upload_vec(m, lt[7], KD, &L.bv, "attn_v.bias");
+        } else {
+            // this rank's heads: Q/K/V rows, Wo columns (shard-aware upload)
+            for (int i = 1; i <= 4 && !st; ++i)
+                if (!lt[i].data) {
+                    set_error("layer %d: attention weights are required", l);
+                    st = OVF_EINVAL;
+                }
+            if (!st) OVF_CHECK_ARG(lt[1].rows == QD && lt[2].rows == KD && lt[3].rows == KD && lt[4].cols == QD,
+                                   "layer %d: attention shapes", l);
+            if (!st) st = upload_matrix(m, host_rows(lt[1], q0, QDl), QDl, D, false, &L.wq, "attn_q");
+            if (!st) st = upload_matrix(m, host_rows(lt[2], k0, KDl), KDl, D, false, &L.wk, "attn_k");
+            if (!st) st = upload_matrix(m, host_rows(lt[3], k0, KDl), KDl, D, false, &L.wv, "attn_v");
+            if (!st) st = upload_wo_local(m, lt[4], D, QD, q0, QDl, &L.wo);
+            if (!st) st = upload_vec(m, host_vec_slice(lt[5], q0, QDl), QDl, &L.bq, "attn_q.bias");
+            if (!st) st = upload_vec(m, host_vec_slice(lt[6], k0, KDl), KDl, &L.bk, "attn_k.bias");
+            if (!st) st = upload_vec(m, host_vec_slice(lt[7], k0, KDl), KDl, &L.bv, "attn_v.bias");
+        }
         if (!st) st = upload_vec(m, lt[8], D, &L.bo, "attn_output.bias");
         if (!st) st = upload_vec(m, lt[9], D, &L.ffn_norm, "ffn_norm");
         const int64_t E = c.n_experts > 0 ? c.n_experts : 1;
-        if (!st) st = upload_matrix(m, lt[10], E * c.d_ff, D, false, &L.gate, "ffn_gate");
-        if (!st) st = upload_matrix(m, lt[11], E * c.d_ff, D, false, &L.up, "ffn_up");
-        if (!st) st = upload_matrix(m, lt[12], E * D, c.d_ff, false, &L.down, "ffn_down");
+        if (!tp) {
+            if (!st) st = upload_matrix(m, lt[10], E * c.d_ff, D, false, &L.gate, "ffn_gate");
+            if (!st) st = upload_matrix(m, lt[11], E * c.d_ff, D, false, &L.up, "ffn_up");
+            if (!st) st = upload_matrix(m, lt[12], E * D, c.d_ff, false, &L.down, "ffn_down");
+        } else {
+            // this rank's FFN slice: gate/up rows, down columns
+            if (!st && (!lt[10].data || !lt[11].data || !lt[12].data || lt[12].cols != c.d_ff || lt[12].rows != D)) {
+                set_error("layer %d: FFN weights are required", l);
+                st = OVF_EINVAL;
+            }
+            if (!st) st = upload_matrix(m, host_rows(lt[10], f0, FFl), FFl, D, false, &L.gate, "ffn_gate");
+            if (!st) st = upload_matrix(m, host_rows(lt[11], f0, FFl), FFl, D, false, &L.up, "ffn_up");
+            if (!st) st = upload_matrix(m, host_cols(lt[12], f0, FFl, colbuf), D, FFl, false, &L.down, "ffn_down");
+        }
         if (!st && c.n_experts > 0) {
             // Mixtral: ffn_gate_inp as the input-major F32 router; experts stacked
             ovf_tensor rt = lt[13];
@@ -1131,7 +1353,30 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
         }
     }
     if (!st) st = upload_vec(m, tail[1], D, &m->final_norm, "output_norm");
-    if (!st) {
+    if (!st && tp) {
+        // this rank's vocabulary rows of the LM head (tied: of the embedding)
+        const ovf_tensor &o = tail[2];
+        const int64_t v0 = (int64_t)rank * m->v_loc, vl = m->v_loc;
+        if (o.data && o.type >= 0) {
+            st = upload_matrix(m, host_rows(o, v0, vl), vl, D, o.type == OVF_TYPE_F32, &m->lm_head, "output");
+        } else if (m->embed.type == OVF_TYPE_F32) {
+            ovf_tensor tt{OVF_TYPE_F32, tail[0].data, c.vocab, D};
+            st = upload_matrix(m, host_rows(tt, v0, vl), vl, D, true, &m->lm_head, "output(tied)");
+        } else {
+            m->lm_head = m->embed;
+            m->lm_head.owns = false;
+            m->lm_head.rows = vl;
+            if (m->embed.type == OVF_TYPE_Q8_0) {
+                m->lm_head.data = m->embed.data + v0 * D;
+                m->lm_head.scales = m->embed.scales + v0 * D / 32;
+                m->weight_bytes += vl * D * 9 / 8;
+            } else {
+                m->lm_head.data = m->embed.data + v0 * host_row_bytes(m->embed.type, D);
+                m->weight_bytes += tensor_bytes(m->embed.type, vl, D);
+            }
+        }
+    }
+    if (!st && !tp) {
         const ovf_tensor &o = tail[2];
         if (o.data && o.type >= 0) {
             st = upload_matrix(m, o, c.vocab, D, o.type == OVF_TYPE_F32, &m->lm_head, "output");
@@ -1146,6 +1391,7 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
                                                                 : tensor_bytes(m->embed.type, c.vocab, D);
         }
     }
+    if (!st && tp) st = tp_arena_alloc(m);
     if (st) {
         ovf_model_destroy(m);
         return st;
@@ -1154,11 +1400,59 @@ ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const o
     return OVF_OK;
 }
 
+ovf_status ovf_model_create(int32_t device, const ovf_model_config *cfg, const ovf_tensor *t, int32_t n_tensors,
+                            ovf_model **out) {
+    return model_create(device, cfg, t, n_tensors, 0, 1, out);
+}
+
+ovf_status ovf_model_create_tp(int32_t device, const ovf_model_config *cfg, const ovf_tensor *t, int32_t n_tensors,
+                               int32_t rank, int32_t world, ovf_model **out) {
+    return model_create(device, cfg, t, n_tensors, rank, world, out);
+}
+
+ovf_status ovf_model_tp_export(ovf_model *m, void *handle_out) {
+    OVF_CHECK_ARG(m && handle_out, "tp_export: null argument");
+    OVF_CHECK_ARG(m->tp_world > 1 && m->arena, "tp_export: not a tensor-parallel model");
+    DeviceGuard guard(m->device);
+    cudaIpcMemHandle_t h;
+    OVF_CUDA_TRY(cudaIpcGetMemHandle(&h, m->arena));
+    memcpy(handle_out, &h, sizeof(h));
+    return OVF_OK;
+}
+
+ovf_status ovf_model_tp_connect(ovf_model *m, const void *handles) {
+    OVF_CHECK_ARG(m && handles, "tp_connect: null argument");
+    OVF_CHECK_ARG(m->tp_world > 1 && m->arena, "tp_connect: not a tensor-parallel model");
+    OVF_CHECK_ARG(!m->tp_ready, "tp_connect: already connected");
+    DeviceGuard guard(m->device);
+    for (int w = 0; w < m->tp_world; ++w) {
+        if (w == m->tp_rank) {
+            m->peer[w] = m->arena;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char *>(handles) + (size_t)w * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int v = 0; v < w; ++v)
+                if (v != m->tp_rank && m->peer[v]) cudaIpcCloseMemHandle(m->peer[v]);
+            return cuda_status(e, "cudaIpcOpenMemHandle");
+        }
+        m->peer[w] = static_cast<char *>(p);
+    }
+    m->tp_ready = true;
+    return OVF_OK;
+}
+
 ovf_status ovf_model_destroy(ovf_model *m) {
     if (!m) return OVF_OK;
     DeviceGuard guard(m->device);
     if (m->btok_host) cudaFreeHost(m->btok_host);
     if (m->bmoe.host) cudaFreeHost(m->bmoe.host);
+    if (m->tp_ready)
+        for (int w = 0; w < m->tp_world; ++w)
+            if (w != m->tp_rank && m->peer[w]) cudaIpcCloseMemHandle(m->peer[w]);
     for (void *p : m->allocs) cudaFree(p);
     delete m;
     return OVF_OK;
@@ -1184,7 +1478,9 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     s->max_ctx = max_ctx;
     s->kv_dtype = kv_dtype;
     const ovf_model_config &c = m->cfg;
-    const size_t D = c.d_model, QD = (size_t)c.n_heads * c.head_dim, KD = (size_t)c.n_kv_heads * c.head_dim;
+    // tensor parallel: this rank's heads and FFN rows only
+    const size_t D = c.d_model, QD = (size_t)m->h_loc * c.head_dim, KD = (size_t)m->kvh_loc * c.head_dim;
+    const size_t FF = (size_t)m->ff_loc;
     const size_t kv = (size_t)c.n_layers * KD * max_ctx;
     ovf_status st = OVF_OK;
     auto A = [&](void **p, size_t bytes) {
@@ -1203,14 +1499,14 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
     A((void **)&s->k, KD * 4);
     A((void **)&s->v, KD * 4);
     A((void **)&s->attn, QD * 4);
-    A((void **)&s->h, (size_t)c.d_ff * 4);
-    A((void **)&s->gtmp, (size_t)c.d_ff * 4);
-    A((void **)&s->utmp, (size_t)c.d_ff * 4);
+    A((void **)&s->h, FF * 4);
+    A((void **)&s->gtmp, FF * 4);
+    A((void **)&s->utmp, FF * 4);
     A((void **)&s->logits, (size_t)c.vocab * 4);
     A((void **)&s->rope_cos, (size_t)max_ctx * c.head_dim / 2 * 4);
     A((void **)&s->rope_sin, (size_t)max_ctx * c.head_dim / 2 * 4);
-    A((void **)&s->partial, (size_t)attn_scratch_bytes(c.n_heads, c.n_kv_heads, c.head_dim));
-    A((void **)&s->counters, (size_t)c.n_kv_heads * 4);
+    A((void **)&s->partial, (size_t)attn_scratch_bytes(m->h_loc, m->kvh_loc, c.head_dim));
+    A((void **)&s->counters, (size_t)m->kvh_loc * 4);
     A((void **)&s->norm_s, 2 * 4);
     if (env_flag("OVF_TRACE")) {
         s->trace_cap = 8 * c.n_layers + 16;
@@ -1226,7 +1522,8 @@ ovf_status ovf_session_create_kv(ovf_model *m, int32_t max_ctx, int32_t kv_dtype
         A((void **)&s->meo, (size_t)c.n_experts_used * D * 4);
     }
     if (!st) st = cuda_status(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
-    if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)c.n_kv_heads * 4), "memset");
+    if (!st) st = cuda_status(cudaMemset(s->counters, 0, (size_t)m->kvh_loc * 4), "memset");
+    s->prefill_single = m->tp_world > 1;  // the batched prefill is not split over ranks
     if (!st) st = cuda_status(cudaMemset(s->step, 0, sizeof(DevStep)), "memset");
     if (!st) st = cuda_status(cudaMemset(s->kc, 0, kv * esz), "memset");
     if (!st) st = cuda_status(cudaMemset(s->vc, 0, kv * esz), "memset");
@@ -1295,6 +1592,10 @@ static ovf_status decode_impl(ovf_session *s, const int32_t *tokens, int32_t n, 
         return OVF_ESTATE;
     }
     OVF_CHECK_ARG(n >= 0 && (n == 0 || tokens), "decode: bad token array");
+    if (s->m->tp_world > 1 && !s->m->tp_ready) {
+        set_error("tensor-parallel model: call ovf_model_tp_connect on every rank first");
+        return OVF_ESTATE;
+    }
     OVF_CHECK_ARG(s->pos + n <= s->max_ctx, "KV cache is full (ContextLength=%d, position %d, %d new tokens)", s->max_ctx,
                   s->pos, n);
     if (n == 0) return OVF_OK;
@@ -1344,6 +1645,10 @@ ovf_status ovf_session_prefill(ovf_session *s, const int32_t *tokens, int32_t n,
 ovf_status ovf_session_generate_greedy(ovf_session *s, int32_t n_steps, int32_t *tokens_out) {
     OVF_CHECK_ARG(s && n_steps >= 0 && (n_steps == 0 || tokens_out), "generate: bad arguments");
     OVF_CHECK_ARG(s->n_logits > 0, "Session is empty. Call Reset with at least one prompt token first.");
+    if (s->m->tp_world > 1 && !s->m->tp_ready) {
+        set_error("tensor-parallel model: call ovf_model_tp_connect on every rank first");
+        return OVF_ESTATE;
+    }
     OVF_CHECK_ARG(s->pos + n_steps <= s->max_ctx, "KV cache is full (ContextLength=%d)", s->max_ctx);
     DeviceGuard guard(s->m->device);
     const int first = s->n_logits - 1;  // the token sampled from the current logits
@@ -1363,6 +1668,10 @@ ovf_status ovf_session_decode_batch(ovf_session *const *sessions, int32_t n, con
     OVF_CHECK_ARG(n <= kBatchMax, "decode batch: at most %d sessions per call, got %d", kBatchMax, n);
     ovf_model *m = sessions[0] ? sessions[0]->m : nullptr;
     OVF_CHECK_ARG(m, "decode batch: null session");
+    if (m->tp_world > 1) {
+        set_error("decode batch: not available on a tensor-parallel model");
+        return OVF_EUNSUPPORTED;
+    }
     for (int i = 0; i < n; ++i) {
         ovf_session *s = sessions[i];
         OVF_CHECK_ARG(s && s->m == m, "decode batch: session %d is null or of another model", i);
@@ -1426,6 +1735,10 @@ ovf_status ovf_session_verify(ovf_session *s, const int32_t *tokens, int32_t n, 
                               int32_t *argmax_out) {
     OVF_CHECK_ARG(s && tokens && n >= 1, "verify: bad arguments");
     OVF_CHECK_ARG(n <= kVerifyMax, "verify: at most %d rows per call, got %d", kVerifyMax, n);
+    if (s->m->tp_world > 1) {
+        set_error("verify: not available on a tensor-parallel model");
+        return OVF_EUNSUPPORTED;
+    }
     if (s->needs_reset) {
         set_error("session state is undefined after a failed batch call; call ovf_session_reset");
         return OVF_ESTATE;

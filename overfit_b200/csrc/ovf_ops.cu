@@ -378,7 +378,8 @@ ovf_status launch_rope(float *v, int n_vec, int hd, const float *c, const float 
 // position; then warp 0 runs the first layer's RMSNorm sum of squares in
 // the reference's order and leaves the scale in norm_out (one CTA).
 __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict__ w, const float *__restrict__ q8s,
-                             int d, float *__restrict__ hidden, float *norm_out, float eps, TraceSlot *trace) {
+                             int d, float *__restrict__ hidden, float *norm_out, float eps, TraceSlot *trace,
+                             unsigned *epoch) {
     if (threadIdx.x == 0) trace_mark(trace, TR_START);
     pdl_wait();
     if (threadIdx.x == 0) trace_mark(trace, TR_WAITED);
@@ -396,6 +397,7 @@ __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict_
     if (threadIdx.x == 0) {
         step->cur_pos = step->next_pos;
         step->next_pos += 1;
+        if (epoch) *epoch += 1;  // tensor parallel: this step's exchange epoch
     }
     if (norm_out) {
         __shared__ __align__(16) float stage[2048];
@@ -407,9 +409,10 @@ __global__ void embed_kernel(DevStep *step, int type, const uint8_t *__restrict_
 }
 
 ovf_status launch_embed(const DevStep *, int type, const void *w, const float *q8s, int d, float *hidden,
-                        DevStep *step, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st, bool pdl) {
+                        DevStep *step, float *norm_out, float eps, TraceSlot *trace, cudaStream_t st, bool pdl,
+                        unsigned *epoch) {
     cudaError_t e = launch_pdl(embed_kernel, dim3(1), dim3(1024), 0, st, pdl, step, type, (const uint8_t *)w, q8s, d,
-                               hidden, norm_out, eps, trace);
+                               hidden, norm_out, eps, trace, epoch);
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "embed");
 }
 

@@ -95,19 +95,72 @@ def model_config(cfg: dict) -> ModelConfig:
                        float(cfg["theta"]))
 
 
-class CudaLlamaInferenceEngine:
-    """GPU engine behind ISlmInferenceEngine (weights resident on one device)."""
+def tp_check(cfg: dict, world: int) -> None:
+    """The shapes tensor parallelism over `world` ranks accepts (the checks
+    ovf_model_create_tp makes): KV heads, FFN rows in 256-blocks and the
+    vocabulary split evenly; no MoE (experts are split by expert instead)."""
+    if world < 1 or world > 8:
+        raise ValueError("tensor parallelism: 1..8 ranks")
+    if world == 1:
+        return
+    if cfg.get("n_experts", 0):
+        raise ValueError("tensor parallelism: MoE models are split by experts, not heads")
+    if cfg["n_kv_heads"] % world:
+        raise ValueError(f"tensor parallelism: {cfg['n_kv_heads']} KV heads do not split over {world} ranks")
+    if cfg["d_ff"] % world or (cfg["d_ff"] // world) % 256:
+        raise ValueError(f"tensor parallelism: d_ff {cfg['d_ff']} must split into multiples of 256")
+    if cfg["vocab"] % world:
+        raise ValueError(f"tensor parallelism: vocab {cfg['vocab']} must split evenly")
 
-    def __init__(self, cfg: dict, model_file: dict, device: int = 0):
+
+def exchange_handles(handle: bytes, group=None) -> bytes:
+    """All ranks' exchange-arena handles, concatenated in rank order, through
+    the torch.distributed process group (host-side plumbing; the data path
+    itself is peer memory)."""
+    import torch.distributed as dist
+
+    gathered = [None] * dist.get_world_size(group)
+    dist.all_gather_object(gathered, bytes(handle), group=group)
+    if any(len(h) != _lib.TP_HANDLE_BYTES for h in gathered):
+        raise ValueError("tensor parallelism: malformed exchange handle")
+    return b"".join(gathered)
+
+
+class CudaLlamaInferenceEngine:
+    """GPU engine behind ISlmInferenceEngine (weights resident on one device).
+
+    ``tp_group``: a torch.distributed process group of one process per GPU;
+    with more than one rank the model is split tensor-parallel (every rank
+    passes the full model file, uploads its shard and connects to the other
+    ranks' exchange buffers) and every rank must then make the same session
+    calls in the same order."""
+
+    def __init__(self, cfg: dict, model_file: dict, device: int = 0, tp_group=None):
         self.cfg = dict(cfg)
         self.device = device
         lib = _lib.load()
         table, keep = tensor_table(cfg, model_file)
         mc = model_config(cfg)
         handle = C.c_void_p()
-        check(lib.ovf_model_create(device, C.byref(mc), table, len(table), C.byref(handle)), "ovf_model_create")
+        world, rank = 1, 0
+        if tp_group is not None:
+            import torch.distributed as dist
+            world, rank = dist.get_world_size(tp_group), dist.get_rank(tp_group)
+        self.tp_world, self.tp_rank = world, rank
+        if world == 1:
+            check(lib.ovf_model_create(device, C.byref(mc), table, len(table), C.byref(handle)), "ovf_model_create")
+        else:
+            tp_check(cfg, world)
+            check(lib.ovf_model_create_tp(device, C.byref(mc), table, len(table), rank, world, C.byref(handle)),
+                  "ovf_model_create_tp")
         del keep
         self._h = handle
+        if world > 1:
+            mine = (C.c_char * _lib.TP_HANDLE_BYTES)()
+            check(lib.ovf_model_tp_export(self._h, mine), "tp_export")
+            allh = exchange_handles(bytes(mine), tp_group)
+            buf = (C.c_char * len(allh)).from_buffer_copy(allh)
+            check(lib.ovf_model_tp_connect(self._h, buf), "tp_connect")
 
     @property
     def weight_bytes(self) -> int:
