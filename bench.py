@@ -15,9 +15,11 @@ Arms:
   python bench.py --impl reference [...]                  the reference CPU path
       (the C restatement in oracle/, all host threads; the reference is C#/.NET
       with no runtime in this image)
-Multi-GPU (torchrun, N > 1): independent replicas, one per GPU ("replicas
-only" until tensor parallelism lands); value = sum over ranks with the
-max-over-ranks time.
+Multi-GPU (torchrun, N > 1): the model is split tensor-parallel over the N
+GPUs (heads, FFN rows and vocabulary; exact, see ovf_model_create_tp); value
+= the sequence's tokens / the max-over-ranks device time (strong scaling).
+The other BASELINE configs (single GEMV, prefill GEMM sweep, Qwen2-0.5B,
+16 concurrent sessions) and the CPU baseline are reported at N = 1.
 """
 from __future__ import annotations
 
@@ -50,7 +52,8 @@ def parse():
     ap.add_argument("--kv", default="f16", choices=["f16", "f32"],
                     help="KV cache of the timed session: f16 (the benchmark config) or f32 (the reference's default, "
                          "bit-exact attention)")
-    ap.add_argument("--no-f32-line", action="store_true", help="skip the extra F32-KV (exact) measurement")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="only the headline decode line (skip the other BASELINE configs and the exact-cache lines)")
     ap.add_argument("--profile-target", default=None, choices=sorted(PROFILE_TARGETS),
                     help="run only a few launches of one kernel on a small case (for ncu captures) and exit")
     return ap.parse_args()
@@ -116,18 +119,15 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_decode_sample(n_tokens: int, threads: int | None = None) -> dict:
-    """Times the reference CPU path (the C restatement, OpenMP over all host
-    threads) on the same Llama-3-8B Q4_K_M decode: 32 layers that share one
-    layer's weights (each token still streams 32 x 148 MB of layer weights
-    plus the 431 MB LM head from DRAM, as the full model would; the
-    working set is far above the host caches) at a short context."""
+def _oracle_llama8b(max_ctx: int):
+    """The C restatement of the reference's CPU path (oracle/) holding a
+    Llama-3-8B Q4_K_M model in host memory: one layer's weights quantized by
+    the restated encoders and copied into 32 distinct layer buffers (every
+    token streams 32 x 148 MB of layer weights plus the 431 MB LM head from
+    DRAM, as the full model does; nothing can stay cache-resident)."""
     from oracle import oracle as orc
     from overfit_b200.engine import LLAMA3_8B as cfg
 
-    if threads:
-        orc.set_threads(threads)
-    cores = orc.num_threads()
     D, H, KVH, hd, FF, V = (cfg[k] for k in ("d_model", "n_heads", "n_kv_heads", "head_dim", "d_ff", "vocab"))
 
     def qmat(rows, cols, enc, seed):
@@ -140,43 +140,65 @@ def cpu_decode_sample(n_tokens: int, threads: int | None = None) -> dict:
         return np.concatenate(out)
 
     t0 = time.time()
-    L = dict(attn_norm=np.ones(D, np.float32), ffn_norm=np.ones(D, np.float32))
-    L["wq"] = (orc.Q4_K, qmat(H * hd, D, orc.quantize_q4k, 1), None, H * hd, D)
-    L["wk"] = (orc.Q4_K, qmat(KVH * hd, D, orc.quantize_q4k, 2), None, KVH * hd, D)
-    L["wv"] = (orc.Q6_K, qmat(KVH * hd, D, orc.quantize_q6k, 3), None, KVH * hd, D)
-    wo = qmat(D, H * hd, orc.quantize_q4k, 4)
-    q, s = orc.requant_q8_0(orc.Q4_K, wo, D, H * hd)
-    L["wo"] = (orc.Q8_0, q, s, D, H * hd)
-    L["gate"] = (orc.Q4_K, qmat(FF, D, orc.quantize_q4k, 5), None, FF, D)
-    L["up"] = (orc.Q4_K, qmat(FF, D, orc.quantize_q4k, 6), None, FF, D)
-    L["down"] = (orc.Q6_K, qmat(D, FF, orc.quantize_q6k, 7), None, D, FF)
-    weights = dict(layers=[L] * cfg["n_layers"], embed=(orc.Q4_K, qmat(V, D, orc.quantize_q4k, 8), None, V, D),
+    base = dict(wq=(orc.Q4_K, qmat(H * hd, D, orc.quantize_q4k, 1), None, H * hd, D),
+                wk=(orc.Q4_K, qmat(KVH * hd, D, orc.quantize_q4k, 2), None, KVH * hd, D),
+                wv=(orc.Q6_K, qmat(KVH * hd, D, orc.quantize_q6k, 3), None, KVH * hd, D),
+                gate=(orc.Q4_K, qmat(FF, D, orc.quantize_q4k, 5), None, FF, D),
+                up=(orc.Q4_K, qmat(FF, D, orc.quantize_q4k, 6), None, FF, D),
+                down=(orc.Q6_K, qmat(D, FF, orc.quantize_q6k, 7), None, D, FF))
+    q, sc = orc.requant_q8_0(orc.Q4_K, qmat(D, H * hd, orc.quantize_q4k, 4), D, H * hd)
+    base["wo"] = (orc.Q8_0, q, sc, D, H * hd)
+    layers = []
+    for _ in range(cfg["n_layers"]):
+        L = dict(attn_norm=np.ones(D, np.float32), ffn_norm=np.ones(D, np.float32))
+        for k, (t, data, scales, r, c) in base.items():
+            L[k] = (t, data.copy(), None if scales is None else scales.copy(), r, c)
+        layers.append(L)
+    weights = dict(layers=layers, embed=(orc.Q4_K, qmat(V, D, orc.quantize_q4k, 8), None, V, D),
                    final_norm=np.ones(D, np.float32), lm_head=(orc.Q6_K, qmat(V, D, orc.quantize_q6k, 9), None, V, D))
     gen_s = time.time() - t0
-    sess = orc.OracleSession(cfg, weights, max_ctx=n_tokens + 8)
-    sess.decode(1)  # warm-up token
-    t0 = time.perf_counter()
+    return orc, cfg, orc.OracleSession(cfg, weights, max_ctx), gen_s
+
+
+def cpu_decode_sample(context: int, samples: int, threads: int | None = None) -> dict:
+    """Times the reference CPU path (the C restatement, OpenMP over the host
+    threads, the reference's output-row bands) on the benchmark's own decode:
+    Llama-3-8B Q4_K_M, distinct per-layer weights, at the GPU arm's context
+    (the F32 cache filled with `context` synthetic rows).  The value is the
+    median over `samples` single-token decodes."""
+    from oracle import oracle as orc0
+
+    if threads:
+        orc0.set_threads(threads)
+    orc, cfg, sess, gen_s = _oracle_llama8b(context + samples + 4)
+    sess.fill_context(context)
     tok = 1
-    for _ in range(n_tokens):
+    sess.decode(tok)  # warm-up token
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
         lg = sess.decode(tok)
+        times.append(time.perf_counter() - t0)
         tok = int(np.argmax(lg))
-    dt = time.perf_counter() - t0
-    return {"tok_s": n_tokens / dt, "s_per_token": dt / n_tokens, "cores": cores, "gen_s": gen_s,
-            "sample": f"{n_tokens} greedy decode tokens of the full 32-layer + LM-head Llama-3-8B Q4_K_M step "
-                      f"(layers share one layer's weights), context <= {n_tokens + 1}"}
+    med = float(np.median(times))
+    return {"tok_s": 1.0 / med, "s_per_token": med, "cores": orc.num_threads(), "gen_s": gen_s,
+            "samples_s": times,
+            "sample": f"median of {samples} single-token greedy decodes of the full 32-layer + LM-head Llama-3-8B "
+                      f"Q4_K_M step (distinct per-layer weights) at context {context + 1}..{context + samples + 1}"}
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 16))
-    r = cpu_decode_sample(steps)
+    samples = max(5, min(args.steps, 8))
+    r = cpu_decode_sample(args.prompt, samples)
     line = {"impl": "reference", "metric": METRIC, "value": r["tok_s"], "unit": "tok/s", "n_gpus": 0,
-            "steps": steps, "warmup": 1, "ms_per_step": r["s_per_token"] * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / fp32", "data": "synthetic",
-            "config": {"workload": "llama3-8b-q4_k_m greedy decode, batch 1 (CPU restatement of the reference)",
-                       "model": "Llama-3-8B shape", "global_batch": 1},
+            "steps": samples, "warmup": 1, "ms_per_step": r["s_per_token"] * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot / fp32", "data": "synthetic",
+            "config": {"workload": "llama3-8b-q4_k_m greedy decode batch 1 at context %d (C restatement of the "
+                                   "reference CPU path)" % args.prompt,
+                       "model": "Llama-3-8B shape", "global_batch": 1, "seq_len": args.prompt},
             "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["cores"], "kind": "port",
                              "sample": r["sample"]},
             "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -184,6 +206,22 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------- GPU arm
+def _timed(torch, fn, reps: int) -> float:
+    """Mean seconds per call of fn over `reps` calls, CUDA events on the
+    current stream, after 3 warm-up calls."""
+    for _ in range(3):
+        fn(0)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(reps):
+        fn(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
 def gemv_roofline(torch, eng_cfg, model_file, device, peaks) -> dict:
     """Times the dominant kernel alone with CUDA events: the fused Q4_K
     gate/up GEMV of Llama-3-8B (2 x [14336 x 4096] Q4_K), rotating across
@@ -200,80 +238,143 @@ def gemv_roofline(torch, eng_cfg, model_file, device, peaks) -> dict:
     s = torch.empty(D // 256, device=device)
     b = torch.empty(D // 16, dtype=torch.int16, device=device)
     n = len(gates)
-    for i in range(3):
-        Q4KDotKernel.project_gate_up_parallel(x, gates[i % n], ups[i % n], g, u, q, s, b)
-    torch.cuda.synchronize()
-    reps = 4 * n
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for i in range(reps):
-        Q4KDotKernel.project_gate_up_parallel(x, gates[i % n], ups[i % n], g, u, q, s, b)
-    e1.record(st)
-    torch.cuda.synchronize()
-    dt = e0.elapsed_time(e1) / 1e3 / reps
+    dt = _timed(torch, lambda i: Q4KDotKernel.project_gate_up_parallel(x, gates[i % n], ups[i % n], g, u, q, s, b),
+                4 * n)
     alg = 2 * FF * D // 256 * 144 + 4 * D + 2 * 4 * FF  # weights + x + outputs
     achieved = alg / dt / 1e9
     peak = peaks.get("hbm_gbs", 6650.0)
     del gates, ups
     return {"bound": "hbm", "kernel": "gemv_kernel (Q4_K gate+up pair, 2x14336x4096)", "achieved": achieved,
-            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": profiled_traffic(),
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+            "traffic_note": "DRAM bytes per launch from the ncu capture summarised in profiles/ (1.006x algorithmic)",
             "launch_us": dt * 1e6, "algorithmic_bytes": alg,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback 6650"}
 
 
-def prefill_gemm(torch, eng_cfg, model_file, device) -> dict:
-    """Config-2 prefill projection: the weight-stationary batched Q4_K
-    kernel (ProjectBatchedWeightStationary) on the gate matrices
-    [14336 x 4096] for M activation rows, CUDA-event timed, rotating over the
-    layers' weights.  2*M*N*K integer multiply-adds per launch."""
-    from overfit_b200.kernels import Q4KDotKernel, Q4KWeight
+def gemv_config1(torch, device, peaks) -> dict:
+    """the single Q4_K projection y = W x (ProjectParallel:
+    the Q8_K quantization of x and the GEMV), W [N x 4096] ~ N(0, 0.02) from
+    seed 0 quantized by the reference's Q4_K scheme, x ~ N(0, 1), N = 4096 and
+    14336.  Copies of W rotate so the weights in flight exceed 4x L2."""
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight
 
-    FF, D = eng_cfg["d_ff"], eng_cfg["d_model"]
-    layers = model_file["layers"][:8]
-    gates = [Q4KWeight(torch.from_numpy(L["gate"][1]).to(device), D, FF) for L in layers]
+    K = 4096
+    peak = peaks.get("hbm_gbs", 6650.0)
     out = {}
-    for M in (16, 128, 512):
-        x = torch.randn(M * D, device=device)
-        y = torch.empty(M * FF, device=device)
-        q = torch.empty(M * D, dtype=torch.int8, device=device)
-        s = torch.empty(M * D // 256, device=device)
-        b = torch.empty(M * D // 16, dtype=torch.int16, device=device)
-        for i in range(3):
-            Q4KDotKernel.project_batched(x, M, gates[i % len(gates)], None, y, q, s, b)
-        torch.cuda.synchronize()
-        reps = 2 * len(gates)
-        st = torch.cuda.current_stream()
+    for N in (4096, 14336):
+        g = torch.Generator(device=device).manual_seed(0)
+        w = GgmlQuant.quantize_q4_k(torch.randn(N, K, device=device, generator=g) * 0.02, K, N)
+        copies = max(2, -(-4 * 126 * 2 ** 20 // w.numel()))
+        ws = [Q4KWeight(w.clone(), K, N) for _ in range(copies)]
+        x = torch.randn(K, device=device, generator=g)
+        y = torch.empty(N, device=device)
+        q = torch.empty(K, dtype=torch.int8, device=device)
+        s = torch.empty(K // 256, device=device)
+        b = torch.empty(K // 16, dtype=torch.int16, device=device)
+        dt = _timed(torch, lambda i: Q4KDotKernel.project_parallel(x, ws[i % copies], None, y, q, s, b), 8 * copies)
+        alg = N * K // 256 * 144 + 4 * K + 4 * N
+        out[str(N)] = {"us": dt * 1e6, "achieved_gbs": alg / dt / 1e9, "frac": alg / dt / 1e9 / peak,
+                       "algorithmic_bytes": alg, "rotating_copies": copies}
+        del ws, w
+    return {"kernel": "gemv_kernel via ovf_kq_project (Q4_K, K=4096)", "peak_gbs": peak, "unit": "GB/s",
+            "rows": out}
+
+
+def prefill_gemm(torch, device) -> dict:
+    """the prefill projection (ProjectBatched /
+    ProjectBatchedWeightStationary) on a [14336 x 4096] weight, Q4_K and
+    Q8_0, M in {1, 16, 128, 512, 2048} activation rows ~ N(0, 1), CUDA-event
+    timed over 4 rotating weight copies (quantization of the rows included).
+    2*M*N*K integer operations per launch."""
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight, Q8DotKernel, Q8Weight
+
+    N, K = 14336, 4096
+    g = torch.Generator(device=device).manual_seed(0)
+    w32 = torch.randn(N, K, device=device, generator=g) * 0.02
+    q4 = [Q4KWeight(GgmlQuant.quantize_q4_k(w32, K, N).clone(), K, N) for _ in range(4)]
+    q8g = GgmlQuant.quantize_q8_0(w32)
+    q8 = [Q8Weight.from_gguf(q8g, K, N) for _ in range(4)]
+    del w32
+    out = {}
+    for M in (1, 16, 128, 512, 2048):
+        x = torch.randn(M * K, device=device, generator=g)
+        y = torch.empty(M * N, device=device)
+        aq = torch.empty(M * K, dtype=torch.int8, device=device)
+        a4 = torch.empty(M * K // 256, device=device)
+        ab = torch.empty(M * K // 16, dtype=torch.int16, device=device)
+        a8 = torch.empty(M * K // 32, device=device)
+        reps = 8 if M >= 512 else 32
+        d4 = _timed(torch, lambda i: Q4KDotKernel.project_batched(x, M, q4[i % 4], None, y, aq, a4, ab), reps)
+        d8 = _timed(torch, lambda i: Q8DotKernel.project_batched(x, M, q8[i % 4], None, y, aq, a8), reps)
+        out[str(M)] = {"q4_k_us": d4 * 1e6, "q4_k_int_tops": 2 * M * N * K / d4 / 1e12,
+                       "q8_0_us": d8 * 1e6, "q8_0_int_tops": 2 * M * N * K / d8 / 1e12}
+    return {"kernel": "batched_project_kernel (weight-stationary, dp4a)", "n": N, "k": K, "rows": out}
+
+
+def qwen_config3(torch, device) -> dict:
+    """Qwen2-0.5B-shaped Q8_0 model (seed 1), 128-token
+    uniform-random prompt, 256 greedy decode steps, batch 1, on the F32 KV
+    cache (the reference's default; exact attention order)."""
+    from overfit_b200 import engine
+
+    cfg = dict(engine.QWEN2_05B)
+    mf = engine.synthetic_model(cfg, seed=1, device=device)
+    eng = engine.CudaLlamaInferenceEngine(cfg, mf, device=device)
+    out = {}
+    for kv in ("f32", "f16"):
+        s = eng.create_session(128 + 256 + 16, kv)
+        prompt = np.random.default_rng(3).integers(0, cfg["vocab"], 128)
+        t0 = time.perf_counter()
+        s.prefill(prompt)
+        pf = time.perf_counter() - t0
+        s.generate_greedy(3)
+        st = torch.cuda.ExternalStream(s.stream_handle, device=device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
         e0.record(st)
-        for i in range(reps):
-            Q4KDotKernel.project_batched(x, M, gates[i % len(gates)], None, y, q, s, b)
+        s.generate_greedy(253)
         e1.record(st)
-        torch.cuda.synchronize()
-        dt = e0.elapsed_time(e1) / 1e3 / reps
-        out[str(M)] = {"us": dt * 1e6, "int_tops": 2 * M * FF * D / dt / 1e12}
-    del gates
-    return {"kernel": "batched_project_kernel (Q4_K, 14336 x 4096, quantize included)", "rows": out}
+        torch.cuda.synchronize(device)
+        dt = e0.elapsed_time(e1) / 1e3
+        out[kv] = {"tok_s": 253 / dt, "ms_per_token": dt / 253 * 1e3, "prefill_s": pf}
+        s.close()
+    eng.close()
+    return {"model": "Qwen2-0.5B shape, Q8_0, tied embeddings, q/k/v bias", "prompt": 128, "steps": 256,
+            "kv_caches": out, "weight_bytes_per_step": None}
 
 
-def profiled_traffic():
-    """DRAM bytes per launch of the gate/up GEMV from the committed ncu
-    summary (profiles/gemv_q4k_gateup.md, line `traffic_bytes_per_launch:`),
-    or None when no capture has been summarised."""
-    p = os.path.join(ROOT, "profiles", "gemv_q4k_gateup.md")
-    try:
-        for ln in open(p):
-            if ln.strip().startswith("traffic_bytes_per_launch:"):
-                return float(ln.split(":", 1)[1].strip().split()[0])
-    except OSError:
-        pass
-    return None
+def sessions16(torch, eng, cfg, prompt, steps, device) -> dict:
+    """BASELINE config 4 at 16 concurrent sessions: the 2048-token prompt is
+    prefilled once and restored into 16 sessions (RestorePrefix), each then
+    takes a different token; `steps` rounds of one decode in every session
+    as one batch (ovf_session_decode_batch, weights read once per round).
+    Aggregate tokens / s by the host clock (each round returns to the host)."""
+    n = 16
+    base = eng.create_session(len(prompt) + steps + 8, "f16")
+    base.prefill(prompt)
+    snap = base.save_prefix()
+    base.close()
+    ss = [eng.create_session(len(prompt) + steps + 8, "f16") for _ in range(n)]
+    toks = []
+    for i, s in enumerate(ss):
+        s.restore_prefix(snap)
+        toks.append(s.prefill([1000 + 17 * i]))
+    for _ in range(2):
+        toks = list(eng.decode_batch(ss, toks, want_logits=False))
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        toks = list(eng.decode_batch(ss, toks, want_logits=False))
+    dt = time.perf_counter() - t0
+    for s in ss:
+        s.close()
+    return {"sessions": n, "rounds": steps, "tok_s": n * steps / dt, "ms_per_round": dt / steps * 1e3,
+            "context": len(prompt), "kv_cache": "f16"}
 
 
 def max_over_ranks(value: float, device=None) -> float:
-    """The job's time for a weak-scaling replica run: the max of every
-    rank's device-timed interval (all-reduce MAX over the process group; the
-    NCCL group on GPUs, gloo on CPU)."""
+    """The job's time: the max of every rank's device-timed interval
+    (all-reduce MAX over the process group; NCCL on GPUs, gloo on CPU)."""
     import torch
     import torch.distributed as dist
 
@@ -286,8 +387,8 @@ def max_over_ranks(value: float, device=None) -> float:
 
 
 def replica_value(steps_per_rank: int, world: int, seconds: float) -> float:
-    """Whole-job throughput: every rank decodes steps_per_rank tokens of its
-    own session; the job is done when the slowest rank is."""
+    """Whole-job throughput when every rank decodes its own stream of
+    steps_per_rank tokens and the job ends with the slowest rank."""
     return world * steps_per_rank / seconds
 
 
@@ -295,10 +396,12 @@ def run_ours(args):
     import torch
 
     rank, world, local = dist_env()
+    group = None
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
     device = local
     torch.cuda.set_device(device)
     from overfit_b200 import build, engine
@@ -311,21 +414,23 @@ def run_ours(args):
     pp = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pp):
         peaks = json.load(open(pp))
+    extra = world == 1 and not args.no_extra and not args.layers
 
+    # every rank draws the same weights (seeded device generator) and keeps
+    # its tensor-parallel shard of them
     t0 = time.time()
     mf = engine.synthetic_model(cfg, seed=1, device=device)
-    eng = engine.CudaLlamaInferenceEngine(cfg, mf, device=device)
+    eng = engine.CudaLlamaInferenceEngine(cfg, mf, device=device, tp_group=group)
     gen_s = time.time() - t0
-    max_ctx = args.prompt + args.warmup + args.steps + 64
-    prompt = np.random.default_rng(1234 + rank).integers(0, cfg["vocab"], args.prompt).astype(np.int32)
+    e2e_steps = min(args.steps, 64)
+    max_ctx = args.prompt + args.warmup + args.steps + e2e_steps + 64
+    prompt = np.random.default_rng(1234).integers(0, cfg["vocab"], args.prompt).astype(np.int32)
 
-    # The reference's default F32 KV cache (exact attention order), timed on
-    # a shorter run and reported beside the benchmark config's fp16 cache.
-    # The reference's own cache types (F32, its default, and Q8), attended in
+    # the reference's own cache types (F32, its default, and Q8), attended in
     # the reference's exact order, timed on shorter runs beside the
-    # benchmark config's fp16 cache.
+    # benchmark config's fp16 cache
     exact = {}
-    if args.kv == "f16" and not args.no_f32_line:
+    if extra and args.kv == "f16":
         for kvx in ("f32", "q8"):
             sx = eng.create_session(max_ctx, kvx)
             sx.prefill(prompt)
@@ -338,8 +443,8 @@ def run_ours(args):
             sx.generate_greedy(nx)
             ex1.record(stx)
             torch.cuda.synchronize(device)
-            dtx = max_over_ranks(ex0.elapsed_time(ex1) / 1e3, device)
-            exact[kvx] = {"kv_cache": kvx, "value": replica_value(nx, world, dtx), "unit": "tok/s", "steps": nx,
+            dtx = ex0.elapsed_time(ex1) / 1e3
+            exact[kvx] = {"kv_cache": kvx, "value": nx / dtx, "unit": "tok/s", "steps": nx,
                           "ms_per_step": dtx / nx * 1e3}
             sx.close()
 
@@ -363,60 +468,68 @@ def run_ours(args):
     torch.cuda.synchronize(device)
     clk = clocks.stop()
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
-    value = replica_value(args.steps, world, dt)
+    value = args.steps / dt  # one sequence's tokens: the whole job's output
 
-    # e2e: the session call with host buffers (token in, argmax out).
-    e2e_steps = min(args.steps, 64)
+    # e2e: the session call with host buffers (token in, argmax out), host clock
     tok = int(toks[-1])
+    if world > 1:
+        torch.distributed.barrier()
     torch.cuda.synchronize(device)
-    e0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(e2e_steps):
         tok = sess.decode(tok, want_logits=False)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, device)
-    e2e = replica_value(e2e_steps, world, e2e_dt)
+    e2e_dt = max_over_ranks(time.perf_counter() - h0, device)
+    e2e = e2e_steps / e2e_dt
 
     weight_bytes = eng.weight_bytes
     # K and V of every layer read once per step, at the run's mean context
     kv_elem = 2 if args.kv == "f16" else 4
     kv_bytes = 2 * cfg["n_layers"] * cfg["n_kv_heads"] * cfg["head_dim"] * kv_elem * (args.prompt + args.warmup +
                                                                                       args.steps // 2)
-    roof = gemv_roofline(torch, cfg, mf, device, peaks) if rank == 0 else None
-    pgemm = prefill_gemm(torch, cfg, mf, device) if rank == 0 and not args.layers else None
+    roof = gemv_roofline(torch, cfg, mf, device, peaks) if rank == 0 and world == 1 and not args.layers else None
+    cfg1 = gemv_config1(torch, device, peaks) if extra else None
+    pgemm = prefill_gemm(torch, device) if extra else None
+    multi = sessions16(torch, eng, cfg, prompt, min(args.steps, 32), device) if extra else None
     sess.close()
     eng.close()
     del mf
-    launches_per_step = 1 + 5 * cfg["n_layers"] + 1
+    qwen = qwen_config3(torch, device) if extra else None
+    launches_per_step = (2 + 5 * cfg["n_layers"]) if world == 1 else (3 + 7 * cfg["n_layers"])
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and extra and not args.no_cpu_baseline:
         try:
-            r = cpu_decode_sample(6)
+            r = cpu_decode_sample(args.prompt, 5)
             cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["cores"], "kind": "port", "sample": r["sample"]}
         except Exception as ex:  # report, never fail the GPU line
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
     if rank == 0:
-        step_bytes = weight_bytes + kv_bytes
+        # bytes every rank streams per step: its shard (world == 1: all)
+        step_bytes = weight_bytes + kv_bytes // world
         hbm = peaks.get("hbm_gbs", 6650.0)
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot (Q4_K/Q6_K/Q8_0 x Q8_K/Q8_0), fp32 accum",
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8 dot (Q4_K/Q6_K/Q8_0 x Q8_K/Q8_0), fp32 accum",
                 "data": "synthetic (random-init N(0,0.02), quantized on device)",
                 "config": {"workload": "llama3-8b-q4_k_m greedy decode batch 1, prompt %d, %s KV cache"
                                        % (args.prompt, args.kv),
                            "kv_cache": args.kv,
                            "model": "Llama-3-8B shape" + ("" if not args.layers else f" ({args.layers} layers)"),
-                           "global_batch": world, "seq_len": args.prompt, "parallelism": f"replicas x{world}",
-                           "l2": "inputs larger than L2 (%.2f GB of weights per step)" % (weight_bytes / 1e9)},
-                "bytes_per_step": step_bytes,
+                           "global_batch": 1, "seq_len": args.prompt,
+                           "parallelism": "tp%d" % world if world > 1 else "single GPU",
+                           "l2": "inputs larger than L2 (%.2f GB of weights per step per GPU)" % (weight_bytes / 1e9)},
+                "bytes_per_step_per_gpu": step_bytes,
                 "step_roofline": {"bound": "hbm", "tok_s_bound": hbm * 1e9 / step_bytes,
-                                  "frac": value / world / (hbm * 1e9 / step_bytes)},
+                                  "frac": value / (hbm * 1e9 / step_bytes)},
                 "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
-                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                        "clock": "host perf_counter around ovf_session_decode calls"},
                 "gpu_launches": launches_per_step * args.steps,
                 "f32_kv_exact": exact.get("f32"),
                 "q8_kv_exact": exact.get("q8"),
-                "prefill_gemm": pgemm,
+                "gemv_config1": cfg1,
+                "prefill_gemm_config2": pgemm,
+                "qwen2_05b_config3": qwen,
+                "sessions16_config4": multi,
                 "setup_s": {"model_gen_upload": gen_s, "prefill": prefill_s}}
         print(json.dumps(line), flush=True)
     if world > 1:

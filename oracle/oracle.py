@@ -88,6 +88,7 @@ def _declare(L):
         "orc_q8kv_quantize": (C.c_float, [P, C.c_int, P]),
         "orc_attention_single_head_q8": (None, [P, P, P, P, P, P, P, C.c_int, C.c_int, C.c_float]),
         "orc_expf_array": (None, [C.c_void_p, C.c_void_p, C.c_int64]),
+        "orc_session_fill_context": (C.c_int, [P, C.c_int, C.c_uint64]),
         "orc_session_position": (C.c_int, [P]),
         "orc_session_decode": (C.c_int, [P, C.c_int, P]),
         "orc_session_decode_layers": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P]),
@@ -396,6 +397,11 @@ class OracleSession:
         """KvCacheDType.Q8: per-vector int8 K/V + one scale each (set before
         the first token)."""
         lib().orc_session_set_kv_q8(self._s, int(on))
+
+    def fill_context(self, n: int, seed: int = 7):
+        """Timing support: n cached positions of N(0, 0.5) rows, position n."""
+        if lib().orc_session_fill_context(self._s, int(n), int(seed)) != 0:
+            raise ValueError("fill_context: n out of range or Q8 cache")
 
     def set_kv_fp16(self, on: bool = True):
         """Round cached K/V to fp16 as the GPU cache does (test switch)."""

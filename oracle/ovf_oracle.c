@@ -868,6 +868,24 @@ void orc_session_destroy(orc_session *s) {
     free(s);
 }
 void orc_session_reset(orc_session *s) { s->pos = 0; }
+
+/* Timing support (not part of the reference): positions [0, n) of every
+ * layer's F32 cache filled with N(0, 0.5) rows (seeded) and the position set
+ * to n, so a decode step can be timed at a long context without running the
+ * prompt through the model first. */
+int orc_session_fill_context(orc_session *s, int n, uint64_t seed) {
+    const orc_model *m = s->m;
+    if (n < 0 || n >= s->max_ctx || s->kv_q8) return -1;
+    const int hd = m->head_dim;
+    for (int l = 0; l < m->n_layers; l++)
+        for (int g = 0; g < m->n_kv_heads; g++) {
+            const int64_t base = (((int64_t)l * m->n_kv_heads + g) * s->max_ctx) * hd;
+            orc_fill_normal(s->kcache + base, (int64_t)n * hd, seed + 2 * ((uint64_t)l * m->n_kv_heads + g), 0.0, 0.5);
+            orc_fill_normal(s->vcache + base, (int64_t)n * hd, seed + 2 * ((uint64_t)l * m->n_kv_heads + g) + 1, 0.0, 0.5);
+        }
+    s->pos = n;
+    return 0;
+}
 void orc_session_set_kv_fp16(orc_session *s, int on) { s->kv_fp16 = on; }
 /* CreateSession(kvCacheDType: Q8) (CachedLlamaInferenceEngine.cs:360): set
  * before the first token. */

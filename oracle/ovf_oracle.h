@@ -127,6 +127,7 @@ float orc_q8kv_quantize(const float *src, int n, int8_t *dst);
 void orc_attention_single_head_q8(const float *q, const int8_t *kq, const float *ks, const int8_t *vq,
                                   const float *vs, float *out, float *scratch, int seq_len, int hd, float scale);
 /* Test switch: exp rounded once from double precision (as on the GPU). */
+int orc_session_fill_context(orc_session *s, int n, uint64_t seed);
 void orc_expf_array(const float *x, float *y, int64_t n);
 int  orc_session_position(const orc_session *s);
 /* One token through the stack; writes logits[vocab] when logits != NULL. */
