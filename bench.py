@@ -594,7 +594,33 @@ def _prof_gemv_gateup():
     print(json.dumps({"profile_target": "gemv_gateup", "launches": 6}))
 
 
+def _prof_gemv_config1(N: int):
+    """3 warm-up + 3 launches of the config-1 Q4_K projection (ProjectParallel,
+    K = 4096) over 8 rotating weight copies."""
+    import torch
+
+    from overfit_b200 import build
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight
+
+    build.build()
+    K = 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = GgmlQuant.quantize_q4_k(torch.randn(N, K, device="cuda", generator=g) * 0.02, K, N)
+    ws = [Q4KWeight(w.clone(), K, N) for _ in range(8)]
+    x = torch.randn(K, device="cuda", generator=g)
+    y = torch.empty(N, device="cuda")
+    q = torch.empty(K, dtype=torch.int8, device="cuda")
+    s = torch.empty(K // 256, device="cuda")
+    b = torch.empty(K // 16, dtype=torch.int16, device="cuda")
+    for i in range(6):
+        Q4KDotKernel.project_parallel(x, ws[i % 8], None, y, q, s, b)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_target": f"gemv_config1_{N}", "launches": 6}))
+
+
 PROFILE_TARGETS = {
+    "gemv_config1_4096": lambda: _prof_gemv_config1(4096),
+    "gemv_config1_14336": lambda: _prof_gemv_config1(14336),
     "attn_exact_f16": lambda: _prof_attn("f16"),
     "attn_exact_f32": lambda: _prof_attn("f32"),
     "gemv_gateup": _prof_gemv_gateup,
