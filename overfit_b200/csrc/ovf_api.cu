@@ -79,18 +79,21 @@ ovf_status ovf_kq_project(int32_t type, const float *x, const void *w, int64_t n
     if (st) return st;
     OVF_CHECK_ARG(x && y && act_q && act_scales && act_bsums, "ProjectParallel: null buffer");
     OVF_CHECK_ARG(aligned16(x), "ProjectParallel: input must be 16-byte aligned");
+    // QuantizeActivationQ8K once into the caller's scratch (as the reference
+    // fills it), then the projection of the pre-quantized activation, launched
+    // so that its weight streaming overlaps the quantization
+    st = launch_quantize_q8k(x, k, act_q, act_scales, act_bsums, S(stream));
+    if (st || n == 0) return st;
     GemvParams p{};
     p.nseg = 1;
     p.seg[0] = GemvSeg{(const uint8_t *)w, nullptr, bias, y, type, (int)n, 0};
     p.K = (int)k;
-    p.act_mode = ACT_F32;
-    p.x = x;
-    p.aq_out = act_q;
-    p.as_out = act_scales;
-    p.ab_out = act_bsums;
+    p.act_mode = ACT_PREQ_Q8K;
+    p.aq = act_q;
+    p.as = act_scales;
+    p.ab = act_bsums;
     p.epi = EPI_STORE;
-    if (n == 0) return launch_quantize_q8k(x, k, act_q, act_scales, act_bsums, S(stream));
-    return gemv_launch(p, S(stream), false);
+    return gemv_launch(p, S(stream), true);
 }
 
 ovf_status ovf_kq_project_prequantized(int32_t type, const void *w, int64_t n, int64_t k, const float *bias, float *y,

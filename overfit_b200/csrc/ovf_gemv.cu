@@ -673,7 +673,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
     pdl_wait();
     size_t eoff_w = 0, eoff_s = 0;
     if (routed) {
-        const int e = p.expert_sel[p.expert_slot];
+        int e = p.expert_sel[p.expert_slot];
+        if (p.expert_mod > 1) {
+            // expert parallel: another rank owns this expert
+            if (e % p.expert_mod != p.expert_rank) {
+                pdl_launch_dependents();
+                if (tid == 0) trace_mark(p.trace, TR_END);
+                return;
+            }
+            e /= p.expert_mod;
+        }
         eoff_w = (size_t)e * (size_t)p.expert_wstride;
         eoff_s = (size_t)e * (size_t)p.expert_sstride;
         if (warp == kProducerWarp && lane == 0)
@@ -821,6 +830,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const __grid
                     for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][grow] = y[0];
                     const unsigned long long kk = argmax_key(y[0], grow);
                     best = kk > best ? kk : best;
+                } else if (p.epi == EPI_ROWS_TP) {
+                    const size_t o = (size_t)p.tp_index0 * p.tp_rows + row;
+                    for (int w = 0; w < p.tp_world; ++w) p.tp_dst[w][o] = y[0];
                 } else if (p.epi != EPI_GROUPS_TP) {
                     float *out = p.seg[seg].out;
                     if (p.epi == EPI_RESIDUAL) out[row] = fadd(res, y[0]);

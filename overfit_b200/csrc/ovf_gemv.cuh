@@ -30,6 +30,7 @@ enum EpiMode : int {
     EPI_GROUPS_TP = 4,      // Q8_0 groups (heads): dst[(tp_index0 + group) * tp_rows + row] = group sum
     EPI_TERMS_TP = 5,       // every block's term: dst[(tp_index0 + block) * tp_rows + row]
     EPI_LOGITS_TP = 6,      // dst[tp_index0 + row] = sum; the rank's argmax key goes to tp_keys[w][tp_rank]
+    EPI_ROWS_TP = 7,        // dst[tp_index0 * tp_rows + row] = bias + sum (an expert's output for every rank)
 };
 
 // Device-resident per-session step state (greedy loop without host syncs).
@@ -93,6 +94,8 @@ struct GemvParams {
     int tp_world, tp_rank, tp_index0, tp_rows;
     int64_t expert_wstride;  // bytes between experts' quants
     int64_t expert_sstride;  // bytes between experts' Q8_0 scales
+    int expert_mod, expert_rank;  // expert parallel (mod > 1): run only if expert % mod == rank, as local
+                                  // expert expert / mod; other ranks' CTAs leave at once
     L2Prefetch pf;       // weights of a later launch to pull into L2 once this one's are issued
     TraceSlot *trace;    // OVF_TRACE timeline slot, or null
 };

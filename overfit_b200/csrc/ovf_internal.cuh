@@ -124,6 +124,8 @@ struct TpExchange {
 };
 ovf_status launch_tp_sum_combine(const TpExchange &x, const float *recv, int n, const float *bias, const float *resid,
                                  float *out, float *norm_out, int D, float eps, cudaStream_t st, bool pdl);
+ovf_status launch_tp_moe_combine(const TpExchange &x, const float *recv, const float *w, int K, const float *resid,
+                                 float *out, float *norm_out, int D, float eps, cudaStream_t st, bool pdl);
 ovf_status launch_tp_lm_finish(const TpExchange &x, const unsigned long long *keys, DevStep *step, int32_t *tokens_log,
                                cudaStream_t st, bool pdl);
 // ovf_moe.cu: router, combine, row gather/scatter of the MoE FFN.

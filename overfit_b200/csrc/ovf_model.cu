@@ -105,7 +105,8 @@ struct ovf_model {
     int tp_rank = 0, tp_world = 1;
     int h_loc = 0, kvh_loc = 0, ff_loc = 0, v_loc = 0, nb_down = 0;  // nb_down: down blocks of all ranks
     char *arena = nullptr;
-    size_t arena_bytes = 0, off_heads = 0, off_terms = 0, off_logits = 0, off_keys = 0, off_flags = 0, off_epoch = 0;
+    size_t arena_bytes = 0, off_heads = 0, off_terms = 0, off_logits = 0, off_keys = 0, off_flags = 0, off_epoch = 0,
+           off_moe = 0;
     char *peer[8] = {};
     bool tp_ready = false;
 };
@@ -455,6 +456,25 @@ static void trace_report(ovf_session *s) {
                 x.second.gap / x.second.n);
 }
 
+// Tensor parallelism: the exchange slot `slot` of the model's arena.
+TpExchange tp_exchange(const ovf_model *m, int slot) {
+    TpExchange x{};
+    for (int w = 0; w < m->tp_world; ++w) x.flags_peer[w] = reinterpret_cast<unsigned *>(m->peer[w] + m->off_flags);
+    x.flags_own = reinterpret_cast<const unsigned *>(m->arena + m->off_flags);
+    x.epoch = reinterpret_cast<const unsigned *>(m->arena + m->off_epoch);
+    x.world = m->tp_world;
+    x.rank = m->tp_rank;
+    x.slot = slot;
+    return x;
+}
+
+// Every rank's exchange buffer at byte offset `off` + `elem` floats.
+void tp_dsts(const ovf_model *m, size_t off, size_t elem, GemvParams *p) {
+    for (int w = 0; w < m->tp_world; ++w) p->tp_dst[w] = reinterpret_cast<float *>(m->peer[w] + off) + elem;
+    p->tp_world = m->tp_world;
+    p->tp_rank = m->tp_rank;
+}
+
 // MoE FFN of one decode token (MoeFeedForwardBlock.Decode, :79-138): the
 // router on the device, then for each of the k selected experts a fused
 // gate/up GEMV (SiLU*up) and a down GEMV whose weights are picked by the
@@ -468,10 +488,17 @@ ovf_status enqueue_moe_ffn(ovf_session *s, const DevLayer &L, cudaStream_t st, S
     ovf_status r = launch_moe_route(s->after, D, L.ffn_norm, &s->norm_s[1], L.router, 1, D, c.n_experts, K,
                                     c.normalize_experts, s->msel, s->mw, st, true);
     if (r) return r;
+    const ovf_model *m = s->m;
+    const bool ep = m->tp_world > 1;
+    const int l = (int)(&L - m->layers.data());
     for (int j = 0; j < K; ++j) {
         GemvParams p{};
         p.nseg = 2;
         p.pair = 1;
+        if (ep) {
+            p.expert_mod = m->tp_world;
+            p.expert_rank = m->tp_rank;
+        }
         p.seg[0] = seg_of(L.gate, nullptr, s->mh + (size_t)j * FF);
         p.seg[1] = seg_of(L.up, nullptr, s->mh + (size_t)j * FF);
         p.seg[0].rows = p.seg[1].rows = FF;
@@ -500,29 +527,24 @@ ovf_status enqueue_moe_ffn(ovf_session *s, const DevLayer &L, cudaStream_t st, S
         q.expert_slot = j;
         q.expert_wstride = L.d_wstride;
         q.expert_sstride = L.d_sstride;
+        if (ep) {
+            // the owner of expert sel[j] writes its output into every rank's slot j
+            q.expert_mod = m->tp_world;
+            q.expert_rank = m->tp_rank;
+            q.epi = EPI_ROWS_TP;
+            tp_dsts(m, m->off_moe, ((size_t)l * K) * D, &q);
+            q.tp_index0 = j;
+            q.tp_rows = D;
+        }
         q.trace = tslot("down");
         if ((r = gemv_launch(q, st, true))) return r;
     }
+    if (ep) {
+        const float *recv = reinterpret_cast<const float *>(m->arena + m->off_moe) + (size_t)l * K * D;
+        return launch_tp_moe_combine(tp_exchange(m, 2 * l + 1), recv, s->mw, K, s->after, s->hidden, &s->norm_s[0], D,
+                                     c.eps, st, true);
+    }
     return launch_moe_combine(s->after, s->meo, s->mw, K, D, s->hidden, &s->norm_s[0], c.eps, st, true);
-}
-
-// Tensor parallelism: the exchange slot `slot` of the model's arena.
-TpExchange tp_exchange(const ovf_model *m, int slot) {
-    TpExchange x{};
-    for (int w = 0; w < m->tp_world; ++w) x.flags_peer[w] = reinterpret_cast<unsigned *>(m->peer[w] + m->off_flags);
-    x.flags_own = reinterpret_cast<const unsigned *>(m->arena + m->off_flags);
-    x.epoch = reinterpret_cast<const unsigned *>(m->arena + m->off_epoch);
-    x.world = m->tp_world;
-    x.rank = m->tp_rank;
-    x.slot = slot;
-    return x;
-}
-
-// Every rank's exchange buffer at byte offset `off` + `elem` floats.
-void tp_dsts(const ovf_model *m, size_t off, size_t elem, GemvParams *p) {
-    for (int w = 0; w < m->tp_world; ++w) p->tp_dst[w] = reinterpret_cast<float *>(m->peer[w] + off) + elem;
-    p->tp_world = m->tp_world;
-    p->tp_rank = m->tp_rank;
 }
 
 // Enqueues one token's kernels on s->stream.
@@ -1190,7 +1212,7 @@ extern "C" {
 static ovf_status tp_arena_alloc(ovf_model *m) {
     const ovf_model_config &c = m->cfg;
     const DevLayer &L0 = m->layers[0];
-    m->nb_down = L0.down.type == OVF_TYPE_Q8_0 ? c.d_ff / 32 : c.d_ff / 256;
+    m->nb_down = c.n_experts ? 0 : L0.down.type == OVF_TYPE_Q8_0 ? c.d_ff / 32 : c.d_ff / 256;
     size_t o = 0;
     auto take = [&](size_t bytes) {
         const size_t at = o;
@@ -1198,7 +1220,8 @@ static ovf_status tp_arena_alloc(ovf_model *m) {
         return at;
     };
     m->off_heads = take((size_t)c.n_layers * c.n_heads * c.d_model * 4);
-    m->off_terms = take((size_t)c.n_layers * m->nb_down * c.d_model * 4);
+    m->off_terms = c.n_experts ? 0 : take((size_t)c.n_layers * m->nb_down * c.d_model * 4);
+    m->off_moe = c.n_experts ? take((size_t)c.n_layers * c.n_experts_used * c.d_model * 4) : 0;
     m->off_logits = take((size_t)c.vocab * 4);
     m->off_keys = take((size_t)m->tp_world * 8);
     m->off_flags = take((size_t)(2 * c.n_layers + 1) * m->tp_world * 4);
@@ -1231,10 +1254,11 @@ static ovf_status model_create(int32_t device, const ovf_model_config *cfg, cons
                   world);
     const bool tp = world > 1;
     if (tp) {
-        OVF_CHECK_ARG(c.n_experts == 0, "tensor parallelism: MoE models are split by experts, not heads");
+        OVF_CHECK_ARG(c.n_experts == 0 || c.n_experts % world == 0,
+                      "expert parallelism: %d experts do not split over %d ranks", c.n_experts, world);
         OVF_CHECK_ARG(c.n_kv_heads % world == 0, "tensor parallelism: %d KV heads do not split over %d ranks",
                       c.n_kv_heads, world);
-        OVF_CHECK_ARG(c.d_ff % world == 0 && (c.d_ff / world) % 256 == 0,
+        OVF_CHECK_ARG(c.n_experts > 0 || (c.d_ff % world == 0 && (c.d_ff / world) % 256 == 0),
                       "tensor parallelism: d_ff %d must split into multiples of 256", c.d_ff);
         OVF_CHECK_ARG(c.vocab % world == 0, "tensor parallelism: vocab %d must split evenly", c.vocab);
     }
@@ -1246,7 +1270,7 @@ static ovf_status model_create(int32_t device, const ovf_model_config *cfg, cons
     m->tp_world = world;
     m->h_loc = c.n_heads / world;
     m->kvh_loc = c.n_kv_heads / world;
-    m->ff_loc = c.d_ff / world;
+    m->ff_loc = c.n_experts ? c.d_ff : c.d_ff / world;  // experts stay whole (expert parallel)
     m->v_loc = c.vocab / world;
     m->layers.resize(c.n_layers);
     const int64_t D = c.d_model, hd = c.head_dim, QD = (int64_t)c.n_heads * hd, KD = (int64_t)c.n_kv_heads * hd;
@@ -1286,7 +1310,27 @@ static ovf_status model_create(int32_t device, const ovf_model_config *cfg, cons
         if (!st) st = upload_vec(m, lt[8], D, &L.bo, "attn_output.bias");
         if (!st) st = upload_vec(m, lt[9], D, &L.ffn_norm, "ffn_norm");
         const int64_t E = c.n_experts > 0 ? c.n_experts : 1;
-        if (!tp) {
+        if (tp && c.n_experts > 0) {
+            // expert parallel: this rank's experts e (e % world == rank), stacked
+            // in order as local experts e / world
+            const int64_t El = c.n_experts / world;
+            for (int i = 10; i <= 12 && !st; ++i)
+                if (!lt[i].data || lt[i].rows != E * (i == 12 ? D : c.d_ff)) {
+                    set_error("layer %d: expert weights must hold n_experts matrices", l);
+                    st = OVF_EINVAL;
+                }
+            std::vector<uint8_t> gb, ub, db;
+            auto gather = [&](const ovf_tensor &t, int64_t rows_e, std::vector<uint8_t> &buf) {
+                const int64_t eb = rows_e * host_row_bytes(t.type, t.cols);
+                buf.resize((size_t)(El * eb));
+                for (int64_t j = 0; j < El; ++j)
+                    memcpy(buf.data() + j * eb, static_cast<const char *>(t.data) + (j * world + rank) * eb, (size_t)eb);
+                return ovf_tensor{t.type, buf.data(), El * rows_e, t.cols};
+            };
+            if (!st) st = upload_matrix(m, gather(lt[10], c.d_ff, gb), El * c.d_ff, D, false, &L.gate, "ffn_gate");
+            if (!st) st = upload_matrix(m, gather(lt[11], c.d_ff, ub), El * c.d_ff, D, false, &L.up, "ffn_up");
+            if (!st) st = upload_matrix(m, gather(lt[12], D, db), El * D, c.d_ff, false, &L.down, "ffn_down");
+        } else if (!tp) {
             if (!st) st = upload_matrix(m, lt[10], E * c.d_ff, D, false, &L.gate, "ffn_gate");
             if (!st) st = upload_matrix(m, lt[11], E * c.d_ff, D, false, &L.up, "ffn_up");
             if (!st) st = upload_matrix(m, lt[12], E * D, c.d_ff, false, &L.down, "ffn_down");
@@ -1321,9 +1365,10 @@ static ovf_status model_create(int32_t device, const ovf_model_config *cfg, cons
                     set_error("layer %d: expert matrices must be multiples of 16 bytes", l);
                     st = OVF_EINVAL;
                 }
-                // a decode step streams n_experts_used of the n_experts
-                m->weight_bytes -= (int64_t)(c.n_experts - c.n_experts_used) *
-                                   (2 * (L.gu_wstride + L.gu_sstride) + L.d_wstride + L.d_sstride);
+                // a decode step streams n_experts_used of the n_experts (over all ranks)
+                const int64_t per = 2 * (L.gu_wstride + L.gu_sstride) + L.d_wstride + L.d_sstride;
+                m->weight_bytes -= (int64_t)(c.n_experts / world) * per;
+                m->weight_bytes += (int64_t)c.n_experts_used * per / world;
             }
         }
         if (!st && (!L.attn_norm || !L.ffn_norm)) {

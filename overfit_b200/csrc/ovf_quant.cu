@@ -14,6 +14,10 @@ namespace ovf {
 // 256-element block, 8 consecutive elements per lane.
 __global__ void quantize_q8k_kernel(const float *__restrict__ x, int64_t nblocks, int8_t *__restrict__ q,
                                     float *__restrict__ scales, int16_t *__restrict__ bsums) {
+    // a dependent GEMV may launch at once and stream its weights while the
+    // activation is quantized (it reads the activation after its
+    // griddepcontrol.wait, i.e. after this grid has completed)
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= nblocks) return;

@@ -91,6 +91,35 @@ ovf_status launch_tp_sum_combine(const TpExchange &x, const float *recv, int n, 
     return e == cudaSuccess ? OVF_OK : cuda_status(e, "tp_sum_combine");
 }
 
+// Expert parallel combine: every rank's selected experts' outputs y_j
+// (written by their owners) in top-k order, hidden = after + (((0 + w_0 y_0)
+// + w_1 y_1) + ...), then the next RMSNorm's scale (MoeFeedForwardBlock.Decode
+// :121-137 and the residual).  One CTA.
+__global__ void tp_moe_combine_kernel(const TpExchange x, const float *__restrict__ recv, const float *__restrict__ w,
+                                      int K, const float *__restrict__ resid, float *__restrict__ out, float *norm_out,
+                                      int D, float eps) {
+    pdl_wait();
+    if (threadIdx.x == 0) tp_signal_and_wait(x);
+    __syncthreads();
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float f = 0.0f;
+        for (int j = 0; j < K; ++j) f = fadd(f, fmul(w[j], __ldcg(recv + (size_t)j * D + i)));
+        out[i] = fadd(resid[i], f);
+    }
+    __syncthreads();
+    __shared__ __align__(16) float stage[2048];
+    const float ss = cta_seq_sumsq(out, D, 0.0f, stage);
+    if (threadIdx.x == 0 && norm_out) *norm_out = rms_scale(ss, D, eps);
+    pdl_launch_dependents();
+}
+
+ovf_status launch_tp_moe_combine(const TpExchange &x, const float *recv, const float *w, int K, const float *resid,
+                                 float *out, float *norm_out, int D, float eps, cudaStream_t st, bool pdl) {
+    cudaError_t e = launch_pdl(tp_moe_combine_kernel, dim3(1), dim3(1024), 0, st, pdl, x, recv, w, K, resid, out,
+                               norm_out, D, eps);
+    return e == cudaSuccess ? OVF_OK : cuda_status(e, "tp_moe_combine");
+}
+
 // The greedy token from every rank's first-maximum key: the largest key
 // (orderable logit, then the lower index) is the whole vocabulary's.
 __global__ void tp_lm_finish_kernel(const TpExchange x, const unsigned long long *keys, DevStep *step,

@@ -98,16 +98,19 @@ def model_config(cfg: dict) -> ModelConfig:
 def tp_check(cfg: dict, world: int) -> None:
     """The shapes tensor parallelism over `world` ranks accepts (the checks
     ovf_model_create_tp makes): KV heads, FFN rows in 256-blocks and the
-    vocabulary split evenly; no MoE (experts are split by expert instead)."""
+    vocabulary split evenly; MoE models split their experts whole (expert
+    parallelism, attention still split by heads)."""
     if world < 1 or world > 8:
         raise ValueError("tensor parallelism: 1..8 ranks")
     if world == 1:
         return
-    if cfg.get("n_experts", 0):
-        raise ValueError("tensor parallelism: MoE models are split by experts, not heads")
     if cfg["n_kv_heads"] % world:
         raise ValueError(f"tensor parallelism: {cfg['n_kv_heads']} KV heads do not split over {world} ranks")
-    if cfg["d_ff"] % world or (cfg["d_ff"] // world) % 256:
+    if cfg.get("n_experts", 0):
+        # expert parallel: rank r owns the experts e with e % world == r
+        if cfg["n_experts"] % world:
+            raise ValueError(f"expert parallelism: {cfg['n_experts']} experts do not split over {world} ranks")
+    elif cfg["d_ff"] % world or (cfg["d_ff"] // world) % 256:
         raise ValueError(f"tensor parallelism: d_ff {cfg['d_ff']} must split into multiples of 256")
     if cfg["vocab"] % world:
         raise ValueError(f"tensor parallelism: vocab {cfg['vocab']} must split evenly")

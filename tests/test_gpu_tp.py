@@ -94,3 +94,25 @@ def test_tp2_tiny_llama_bit_exact(orc, kv):
         assert tok == int(np.argmax(lg))
         if i < len(t0) - 1:
             lg = ref.decode(tok)
+
+
+@needs2
+def test_ep2_tiny_mixtral_bit_exact(orc):
+    """Expert parallelism: Mixtral-style MoE with experts split whole over 2
+    ranks (rank r owns experts e % 2 == r, attention split by heads); the
+    owner of each selected expert sends its output to every rank, which sum
+    them in top-k order: bit-identical to the unsplit restatement."""
+    from model_helpers import TINY_MIXTRAL, oracle_session
+    cfg = dict(TINY_MIXTRAL)
+    prompt = [int(x) for x in np.random.default_rng(8).integers(0, cfg["vocab"], 10)]
+    out = _run(cfg, 22, "f32", prompt, 16)
+    (_, t0, l0, d0, mf), (_, t1, l1, d1, _) = out
+    assert t0 == t1 and d0 == d1
+    ref = oracle_session(cfg, mf, len(prompt) + 32)
+    for t in prompt:
+        lg = ref.decode(t)
+    for i, (tok, got) in enumerate(zip(t0, l0)):
+        np.testing.assert_array_equal(got, lg, err_msg=f"step {i}")
+        assert tok == int(np.argmax(lg))
+        if i < len(t0) - 1:
+            lg = ref.decode(tok)

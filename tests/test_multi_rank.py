@@ -88,7 +88,8 @@ def test_tp_split_rules():
         engine.tp_check(cfg, 3)  # 8 KV heads over 3 ranks
     with pytest.raises(ValueError):
         engine.tp_check(dict(cfg, d_ff=14336 + 256), 8)
+    engine.tp_check(dict(cfg, n_experts=8, n_experts_used=2, d_ff=14336 + 256), 8)  # experts stay whole
     with pytest.raises(ValueError):
-        engine.tp_check(dict(cfg, n_experts=8, n_experts_used=2), 2)
+        engine.tp_check(dict(cfg, n_experts=6, n_experts_used=2), 4)
     with pytest.raises(ValueError):
         engine.tp_check(cfg, 16)
