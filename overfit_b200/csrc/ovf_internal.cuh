@@ -92,6 +92,10 @@ ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool p
 // ovf_attn_group.cu: F32 / fp16 caches, one cluster per KV head (exact order).
 bool attn_group_supported(int H, int KVH, int hd, int kv_dtype, int seq_cap, int smem_optin_bytes);
 ovf_status launch_attention_group(const AttnParams &p, int seq_cap, cudaStream_t st, bool pdl, int kv_dtype);
+// ovf_attn_rows.cu: a prefill chunk's causal attention, one thread per chain.
+bool attn_rows_supported(int hd, int kv_dtype);
+int64_t attn_rows_scratch_floats(int rows, int H, int max_ctx);
+ovf_status launch_attention_rows(const AttnParams &p, int pos0, float *P, cudaStream_t st, int kv_dtype);
 // ovf_attn_exact.cu: F32 / Q8 / fp16 caches in the reference's operation order (bit-exact on the cached values).
 bool attn_exact_supported(int hd);
 int attn_exact_max_seq(int hd);

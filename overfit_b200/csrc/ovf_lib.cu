@@ -11,5 +11,6 @@
 #include "ovf_attn_cluster.cu"
 #include "ovf_attn_group.cu"
 #include "ovf_attn_exact.cu"
+#include "ovf_attn_rows.cu"
 #include "ovf_model.cu"
 #include "ovf_noalloc.cu"

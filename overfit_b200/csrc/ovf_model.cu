@@ -145,6 +145,7 @@ struct ovf_session {
     int16_t *pab = nullptr;
     int32_t *ptok = nullptr;
     MoeRows pmoe;  // MoE scratch of the prefill rows
+    float *pattn = nullptr;  // prefill attention: p_t of every (row, head) of a chunk [rows][heads][max_ctx]
     // speculative verify: per-row logits and argmax of one verify batch
     float *vlogits = nullptr;
     int32_t *vargmax = nullptr;
@@ -881,6 +882,9 @@ ovf_status prefill_alloc(ovf_session *s) {
     A((void **)&s->ptok, (size_t)(s->max_ctx + 1) * 4);
     A((void **)&s->pscale, 16);
     if (!st && c.n_experts > 0) st = moe_rows_alloc(c, kPrefillRows, s->allocs, &s->pmoe);
+    const int64_t pfl = attn_rows_scratch_floats(kPrefillRows, s->m->h_loc, s->max_ctx);
+    if (!st && attn_rows_supported(c.head_dim, s->kv_dtype) && pfl * 4 <= ((int64_t)512 << 20))
+        A((void **)&s->pattn, (size_t)pfl * 4);
     if (!st) s->pf_rows = kPrefillRows;
     return st;
 }
@@ -1055,7 +1059,11 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n, bool all_rows = false)
                 a.max_ctx = s->max_ctx;
                 a.scale = 1.0f / sqrtf((float)hd);
                 if ((r = launch_kv_append_rows(a, s->pk, s->pv, M, base + r0, s->kv_dtype, st))) return r;
-                if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) return r;
+                if (s->pattn) {
+                    if ((r = launch_attention_rows(a, base + r0, s->pattn, st, s->kv_dtype))) return r;
+                } else if ((r = launch_attention_exact(a, s->max_ctx, st, false, s->kv_dtype))) {
+                    return r;
+                }
             }
             // Wo (Q8_0) per head, heads in order on the bias, + residual; FFN
             if ((r = rows_wo_ffn(m, L, pb, &s->pmoe, M, st))) return r;
