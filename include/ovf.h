@@ -91,6 +91,18 @@ ovf_status ovf_q4k_project_gate_up(const float *x, const void *gate_w, const voi
 ovf_status ovf_kq_project_batched(int32_t type, const float *x, int64_t rows, const void *w, int64_t n,
                                   int64_t k, const float *bias, float *y, int8_t *act_q,
                                   float *act_scales, int16_t *act_bsums, void *stream);
+/* Runtime/Q4KDotKernel.cs:819 ProjectBatchedWeightStationary on the tensor
+ * cores (tcgen05.mma, fp32 accumulators in TMEM): the same outputs as
+ * ovf_kq_project_batched, bit for bit (the integer parts of every
+ * super-block dot are exact in the fp32 accumulators; the reference's fp32
+ * tail runs in the epilogue).  Q4_K weights only.  Scratch: the activation
+ * quantization as for ovf_kq_project_batched plus `scratch` of
+ * ovf_tc_scratch_bytes(rows, k) bytes (16-byte aligned) for the packed
+ * operand tiles. */
+int64_t ovf_tc_scratch_bytes(int64_t rows, int64_t k);
+ovf_status ovf_kq_project_batched_tc(int32_t type, const float *x, int64_t rows, const void *w, int64_t n,
+                                     int64_t k, const float *bias, float *y, int8_t *act_q, float *act_scales,
+                                     int16_t *act_bsums, void *scratch, void *stream);
 /* Runtime/Q8DotKernel.cs:252 ProjectParallel over a de-interleaved Q8Weight:
  * y[o] = bias[o] + sum_b (wscale*xscale)*int8dot, ascending b.  Scratch
  * x_q [k], x_scales [k/32].  k % 32 == 0. */

@@ -61,6 +61,8 @@ SIGNATURES = {
     "ovf_kq_project_prequantized": (I32, [I32, P, I64, I64, P, P, P, P, P, P]),
     "ovf_q4k_project_gate_up": (I32, [P, P, P, I64, I64, P, P, P, P, P, P]),
     "ovf_kq_project_batched": (I32, [I32, P, I64, P, I64, I64, P, P, P, P, P, P]),
+    "ovf_tc_scratch_bytes": (I64, [I64, I64]),
+    "ovf_kq_project_batched_tc": (I32, [I32, P, I64, P, I64, I64, P, P, P, P, P, P, P]),
     "ovf_q8_0_project": (I32, [P, P, P, I64, I64, P, P, P, P, P]),
     "ovf_q8_0_project_batched": (I32, [P, I64, P, P, I64, I64, P, P, P, P, P]),
     "ovf_quantize_q4k": (I32, [P, I64, I64, P, P]),

@@ -156,6 +156,25 @@ ovf_status ovf_kq_project_batched(int32_t type, const float *x, int64_t rows, co
                                   S(stream));
 }
 
+int64_t ovf_tc_scratch_bytes(int64_t rows, int64_t k) {
+    if (rows <= 0 || k <= 0 || k % 256) return 0;
+    return tc_scratch_bytes(rows, k);
+}
+
+ovf_status ovf_kq_project_batched_tc(int32_t type, const float *x, int64_t rows, const void *w, int64_t n, int64_t k,
+                                     const float *bias, float *y, int8_t *act_q, float *act_scales,
+                                     int16_t *act_bsums, void *scratch, void *stream) {
+    ovf_status st = check_kq(type, w, n, k);
+    if (st) return st;
+    OVF_CHECK_ARG(type == OVF_TYPE_Q4_K, "ProjectBatched (tensor cores): Q4_K weights only");
+    OVF_CHECK_ARG(rows > 0 && rows <= (int64_t)65535 * 128, "ProjectBatched (tensor cores): rows must be in [1, 8388480]");
+    OVF_CHECK_ARG(x && y && act_q && act_scales && act_bsums && scratch, "ProjectBatched (tensor cores): null buffer");
+    if (n == 0) return OVF_OK;
+    st = launch_quantize_q8k(x, rows * k, act_q, act_scales, act_bsums, S(stream));
+    if (st) return st;
+    return launch_tc_project(type, w, bias, act_q, act_scales, act_bsums, y, n, k, rows, scratch, S(stream));
+}
+
 static ovf_status q8_project_impl(const float *x, const int8_t *wq, const float *ws, int64_t n, int64_t k,
                                   const float *bias, float *y, int8_t *xq, float *xs, cudaStream_t st) {
     OVF_CHECK_ARG(n >= 0 && n <= 0x7FFFFFFF, "Q8 ProjectParallel: bad output size");

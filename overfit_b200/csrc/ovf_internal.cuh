@@ -92,6 +92,12 @@ ovf_status launch_attention_cluster(const AttnParams &p, cudaStream_t st, bool p
 // ovf_attn_group.cu: F32 / fp16 caches, one cluster per KV head (exact order).
 bool attn_group_supported(int H, int KVH, int hd, int kv_dtype, int seq_cap, int smem_optin_bytes);
 ovf_status launch_attention_group(const AttnParams &p, int seq_cap, cudaStream_t st, bool pdl, int kv_dtype);
+// ovf_tc.cu: Q4_K prefill projection on tcgen05 tensor cores (bit-identical).
+int64_t tc_scratch_bytes(int64_t rows, int64_t k);
+bool tc_project_supported(int type, int64_t n, int64_t k, int64_t rows);
+ovf_status launch_tc_project(int type, const void *w, const float *bias, const int8_t *aq, const float *as,
+                             const int16_t *ab, float *y, int64_t n, int64_t k, int64_t rows, void *scratch,
+                             cudaStream_t st, const float *resid = nullptr);
 // ovf_attn_rows.cu: a prefill chunk's causal attention, one thread per chain.
 bool attn_rows_supported(int hd, int kv_dtype);
 int64_t attn_rows_scratch_floats(int rows, int H, int max_ctx);

@@ -5,6 +5,7 @@
 #include "ovf_quant.cu"
 #include "ovf_gemv.cu"
 #include "ovf_batched.cu"
+#include "ovf_tc.cu"
 #include "ovf_ops.cu"
 #include "ovf_moe.cu"
 #include "ovf_tp.cu"

@@ -218,6 +218,28 @@ class Q4KDotKernel(_KQuantKernel):
               "ProjectGateUpParallel")
 
 
+def _q4k_tc(input, rows, weight, bias, output, activation_quants, activation_scales, activation_bsums, scratch):
+    k, n = weight.input_size, weight.output_size
+    _need(input, torch.float32, rows * k, "input")
+    _need(output, torch.float32, rows * n, "output")
+    _need(activation_quants, torch.int8, rows * k, "activationQuants")
+    _need(activation_scales, torch.float32, rows * k // 256, "activationScales")
+    _need(activation_bsums, torch.int16, rows * k // 16, "activationBsums")
+    _need(scratch, torch.uint8, tc_scratch_bytes(rows, k), "scratch")
+    check(_lib.load().ovf_kq_project_batched_tc(TYPE_Q4_K, _ptr(input), rows, _ptr(weight.blocks), n, k, _ptr(bias),
+                                                _ptr(output), _ptr(activation_quants), _ptr(activation_scales),
+                                                _ptr(activation_bsums), _ptr(scratch), _stream()),
+          "ProjectBatched (tensor cores)")
+
+
+def tc_scratch_bytes(rows: int, k: int) -> int:
+    """Packed-operand scratch of Q4KDotKernel.project_batched_tensor_cores."""
+    return int(_lib.load().ovf_tc_scratch_bytes(rows, k))
+
+
+Q4KDotKernel.project_batched_tensor_cores = staticmethod(_q4k_tc)
+
+
 class Q6KDotKernel(_KQuantKernel):
     TYPE = TYPE_Q6_K
 

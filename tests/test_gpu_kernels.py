@@ -434,3 +434,63 @@ def test_swiglu_bit_exact(K, orc):
     K.apply_swiglu(dev(g), dev(u), out)
     ref = orc.silu(g.copy()) * u
     np.testing.assert_array_equal(host(out), ref)
+
+
+# ------------------------------------------------ tensor-core projection
+@pytest.mark.parametrize("rows,n,k,with_bias", [(1, 128, 256, False), (130, 300, 512, True), (64, 256, 4096, False),
+                                                (257, 14336, 4096, False)])
+def test_tensor_core_projection_bit_exact(K, orc, rows, n, k, with_bias):
+    """ProjectBatchedWeightStationary on tcgen05 tensor cores: every output
+    equal to the restatement's per-row dot (ragged row and token tiles)."""
+    rng = np.random.default_rng(rows + n)
+    wf = orc.fill_normal(n * k, rows + 5, 0.0, 0.02).reshape(n, k)
+    w = orc.quantize_q4k(wf)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    x[0, :256] = 0.0
+    bias = rng.uniform(-1, 1, n).astype(np.float32) if with_bias else None
+    y = torch.empty(rows * n, device="cuda")
+    q = torch.empty(rows * k, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows * k // 256, device="cuda")
+    b = torch.empty(rows * k // 16, dtype=torch.int16, device="cuda")
+    scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+    wt = K.Q4KWeight(dev(w), k, n)
+    bd = None if bias is None else dev(bias)
+    K.Q4KDotKernel.project_batched_tensor_cores(dev(x), rows, wt, bd, y, q, s, b, scratch)
+    if rows * n * k <= 1 << 30:
+        ref = orc.kq_project_batched(orc.Q4_K, x, w, n, k, bias)
+    else:  # the 8B shape: against the dp4a kernel (itself bit-exact to the restatement above)
+        y2 = torch.empty(rows * n, device="cuda")
+        K.Q4KDotKernel.project_batched(dev(x), rows, wt, bd, y2, q, s, b)
+        ref = host(y2).reshape(rows, n)
+    np.testing.assert_array_equal(host(y).reshape(rows, n), ref)
+
+
+def test_tensor_core_projection_extreme_magnitudes(K, orc):
+    """The largest integer sums the format allows (6-bit scales of 63, nibbles
+    0 and 15, activations of +-127) stay exact in the fp32 accumulators:
+    identical to the dp4a weight-stationary kernel."""
+    n, k, rows = 128, 512, 128
+    blk = np.zeros((n, k // 256, 144), np.uint8)
+    blk[:, :, 0:2] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    blk[:, :, 2:4] = np.frombuffer(np.float16(0.005).tobytes(), np.uint8)
+    blk[:, :, 4:16] = 0xFF                       # every scale and min 63
+    blk[: n // 2, :, 16:] = 0x00                 # nibbles 0 (centered -8)
+    blk[n // 2:, :, 16:] = 0xFF                  # nibbles 15
+    w = blk.reshape(-1)
+    x = np.ones((rows, k), np.float32)
+    x[rows // 2:] = -1.0
+    outs = []
+    for tc in (True, False):
+        y = torch.empty(rows * n, device="cuda")
+        q = torch.empty(rows * k, dtype=torch.int8, device="cuda")
+        s = torch.empty(rows * k // 256, device="cuda")
+        b = torch.empty(rows * k // 16, dtype=torch.int16, device="cuda")
+        wt = K.Q4KWeight(dev(w), k, n)
+        if tc:
+            scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+            K.Q4KDotKernel.project_batched_tensor_cores(dev(x), rows, wt, None, y, q, s, b, scratch)
+        else:
+            K.Q4KDotKernel.project_batched(dev(x), rows, wt, None, y, q, s, b)
+        outs.append(host(y))
+        assert int(np.abs(host(q)).min()) == 127
+    np.testing.assert_array_equal(outs[0], outs[1])
