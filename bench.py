@@ -286,7 +286,7 @@ def prefill_gemm(torch, device) -> dict:
     Q8_0, M in {1, 16, 128, 512, 2048} activation rows ~ N(0, 1), CUDA-event
     timed over 4 rotating weight copies (quantization of the rows included).
     2*M*N*K integer operations per launch."""
-    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight, Q8DotKernel, Q8Weight
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight, Q8DotKernel, Q8Weight, tc_scratch_bytes
 
     N, K = 14336, 4096
     g = torch.Generator(device=device).manual_seed(0)
@@ -306,9 +306,15 @@ def prefill_gemm(torch, device) -> dict:
         reps = 8 if M >= 512 else 32
         d4 = _timed(torch, lambda i: Q4KDotKernel.project_batched(x, M, q4[i % 4], None, y, aq, a4, ab), reps)
         d8 = _timed(torch, lambda i: Q8DotKernel.project_batched(x, M, q8[i % 4], None, y, aq, a8), reps)
+        sc = torch.empty(tc_scratch_bytes(M, K), dtype=torch.uint8, device=device)
+        dt = _timed(torch, lambda i: Q4KDotKernel.project_batched_tensor_cores(x, M, q4[i % 4], None, y, aq, a4, ab,
+                                                                               sc), reps)
         out[str(M)] = {"q4_k_us": d4 * 1e6, "q4_k_int_tops": 2 * M * N * K / d4 / 1e12,
+                       "q4_k_tc_us": dt * 1e6, "q4_k_tc_tops": 2 * M * N * K / dt / 1e12,
                        "q8_0_us": d8 * 1e6, "q8_0_int_tops": 2 * M * N * K / d8 / 1e12}
-    return {"kernel": "batched_project_kernel (weight-stationary, dp4a)", "n": N, "k": K, "rows": out}
+        del sc
+    return {"kernel": "batched_project_kernel (weight-stationary, dp4a); tc_q4k_project_kernel (tcgen05, fp16 "
+                      "exact-integer operands)", "n": N, "k": K, "rows": out}
 
 
 def qwen_config3(torch, device) -> dict:
@@ -618,7 +624,33 @@ def _prof_gemv_config1(N: int):
     print(json.dumps({"profile_target": f"gemv_config1_{N}", "launches": 6}))
 
 
+def _prof_prefill_tc(M: int):
+    """2 warm-up + 2 launches of the tensor-core Q4_K prefill projection,
+    M activation rows x [14336 x 4096], over 2 weight copies (0.7 GB)."""
+    import torch
+
+    from overfit_b200 import build
+    from overfit_b200.kernels import GgmlQuant, Q4KDotKernel, Q4KWeight, tc_scratch_bytes
+
+    build.build()
+    N, K = 14336, 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w = GgmlQuant.quantize_q4_k(torch.randn(N, K, device="cuda", generator=g) * 0.02, K, N)
+    ws = [Q4KWeight(w.clone(), K, N) for _ in range(2)]
+    x = torch.randn(M * K, device="cuda", generator=g)
+    y = torch.empty(M * N, device="cuda")
+    q = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    s = torch.empty(M * K // 256, device="cuda")
+    b = torch.empty(M * K // 16, dtype=torch.int16, device="cuda")
+    sc = torch.empty(tc_scratch_bytes(M, K), dtype=torch.uint8, device="cuda")
+    for i in range(4):
+        Q4KDotKernel.project_batched_tensor_cores(x, M, ws[i % 2], None, y, q, s, b, sc)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_target": f"prefill_tc_{M}", "launches": 4}))
+
+
 PROFILE_TARGETS = {
+    "prefill_tc_512": lambda: _prof_prefill_tc(512),
     "gemv_config1_4096": lambda: _prof_gemv_config1(4096),
     "gemv_config1_14336": lambda: _prof_gemv_config1(14336),
     "attn_exact_f16": lambda: _prof_attn("f16"),

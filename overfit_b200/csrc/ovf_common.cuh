@@ -155,6 +155,25 @@ __device__ __forceinline__ bool mbar_wait_sleep_bounded(uint64_t *bar, uint32_t 
     return false;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Polling wait (non-blocking test_wait): gives up after 2^28 polls (well
+// over a second), raises the device error word and returns false.
+__device__ __forceinline__ bool mbar_poll_bounded(uint64_t *bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 28); ++i)
+        if (mbar_test_wait(bar, parity)) return true;
+    raise_dev_error(DEVERR_MBAR_TIMEOUT);
+    return false;
+}
+
 // Bounded wait: gives up after ~2^26 polls (each try_wait itself suspends
 // for a while), raises the device error word and returns false.  A correct
 // program never gets near the limit.
