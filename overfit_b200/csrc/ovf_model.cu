@@ -143,6 +143,7 @@ struct ovf_session {
           *pg = nullptr, *pu = nullptr, *ph = nullptr, *pas = nullptr, *pscale = nullptr;
     int8_t *paq = nullptr;
     int16_t *pab = nullptr;
+    void *ptc = nullptr;  // packed operands of the tensor-core Q4_K projection
     int32_t *ptok = nullptr;
     MoeRows pmoe;  // MoE scratch of the prefill rows
     float *pattn = nullptr;  // prefill attention: p_t of every (row, head) of a chunk [rows][heads][max_ctx]
@@ -879,6 +880,7 @@ ovf_status prefill_alloc(ovf_session *s) {
     A((void **)&s->paq, R * KM);
     A((void **)&s->pas, R * KM / 32 * 4);
     A((void **)&s->pab, R * KM / 16 * 2);
+    A(&s->ptc, (size_t)tc_scratch_bytes((int64_t)R, (int64_t)KM));
     A((void **)&s->ptok, (size_t)(s->max_ctx + 1) * 4);
     A((void **)&s->pscale, 16);
     if (!st && c.n_experts > 0) st = moe_rows_alloc(c, kPrefillRows, s->allocs, &s->pmoe);
@@ -895,7 +897,14 @@ struct ActRows {  // quantized activation rows (Q8_K or Q8_0) of a batch
     int8_t *aq;
     float *as;
     int16_t *ab;
+    void *tc = nullptr;  // tensor-core operand scratch (tc_scratch_bytes of the rows), or none
 };
+
+// From this many rows on, Q4_K projections run on the tensor cores
+// (tc_q4k_project_kernel); fewer rows stay on the dp4a weight-stationary
+// kernel, which streams the weights once with no operand expansion.  Both are
+// bit-identical to the reference's per-row dot.
+constexpr int kTcMinRows = 32;
 
 ovf_status quantize_rows_for(const ActRows &ar, const DevWeight &w, const float *x, int rows, int64_t k, int *fam,
                              cudaStream_t st) {
@@ -908,6 +917,8 @@ ovf_status quantize_rows_for(const ActRows &ar, const DevWeight &w, const float 
 
 ovf_status project_rows(const ActRows &ar, const DevWeight &w, const float *bias, float *y, int rows, cudaStream_t st,
                         int group = 0, const float *resid = nullptr) {
+    if (ar.tc && group == 0 && rows >= kTcMinRows && tc_project_supported(w.type, w.rows, w.cols, rows))
+        return launch_tc_project(w.type, w.data, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols, rows, ar.tc, st, resid);
     const size_t qbytes = w.type == OVF_TYPE_Q8_0 ? (size_t)w.rows * w.cols : (size_t)tensor_bytes(w.type, w.rows, w.cols);
     return launch_batched_project(w.type, w.data, w.scales, qbytes, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols,
                                   rows, st, group, resid);
@@ -1016,7 +1027,7 @@ ovf_status enqueue_prefill_batched(ovf_session *s, int n, bool all_rows = false)
     const int D = c.d_model, H = c.n_heads, KVH = c.n_kv_heads, hd = c.head_dim, FF = c.d_ff;
     const int QD = H * hd, KD = KVH * hd;
     const int base = s->pos;
-    const ActRows ar{s->paq, s->pas, s->pab};
+    const ActRows ar{s->paq, s->pas, s->pab, s->ptc};
     const RowBufs pb{ar, s->px, s->pa, s->pn, s->pq, s->pk, s->pv, s->patt, s->pg, s->pu, s->ph};
     ovf_status r = OVF_OK;
     int last_rows = 0;
