@@ -649,7 +649,33 @@ def _prof_prefill_tc(M: int):
     print(json.dumps({"profile_target": f"prefill_tc_{M}", "launches": 4}))
 
 
+def _prof_prefill_layers():
+    """A 2048-token prefill (8 chunks of 256 rows) through 2 layers of the
+    Llama-3-8B shape (Q4_K_M, fp16 KV cache): every per-layer launch of the
+    batched prefill, for a launch list."""
+    import time
+
+    import torch
+
+    from overfit_b200 import build, engine
+
+    build.build()
+    cfg = dict(engine.LLAMA3_8B, n_layers=2)
+    mf = engine.synthetic_model(cfg, seed=1, device=0)
+    eng = engine.CudaLlamaInferenceEngine(cfg, mf, device=0)
+    s = eng.create_session(2048 + 8, "f16")
+    prompt = np.random.default_rng(5).integers(0, cfg["vocab"], 2048)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    s.prefill(prompt)
+    dt = time.perf_counter() - t0
+    s.close()
+    eng.close()
+    print(json.dumps({"profile_target": "prefill_2layers", "prefill_s": dt}))
+
+
 PROFILE_TARGETS = {
+    "prefill_2layers": _prof_prefill_layers,
     "prefill_tc_512": lambda: _prof_prefill_tc(512),
     "gemv_config1_4096": lambda: _prof_gemv_config1(4096),
     "gemv_config1_14336": lambda: _prof_gemv_config1(14336),

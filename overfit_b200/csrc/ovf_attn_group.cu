@@ -36,6 +36,12 @@ namespace gcg = cooperative_groups;
 __device__ unsigned long long g_phase[16];
 #define OVF_PHASE(i) \
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) g_phase[i] = clock64()
+}  // namespace ovf
+// Probe builds only: the last launch's phase clocks of CTA (0, 0).
+extern "C" __attribute__((visibility("default"))) int ovf_debug_attn_phases(unsigned long long *out) {
+    return (int)cudaMemcpyFromSymbol(out, ovf::g_phase, sizeof(ovf::g_phase));
+}
+namespace ovf {
 #else
 #define OVF_PHASE(i)
 #endif

@@ -431,7 +431,7 @@ __device__ __forceinline__ void prefetch_l2_slice(const L2Prefetch &pf, int cta,
 // griddepcontrol.wait return and last exit, in %globaltimer nanoseconds;
 // start is kept as its complement so that every field is an atomicMax.
 struct TraceSlot {
-    unsigned long long start_c, waited, end, pad;
+    unsigned long long start_c, waited, end, tiles;
 };
 
 __device__ __forceinline__ unsigned long long gtime_ns() {
@@ -440,12 +440,14 @@ __device__ __forceinline__ unsigned long long gtime_ns() {
     return t;
 }
 
-enum : int { TR_START = 0, TR_WAITED = 1, TR_END = 2 };
+// TR_TILES: a GEMV's tile CTAs (not its norm CTA) are done.
+enum : int { TR_START = 0, TR_WAITED = 1, TR_END = 2, TR_TILES = 3 };
 __device__ __forceinline__ void trace_mark(TraceSlot *t, int what) {
     if (!t) return;
     const unsigned long long v = gtime_ns();
     if (what == TR_START) atomicMax(&t->start_c, ~v);
     else if (what == TR_WAITED) atomicMax(&t->waited, v);
+    else if (what == TR_TILES) atomicMax(&t->tiles, v);
     else atomicMax(&t->end, v);
 }
 

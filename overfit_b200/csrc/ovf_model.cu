@@ -432,7 +432,7 @@ static void trace_report(ovf_session *s) {
     if (!s->trace || s->trace_n == 0) return;
     std::vector<TraceSlot> t(s->trace_n);
     if (cudaMemcpy(t.data(), s->trace, t.size() * sizeof(TraceSlot), cudaMemcpyDeviceToHost) != cudaSuccess) return;
-    struct Acc { double dur = 0, wait = 0, gap = 0; int n = 0; };
+    struct Acc { double dur = 0, wait = 0, gap = 0, tiles = 0; int n = 0; };
     std::vector<std::pair<std::string, Acc>> acc;
     const unsigned long long t0 = ~t[0].start_c;
     unsigned long long prev_end = t0;
@@ -448,14 +448,17 @@ static void trace_report(ovf_session *s) {
         a->dur += (double)(en - st) / 1e3;
         a->wait += wt > st ? (double)(wt - st) / 1e3 : 0.0;
         a->gap += ((double)st - (double)prev_end) / 1e3;
+        a->tiles += t[i].tiles > wt && wt > 0 ? (double)(t[i].tiles - wt) / 1e3 : 0.0;
         a->n += 1;
         prev_end = en;
     }
     fprintf(stderr, "[ovf trace] step span %.1f us over %d launches\n", (double)(prev_end - t0) / 1e3, s->trace_n);
     for (auto &x : acc)
-        fprintf(stderr, "[ovf trace] %-8s n=%3d  dur %8.2f us  pre-wait %7.2f us  start-after-prev-end %7.2f us\n",
+        fprintf(stderr,
+                "[ovf trace] %-8s n=%3d  dur %8.2f us  pre-wait %7.2f us  start-after-prev-end %7.2f us  "
+                "tiles-done-after-wait %7.2f us\n",
                 x.first.c_str(), x.second.n, x.second.dur / x.second.n, x.second.wait / x.second.n,
-                x.second.gap / x.second.n);
+                x.second.gap / x.second.n, x.second.tiles / x.second.n);
 }
 
 // Tensor parallelism: the exchange slot `slot` of the model's arena.
