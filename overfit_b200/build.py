@@ -6,6 +6,7 @@ torch extension.  Output: overfit_b200/libovf_cuda.so.
 """
 from __future__ import annotations
 
+import fcntl
 import glob
 import os
 import shutil
@@ -42,19 +43,30 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
+    """Compiles the library unless it is newer than every source.  Several
+    processes may call this at once (one per rank under torchrun): a file
+    lock serialises them, and the ones that waited find the library built."""
     if not force and up_to_date():
         return LIB
-    cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include"),
-           "-o", LIB + ".tmp", os.path.join(CSRC, "ovf_lib.cu")]
-    if verbose:
-        print(" ".join(cmd))
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        sys.stderr.write(r.stdout + r.stderr)
-        raise RuntimeError("nvcc failed building libovf_cuda.so")
-    if verbose and (r.stdout or r.stderr):
-        print(r.stdout + r.stderr)
-    os.replace(LIB + ".tmp", LIB)
+    with open(os.path.join(HERE, ".build.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():
+                return LIB
+            tmp = f"{LIB}.{os.getpid()}.tmp"
+            cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-I", os.path.join(ROOT, "include"),
+                   "-o", tmp, os.path.join(CSRC, "ovf_lib.cu")]
+            if verbose:
+                print(" ".join(cmd))
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout + r.stderr)
+                raise RuntimeError("nvcc failed building libovf_cuda.so")
+            if verbose and (r.stdout or r.stderr):
+                print(r.stdout + r.stderr)
+            os.replace(tmp, LIB)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
     return LIB
 
 
