@@ -15,9 +15,12 @@
 //   2. per-head maxima are agreed through distributed shared memory and each
 //      CTA exponentiates its slice;
 //   3. every CTA copies all heads' exponentials into its own shared memory
-//      (16-byte remote loads), then G lanes of warp 0 run the G sumExp chains
-//      while the other seven warps stage this CTA's value columns
-//      [d0, d0 + HD/16) of every position, transposed and widened to fp32;
+//      (bulk copies between the cluster's CTAs), then G lanes of warp 0 run
+//      the G sumExp chains; this CTA's value columns [d0, d0 + HD/16) of
+//      every position are staged transposed (fp32 cache: [d][t] read from the
+//      cache; fp16 cache: copied early as [t][d] in 16-position blocks, each
+//      block transposed in place, so the fp16 layout costs 32 bytes per
+//      position and two CTAs share an SM up to ~3.5K positions);
 //   4. after the probabilities p_t = e_t * invSum are formed, G * HD/16 lanes
 //      run the output chains with 16-byte loads of p and v, no barrier
 //      inside the chain.
@@ -55,11 +58,11 @@ struct GroupLayout {
 };
 
 // Shared memory (floats): qs [G][hd] | kn, vn [hd] | red [264] | exp table
-// [64] | sc [G][chunk] | eall [G][sp] | reg2: the key rows [chunk][hd] while
-// scoring, then vt [hd/16][sp] (fp32, or fp16 for an fp16 cache) | vraw
-// (fp16 cache only): the value columns [sp][hd/16] as cached.  About
-// 48 bytes per position for Llama-3-8B heads, so two CTAs fit an SM at a
-// 2K context and a 16-CTA cluster packs into a GPC.
+// [64] | sc [G][chunk] | eall [G][sp] | then, fp32 cache: the key rows
+// [chunk][hd] while scoring, then vt [hd/16][sp]; fp16 cache: the value
+// columns in 16-position blocks (keys are scored from L2).  For Llama-3-8B
+// heads the fp16 layout is ~32 bytes per position, so two CTAs fit an SM
+// (and a 16-CTA cluster packs into a GPC) up to ~3.5K positions.
 __host__ __device__ inline GroupLayout group_layout(int G, int hd, int seq_cap, int eb) {
     GroupLayout L;
     L.chunk_cap = (((seq_cap + kGrpCluster - 1) / kGrpCluster) + 3) & ~3;
@@ -68,13 +71,21 @@ __host__ __device__ inline GroupLayout group_layout(int G, int hd, int seq_cap, 
     // hit 32 distinct banks
     L.sp_cap = (((seq_cap + 3) & ~3) + 31) / 32 * 32 + 4;
     const int dpc = hd / kGrpCluster;
-    const int64_t kraw = ((int64_t)L.chunk_cap * hd * eb / 4 + 3) & ~int64_t(3);
-    const int64_t vt = (int64_t)dpc * L.sp_cap * eb / 4;
     L.o_sc = (int64_t)G * hd + 2 * hd + 264 + 64;
     L.o_eall = L.o_sc + (int64_t)G * L.chunk_cap;
     L.o_reg2 = L.o_eall + (int64_t)G * L.sp_cap;
-    L.o_vraw = L.o_reg2 + (kraw > vt ? kraw : vt);
-    L.floats = L.o_vraw + (eb == 2 ? (((int64_t)L.sp_cap * dpc * eb / 4 + 3) & ~int64_t(3)) : 0);
+    if (eb == 2) {
+        // fp16 cache: keys are scored straight from global memory (L2); the
+        // value columns land in 16-position blocks [t][dpc] and each block is
+        // transposed in place to [dpc][16] — 32 bytes per position in all
+        L.o_vraw = L.o_reg2;
+        L.floats = L.o_reg2 + (int64_t)((seq_cap + 15) / 16) * 16 * dpc * 2 / 4;
+    } else {
+        const int64_t kraw = ((int64_t)L.chunk_cap * hd * eb / 4 + 3) & ~int64_t(3);
+        const int64_t vt = (int64_t)dpc * L.sp_cap * eb / 4;
+        L.o_vraw = L.o_reg2 + (kraw > vt ? kraw : vt);
+        L.floats = L.o_vraw;
+    }
     return L;
 }
 
@@ -123,6 +134,9 @@ __device__ __forceinline__ void load_cols(const void *src, float *dst) {
     }
 }
 
+// Rotation of row d of an fp16 value block (see the transposition).
+__device__ __forceinline__ int vrot(int d) { return ((d >> 2) & 1) * 8; }
+
 // Async copy of n (4, 8 or a multiple of 16) bytes, 16 at a time.
 __device__ __forceinline__ void cp_async_n(char *dst, const char *src, int n) {
     if (n >= 16) {
@@ -157,7 +171,6 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
     float *eall = gsm + GL.o_eall; // [G][spc] all exponentials, then probabilities
     char *kraw = reinterpret_cast<char *>(gsm + GL.o_reg2);  // key rows [t0, t1) while scoring
     float *vt = gsm + GL.o_reg2;   // then: [DPC][spc] this CTA's value columns, transposed (fp32 cache)
-    __half *vt16 = reinterpret_cast<__half *>(gsm + GL.o_reg2);  // (fp16 cache: fp16)
     char *vraw = reinterpret_cast<char *>(gsm + GL.o_vraw);  // fp16 cache: [spc][DPC] value columns as cached
     const char *kbase = reinterpret_cast<const char *>(p.kc) + (size_t)g * p.max_ctx * HD * EB;
     const char *vbase = reinterpret_cast<const char *>(p.vc) + (size_t)g * p.max_ctx * HD * EB;
@@ -178,7 +191,7 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
     // the cached rows arrive by asynchronous copies while the prologue runs:
     // the CTA's key rows [t0, t1) (contiguous), then its value columns
     // [d0, d0 + DPC) of every earlier position
-    {
+    if (!F16) {
         const char *src = kbase + (size_t)t0 * HD * EB;
         const int n16 = own * HD * EB / 16;
         for (int i = tid; i < n16; i += NT) cp_async16(kraw + 16 * i, src + 16 * (size_t)i);
@@ -262,9 +275,9 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
 #pragma unroll
                 for (int i = 0; i < HD / 16; ++i) kv[u][i] = kn[16 * i + c];
             } else if (F16) {
-                const __half *kr = reinterpret_cast<const __half *>(kraw) + (size_t)(tt - t0) * HD;
+                const __half *kr = reinterpret_cast<const __half *>(kbase) + (size_t)tt * HD;
 #pragma unroll
-                for (int i = 0; i < HD / 16; ++i) kv[u][i] = __half2float(kr[16 * i + c]);
+                for (int i = 0; i < HD / 16; ++i) kv[u][i] = __half2float(__ldg(kr + 16 * i + c));
             } else {
                 const float *kr = reinterpret_cast<const float *>(kraw) + (size_t)(tt - t0) * HD;
 #pragma unroll
@@ -363,7 +376,50 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
     cp_async_wait<0>();
     __syncthreads();
     const int nq = (seq + 3) >> 2;
-    for (int q = tid; q < nq; q += NT) {
+    if (F16) {
+        // block b = positions [16b, 16b + 16): [16][DPC] halves as copied ->
+        // [DPC][16] in place, 16 lanes per block (lane j holds position j
+        // between the warp's read and its writes).  Row d is rotated by
+        // vrot(d) positions so that the output chains' 8-byte loads of rows
+        // d and d + 4 fall in different banks.
+        const int nblk = (seq + 15) >> 4, half = lane >> 4, j = lane & 15;
+        for (int b0 = 2 * warp; b0 < nblk; b0 += 2 * (NT / 32)) {
+            const int b = b0 + half, t = 16 * b + j;
+            __half *bh = reinterpret_cast<__half *>(vraw) + (size_t)b * 16 * DPC;
+            __half h[DPC];
+            if (b < nblk) {
+                if (has_new && t == pos) {
+#pragma unroll
+                    for (int d = 0; d < DPC; ++d) h[d] = __float2half_rn(vn[d0 + d]);
+                } else if (t < seq) {
+                    if (DPC == 8) {
+                        const uint4 u = *reinterpret_cast<const uint4 *>(bh + j * DPC);
+#pragma unroll
+                        for (int d = 0; d < DPC; ++d) h[d] = reinterpret_cast<const __half *>(&u)[d];
+                    } else if (DPC == 4) {
+                        const uint2 u = *reinterpret_cast<const uint2 *>(bh + j * DPC);
+#pragma unroll
+                        for (int d = 0; d < DPC; ++d) h[d] = reinterpret_cast<const __half *>(&u)[d];
+                    } else {
+#pragma unroll
+                        for (int d = 0; d < DPC; ++d) h[d] = bh[j * DPC + d];
+                    }
+                } else {
+#pragma unroll
+                    for (int d = 0; d < DPC; ++d) h[d] = __float2half_rn(0.0f);
+                }
+            }
+            __syncwarp();
+            if (b < nblk) {
+#pragma unroll
+                for (int d = 0; d < DPC; ++d) bh[d * 16 + ((j + vrot(d)) & 15)] = h[d];
+            }
+            __syncwarp();
+        }
+    }
+    // fp32 cache: this CTA's value columns from the cache, transposed to
+    // vt[d][t] over the dead key rows, four positions per thread
+    for (int q = tid; q < (F16 ? 0 : nq); q += NT) {
         float v[4][DPC];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -372,26 +428,15 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
 #pragma unroll
                 for (int d = 0; d < DPC; ++d) v[j][d] = vn[d0 + d];
             } else if (t < seq) {
-                if (F16) load_cols<DPC, true>(vraw + (size_t)t * DPC * EB, v[j]);
-                else load_cols<DPC, false>(vbase + ((size_t)t * HD + d0) * EB, v[j]);
+                load_cols<DPC, false>(vbase + ((size_t)t * HD + d0) * EB, v[j]);
             } else {
 #pragma unroll
                 for (int d = 0; d < DPC; ++d) v[j][d] = 0.0f;
             }
         }
 #pragma unroll
-        for (int d = 0; d < DPC; ++d) {
-            if (F16) {
-                // exact: every value came from an fp16
-                __half2 lo = __floats2half2_rn(v[0][d], v[1][d]), hi = __floats2half2_rn(v[2][d], v[3][d]);
-                uint2 u;
-                u.x = *reinterpret_cast<uint32_t *>(&lo);
-                u.y = *reinterpret_cast<uint32_t *>(&hi);
-                *reinterpret_cast<uint2 *>(vt16 + (size_t)d * spc + 4 * q) = u;
-            } else {
-                *reinterpret_cast<float4 *>(vt + d * spc + 4 * q) = make_float4(v[0][d], v[1][d], v[2][d], v[3][d]);
-            }
-        }
+        for (int d = 0; d < DPC; ++d)
+            *reinterpret_cast<float4 *>(vt + d * spc + 4 * q) = make_float4(v[0][d], v[1][d], v[2][d], v[3][d]);
     }
     mbar_wait_sleep_bounded(bar, 0);  // every slice's exponentials have landed
     __syncthreads();
@@ -456,7 +501,10 @@ __global__ void __launch_bounds__(kGrpThreads) attention_group_kernel(const Attn
             // four values of dimension d at positions t..t+3 (t a multiple of 4)
             auto v4 = [&](int t) -> float4 {
                 if (F16) {
-                    const uint2 u = *reinterpret_cast<const uint2 *>(vt16 + vrow + t);
+                    // blocked layout: block t/16, column d, positions t%16..
+                    const uint2 u = *reinterpret_cast<const uint2 *>(
+                        reinterpret_cast<const __half *>(vraw) + (size_t)(t >> 4) * (16 * DPC) + d * 16 +
+                        (((t & 15) + vrot(d)) & 15));
                     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
                     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
                     return make_float4(a.x, a.y, b.x, b.y);
