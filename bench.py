@@ -208,12 +208,30 @@ def run_reference(args):
 # ------------------------------------------------------------- GPU arm
 def _timed(torch, fn, reps: int) -> float:
     """Mean seconds per call of fn over `reps` calls, CUDA events on the
-    current stream, after 3 warm-up calls."""
+    launching stream, after 3 warm-up calls.  The calls are captured into a
+    CUDA graph and replayed, so the figure is device time per call, not the
+    Python/ctypes launch rate (a small GEMV finishes faster than the host can
+    issue the next call); if capture is refused the calls run eagerly."""
     for _ in range(3):
         fn(0)
     torch.cuda.synchronize()
-    st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            for i in range(reps):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+    except Exception:  # capture not possible: eager loop
+        torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
     e0.record(st)
     for i in range(reps):
         fn(i)
