@@ -264,7 +264,7 @@ def gemv_roofline(torch, eng_cfg, model_file, device, peaks) -> dict:
     del gates, ups
     return {"bound": "hbm", "kernel": "gemv_kernel (Q4_K gate+up pair, 2x14336x4096)", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-            "traffic_note": "DRAM bytes per launch from the ncu capture summarised in profiles/ (1.006x algorithmic)",
+            "traffic_note": "one ncu capture of `bench.py --profile-target gemv_gateup`: 66.78 MB DRAM read+write per launch (1.009x algorithmic)",
             "launch_us": dt * 1e6, "algorithmic_bytes": alg,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if "hbm_gbs" in peaks else "fallback 6650"}
 
