@@ -327,12 +327,15 @@ def prefill_gemm(torch, device) -> dict:
         sc = torch.empty(tc_scratch_bytes(M, K), dtype=torch.uint8, device=device)
         dt = _timed(torch, lambda i: Q4KDotKernel.project_batched_tensor_cores(x, M, q4[i % 4], None, y, aq, a4, ab,
                                                                                sc), reps)
+        d8t = _timed(torch, lambda i: Q8DotKernel.project_batched_tensor_cores(x, M, q8[i % 4], None, y, aq, a8, sc),
+                     reps)
         out[str(M)] = {"q4_k_us": d4 * 1e6, "q4_k_int_tops": 2 * M * N * K / d4 / 1e12,
                        "q4_k_tc_us": dt * 1e6, "q4_k_tc_tops": 2 * M * N * K / dt / 1e12,
-                       "q8_0_us": d8 * 1e6, "q8_0_int_tops": 2 * M * N * K / d8 / 1e12}
+                       "q8_0_us": d8 * 1e6, "q8_0_int_tops": 2 * M * N * K / d8 / 1e12,
+                       "q8_0_tc_us": d8t * 1e6, "q8_0_tc_tops": 2 * M * N * K / d8t / 1e12}
         del sc
-    return {"kernel": "batched_project_kernel (weight-stationary, dp4a); tc_q4k_project_kernel (tcgen05, fp16 "
-                      "exact-integer operands)", "n": N, "k": K, "rows": out}
+    return {"kernel": "batched_project_kernel (weight-stationary, dp4a); tc_q4k_project_kernel (tcgen05 kind::f16, "
+                      "exact-integer operands); tc_q80_project_kernel (tcgen05 kind::i8)", "n": N, "k": K, "rows": out}
 
 
 def qwen_config3(torch, device) -> dict:

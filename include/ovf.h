@@ -103,6 +103,16 @@ int64_t ovf_tc_scratch_bytes(int64_t rows, int64_t k);
 ovf_status ovf_kq_project_batched_tc(int32_t type, const float *x, int64_t rows, const void *w, int64_t n,
                                      int64_t k, const float *bias, float *y, int8_t *act_q, float *act_scales,
                                      int16_t *act_bsums, void *scratch, void *stream);
+/* Runtime/Q8DotKernel.cs:352 ProjectBatched on the tensor cores (tcgen05.mma
+ * kind::i8: every 32-element block dot is an exact int32 in TMEM, the
+ * reference's fp32 tail runs in the epilogue): the same outputs as
+ * ovf_q8_0_project_batched, bit for bit.  k a multiple of 64.  Scratch:
+ * x_q [rows*k], x_scales [rows*k/32] as for ovf_q8_0_project_batched plus
+ * `scratch` of ovf_tc_scratch_bytes(rows, k) bytes (16-byte aligned), which
+ * also covers ovf_kq_project_batched_tc when k is a multiple of 256. */
+ovf_status ovf_q8_0_project_batched_tc(const float *x, int64_t rows, const int8_t *wq, const float *wscales,
+                                       int64_t n, int64_t k, const float *bias, float *y, int8_t *x_q,
+                                       float *x_scales, void *scratch, void *stream);
 /* Runtime/Q8DotKernel.cs:252 ProjectParallel over a de-interleaved Q8Weight:
  * y[o] = bias[o] + sum_b (wscale*xscale)*int8dot, ascending b.  Scratch
  * x_q [k], x_scales [k/32].  k % 32 == 0. */

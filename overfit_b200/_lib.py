@@ -65,6 +65,7 @@ SIGNATURES = {
     "ovf_kq_project_batched_tc": (I32, [I32, P, I64, P, I64, I64, P, P, P, P, P, P, P]),
     "ovf_q8_0_project": (I32, [P, P, P, I64, I64, P, P, P, P, P]),
     "ovf_q8_0_project_batched": (I32, [P, I64, P, P, I64, I64, P, P, P, P, P]),
+    "ovf_q8_0_project_batched_tc": (I32, [P, I64, P, P, I64, I64, P, P, P, P, P, P]),
     "ovf_quantize_q4k": (I32, [P, I64, I64, P, P]),
     "ovf_quantize_q6k": (I32, [P, I64, I64, P, P]),
     "ovf_quantize_q8_0_gguf": (I32, [P, I64, P, P]),

@@ -157,8 +157,9 @@ ovf_status ovf_kq_project_batched(int32_t type, const float *x, int64_t rows, co
 }
 
 int64_t ovf_tc_scratch_bytes(int64_t rows, int64_t k) {
-    if (rows <= 0 || k <= 0 || k % 256) return 0;
-    return tc_scratch_bytes(rows, k);
+    if (rows <= 0 || k <= 0 || k % 64) return 0;
+    const int64_t q8 = tc8_scratch_bytes(rows, k);
+    return k % 256 ? q8 : std::max(q8, tc_scratch_bytes(rows, k));
 }
 
 ovf_status ovf_kq_project_batched_tc(int32_t type, const float *x, int64_t rows, const void *w, int64_t n, int64_t k,
@@ -213,6 +214,22 @@ ovf_status ovf_q8_0_project_batched(const float *x, int64_t rows, const int8_t *
     if (st) return st;
     return launch_batched_project(OVF_TYPE_Q8_0, wq, wscales, (size_t)n * (size_t)k, bias, x_q, x_scales, nullptr, y,
                                   n, k, rows, S(stream));
+}
+
+ovf_status ovf_q8_0_project_batched_tc(const float *x, int64_t rows, const int8_t *wq, const float *wscales,
+                                       int64_t n, int64_t k, const float *bias, float *y, int8_t *x_q,
+                                       float *x_scales, void *scratch, void *stream) {
+    OVF_CHECK_ARG(rows > 0 && rows <= (int64_t)65535 * 64, "Q8 ProjectBatched (tensor cores): rows must be in [1, 4194240]");
+    OVF_CHECK_ARG(n >= 0 && n <= 0x7FFFFFFF, "Q8 ProjectBatched (tensor cores): bad output size");
+    OVF_CHECK_ARG(k > 0 && k % 64 == 0, "Q8 ProjectBatched (tensor cores): inputSize %lld must be a multiple of 64",
+                  (long long)k);
+    OVF_CHECK_ARG(x && wq && wscales && y && x_q && x_scales && scratch, "Q8 ProjectBatched (tensor cores): null buffer");
+    OVF_CHECK_ARG(aligned16(x) && aligned16(wq) && aligned16(x_q) && aligned16(scratch),
+                  "Q8 ProjectBatched (tensor cores): buffers must be 16-byte aligned");
+    if (n == 0) return OVF_OK;
+    ovf_status st = launch_quantize_q8_0(x, rows * k, x_q, x_scales, S(stream));
+    if (st) return st;
+    return launch_tc8_project(wq, wscales, bias, x_q, x_scales, y, n, k, rows, 0, scratch, S(stream));
 }
 
 // --------------------------------------------------------------- codecs

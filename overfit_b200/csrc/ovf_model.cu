@@ -883,7 +883,7 @@ ovf_status prefill_alloc(ovf_session *s) {
     A((void **)&s->paq, R * KM);
     A((void **)&s->pas, R * KM / 32 * 4);
     A((void **)&s->pab, R * KM / 16 * 2);
-    A(&s->ptc, (size_t)tc_scratch_bytes((int64_t)R, (int64_t)KM));
+    A(&s->ptc, (size_t)std::max(tc_scratch_bytes((int64_t)R, (int64_t)KM), tc8_scratch_bytes((int64_t)R, (int64_t)KM)));
     A((void **)&s->ptok, (size_t)(s->max_ctx + 1) * 4);
     A((void **)&s->pscale, 16);
     if (!st && c.n_experts > 0) st = moe_rows_alloc(c, kPrefillRows, s->allocs, &s->pmoe);
@@ -903,10 +903,10 @@ struct ActRows {  // quantized activation rows (Q8_K or Q8_0) of a batch
     void *tc = nullptr;  // tensor-core operand scratch (tc_scratch_bytes of the rows), or none
 };
 
-// From this many rows on, Q4_K projections run on the tensor cores
-// (tc_q4k_project_kernel); fewer rows stay on the dp4a weight-stationary
-// kernel, which streams the weights once with no operand expansion.  Both are
-// bit-identical to the reference's per-row dot.
+// From this many rows on, Q4_K and Q8_0 projections run on the tensor cores
+// (tc_q4k_project_kernel, tc_q80_project_kernel); fewer rows stay on the dp4a
+// weight-stationary kernel, which streams the weights once with no operand
+// expansion.  All are bit-identical to the reference's per-row dot.
 constexpr int kTcMinRows = 32;
 
 ovf_status quantize_rows_for(const ActRows &ar, const DevWeight &w, const float *x, int rows, int64_t k, int *fam,
@@ -922,6 +922,9 @@ ovf_status project_rows(const ActRows &ar, const DevWeight &w, const float *bias
                         int group = 0, const float *resid = nullptr) {
     if (ar.tc && group == 0 && rows >= kTcMinRows && tc_project_supported(w.type, w.rows, w.cols, rows))
         return launch_tc_project(w.type, w.data, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols, rows, ar.tc, st, resid);
+    if (ar.tc && w.type == OVF_TYPE_Q8_0 && rows >= kTcMinRows && tc8_project_supported(w.rows, w.cols, rows, group))
+        return launch_tc8_project(reinterpret_cast<const int8_t *>(w.data), w.scales, bias, ar.aq, ar.as, y, w.rows, w.cols,
+                                  rows, group, ar.tc, st, resid);
     const size_t qbytes = w.type == OVF_TYPE_Q8_0 ? (size_t)w.rows * w.cols : (size_t)tensor_bytes(w.type, w.rows, w.cols);
     return launch_batched_project(w.type, w.data, w.scales, qbytes, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols,
                                   rows, st, group, resid);

@@ -549,6 +549,36 @@ bool tc_project_supported(int type, int64_t n, int64_t k, int64_t rows) {
     return type == OVF_TYPE_Q4_K && k % 256 == 0 && k >= 256 && n >= 1 && rows >= 1 && n <= 0x7FFFFFFF;
 }
 
+// A 2-D tiled tensor map over a byte matrix [rows][inner] (row stride in
+// bytes, a multiple of 16), box `box_rows` x `box_inner` bytes (box_inner a
+// multiple of 16, at most 256), no swizzle, zero fill past the edges.
+static ovf_status encode_bytes_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows,
+                                  uint64_t row_stride, uint32_t box_inner, uint32_t box_rows) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+            set_error("tensor map: cuTensorMapEncodeTiled unavailable");
+            return OVF_ECUDA;
+        }
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)row_stride};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), gdim, gstride, box,
+                               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) {
+        set_error("tensor map encode failed (CUresult %d)", (int)cr);
+        return OVF_EINVAL;
+    }
+    return OVF_OK;
+}
+
 // y [rows x n] (+ bias, + resid) from the Q8_K rows (aq, as, ab) and Q4_K
 // weights; scratch holds tc_scratch_bytes(rows, k).
 ovf_status launch_tc_project(int type, const void *w, const float *bias, const int8_t *aq, const float *as,
@@ -574,30 +604,10 @@ ovf_status launch_tc_project(int type, const void *w, const float *bias, const i
         attr_once.mark(dev);
     }
     // the weight matrix as a 2-D byte tensor [n][nb * 144], box 128 x 144
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
-        cudaDriverEntryPointQueryResult q;
-        void *fn = nullptr;
-        e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
-        {
-            set_error("tensor-core projection: cuTensorMapEncodeTiled unavailable");
-            return OVF_ECUDA;
-        }
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
     CUtensorMap wmap;
-    const cuuint64_t gdim[2] = {(cuuint64_t)(nb * 144), (cuuint64_t)n};
-    const cuuint64_t gstride[1] = {(cuuint64_t)(nb * 144)};
-    const cuuint32_t box[2] = {144, (cuuint32_t)kTcRows};
-    const cuuint32_t estride[2] = {1, 1};
-    const CUresult cr = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), gdim, gstride, box,
-                               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) {
-        set_error("tensor-core projection: weight tensor map (CUresult %d)", (int)cr);
-        return OVF_EINVAL;
-    }
+    if (ovf_status r = encode_bytes_2d(&wmap, w, (uint64_t)nb * 144, (uint64_t)n, (uint64_t)nb * 144, 144,
+                                       (uint32_t)kTcRows))
+        return r;
     TcParams p{};
     p.w = static_cast<const uint8_t *>(w);
     p.x16 = x16;

@@ -288,6 +288,25 @@ class Q8DotKernel:
                                                    _ptr(bias), _ptr(output), _ptr(input_quants), _ptr(input_scales),
                                                    _stream()), "Q8 ProjectBatched")
 
+    @staticmethod
+    def project_batched_tensor_cores(input, rows, weight: Q8Weight, bias, output, input_quants, input_scales,
+                                     scratch) -> None:
+        """ProjectBatched (Runtime/Q8DotKernel.cs:352-445) on the tensor cores:
+        the same outputs as project_batched, bit for bit; K a multiple of 64,
+        `scratch` uint8 of tc_scratch_bytes(rows, K)."""
+        k, n = weight.input_size, weight.output_size
+        if rows <= 0:
+            raise ValueError("rows must be positive")
+        _need(input, torch.float32, rows * k, "input")
+        _need(output, torch.float32, rows * n, "output")
+        _need(input_quants, torch.int8, rows * k, "inputQuants")
+        _need(input_scales, torch.float32, rows * k // 32, "inputScales")
+        _need(scratch, torch.uint8, tc_scratch_bytes(rows, k), "scratch")
+        check(_lib.load().ovf_q8_0_project_batched_tc(_ptr(input), rows, _ptr(weight.quants), _ptr(weight.scales), n,
+                                                      k, _ptr(bias), _ptr(output), _ptr(input_quants),
+                                                      _ptr(input_scales), _ptr(scratch), _stream()),
+              "Q8 ProjectBatched (tensor cores)")
+
 
 class GgmlQuant:
     """Loading/GgmlQuant.cs plus the Q6_K / Q8_0 encoders the reference lacks."""

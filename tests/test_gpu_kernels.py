@@ -494,3 +494,50 @@ def test_tensor_core_projection_extreme_magnitudes(K, orc):
         outs.append(host(y))
         assert int(np.abs(host(q)).min()) == 127
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("rows,n,k,with_bias", [(1, 80, 384, True), (40, 4864, 896, False), (130, 896, 4864, True),
+                                                (257, 300, 1024, False)])
+def test_q8_tensor_core_projection_bit_exact(K, orc, rows, n, k, with_bias):
+    """Q8DotKernel.ProjectBatched on tcgen05 (kind::i8): ragged weight-row and
+    token tiles, Qwen2-0.5B shapes, bit-exact to the restatement."""
+    rng = np.random.default_rng(rows * 3 + n + k)
+    w = rng.normal(0, 0.02, (n, k)).astype(np.float32)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    x[0, :64] = 0.0
+    bias = rng.normal(0, 0.1, n).astype(np.float32) if with_bias else None
+    g = orc.quantize_q8_0_gguf(w)
+    rq, rs = orc.q8_0_deinterleave(g, n * k)
+    ref = orc.q8_0_project_batched(x, rq, rs, n, k, bias)
+    w8 = K.Q8Weight.from_gguf(dev(g), k, n)
+    y = torch.empty(rows * n, device="cuda")
+    xq, xs = torch.empty(rows * k, dtype=torch.int8, device="cuda"), torch.empty(rows * k // 32, device="cuda")
+    scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+    K.Q8DotKernel.project_batched_tensor_cores(dev(x), rows, w8, None if bias is None else dev(bias), y, xq, xs,
+                                               scratch)
+    np.testing.assert_array_equal(host(y).reshape(rows, n), ref)
+
+
+def test_q8_tensor_core_projection_large_and_extreme(K):
+    """The 8B gate shape against the dp4a kernel, and weights and activations
+    at +-127 (the largest block dots) exact in the int32 accumulators."""
+    n, k, rows = 14336, 4096, 200
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w8 = K.Q8Weight.from_gguf(K.GgmlQuant.quantize_q8_0(torch.randn(n, k, device="cuda", generator=g) * 0.02), k, n)
+    x = torch.randn(rows * k, device="cuda", generator=g)
+    for extreme in (False, True):
+        if extreme:
+            w8.quants.copy_(torch.where(torch.arange(n * k, device="cuda").reshape(n, k) % 3 == 0, -127, 127)
+                            .to(torch.int8).reshape(w8.quants.shape))
+            x = torch.where(torch.arange(rows * k, device="cuda") % 5 == 0, -1.0, 1.0)
+        outs = []
+        for tc in (True, False):
+            y = torch.empty(rows * n, device="cuda")
+            xq, xs = torch.empty(rows * k, dtype=torch.int8, device="cuda"), torch.empty(rows * k // 32, device="cuda")
+            if tc:
+                scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+                K.Q8DotKernel.project_batched_tensor_cores(x, rows, w8, None, y, xq, xs, scratch)
+            else:
+                K.Q8DotKernel.project_batched(x, rows, w8, None, y, xq, xs)
+            outs.append(host(y))
+        np.testing.assert_array_equal(outs[0], outs[1])
