@@ -167,12 +167,15 @@ ovf_status ovf_kq_project_batched_tc(int32_t type, const float *x, int64_t rows,
                                      int16_t *act_bsums, void *scratch, void *stream) {
     ovf_status st = check_kq(type, w, n, k);
     if (st) return st;
-    OVF_CHECK_ARG(type == OVF_TYPE_Q4_K, "ProjectBatched (tensor cores): Q4_K weights only");
+    OVF_CHECK_ARG(type == OVF_TYPE_Q4_K || (type == OVF_TYPE_Q6_K && k % 2048 == 0),
+                  "ProjectBatched (tensor cores): Q4_K weights, or Q6_K with inputSize a multiple of 2048");
     OVF_CHECK_ARG(rows > 0 && rows <= (int64_t)65535 * 128, "ProjectBatched (tensor cores): rows must be in [1, 8388480]");
     OVF_CHECK_ARG(x && y && act_q && act_scales && act_bsums && scratch, "ProjectBatched (tensor cores): null buffer");
     if (n == 0) return OVF_OK;
     st = launch_quantize_q8k(x, rows * k, act_q, act_scales, act_bsums, S(stream));
     if (st) return st;
+    if (type == OVF_TYPE_Q6_K)
+        return launch_tc6_project(w, bias, act_q, act_scales, act_bsums, y, n, k, rows, scratch, S(stream));
     return launch_tc_project(type, w, bias, act_q, act_scales, act_bsums, y, n, k, rows, scratch, S(stream));
 }
 

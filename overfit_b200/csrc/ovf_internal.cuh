@@ -95,6 +95,11 @@ ovf_status launch_attention_group(const AttnParams &p, int seq_cap, cudaStream_t
 // ovf_tc.cu: Q4_K prefill projection on tcgen05 tensor cores (bit-identical).
 int64_t tc_scratch_bytes(int64_t rows, int64_t k);
 bool tc_project_supported(int type, int64_t n, int64_t k, int64_t rows);
+// ovf_tc6.cu: the Q6_K projection of M rows on tcgen05 (k a multiple of 2048).
+bool tc6_project_supported(int64_t n, int64_t k, int64_t rows);
+ovf_status launch_tc6_project(const void *w, const float *bias, const int8_t *aq, const float *as, const int16_t *ab,
+                              float *y, int64_t n, int64_t k, int64_t rows, void *scratch, cudaStream_t st,
+                              const float *resid = nullptr);
 // ovf_tc8.cu: the Q8_0 projection of M rows on tcgen05 (kind::i8).
 bool tc8_project_supported(int64_t n, int64_t k, int64_t rows, int group);
 int64_t tc8_scratch_bytes(int64_t rows, int64_t k);

@@ -7,6 +7,7 @@
 #include "ovf_batched.cu"
 #include "ovf_tc.cu"
 #include "ovf_tc8.cu"
+#include "ovf_tc6.cu"
 #include "ovf_ops.cu"
 #include "ovf_moe.cu"
 #include "ovf_tp.cu"

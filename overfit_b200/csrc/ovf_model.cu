@@ -903,8 +903,8 @@ struct ActRows {  // quantized activation rows (Q8_K or Q8_0) of a batch
     void *tc = nullptr;  // tensor-core operand scratch (tc_scratch_bytes of the rows), or none
 };
 
-// From this many rows on, Q4_K and Q8_0 projections run on the tensor cores
-// (tc_q4k_project_kernel, tc_q80_project_kernel); fewer rows stay on the dp4a
+// From this many rows on, Q4_K, Q6_K and Q8_0 projections run on the tensor
+// cores (tc_q4k_project_kernel, tc_q6k_project_kernel, tc_q80_project_kernel); fewer rows stay on the dp4a
 // weight-stationary kernel, which streams the weights once with no operand
 // expansion.  All are bit-identical to the reference's per-row dot.
 constexpr int kTcMinRows = 32;
@@ -922,6 +922,8 @@ ovf_status project_rows(const ActRows &ar, const DevWeight &w, const float *bias
                         int group = 0, const float *resid = nullptr) {
     if (ar.tc && group == 0 && rows >= kTcMinRows && tc_project_supported(w.type, w.rows, w.cols, rows))
         return launch_tc_project(w.type, w.data, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols, rows, ar.tc, st, resid);
+    if (ar.tc && w.type == OVF_TYPE_Q6_K && group == 0 && rows >= kTcMinRows && tc6_project_supported(w.rows, w.cols, rows))
+        return launch_tc6_project(w.data, bias, ar.aq, ar.as, ar.ab, y, w.rows, w.cols, rows, ar.tc, st, resid);
     if (ar.tc && w.type == OVF_TYPE_Q8_0 && rows >= kTcMinRows && tc8_project_supported(w.rows, w.cols, rows, group))
         return launch_tc8_project(reinterpret_cast<const int8_t *>(w.data), w.scales, bias, ar.aq, ar.as, y, w.rows, w.cols,
                                   rows, group, ar.tc, st, resid);

@@ -549,6 +549,23 @@ bool tc_project_supported(int type, int64_t n, int64_t k, int64_t rows) {
     return type == OVF_TYPE_Q4_K && k % 256 == 0 && k >= 256 && n >= 1 && rows >= 1 && n <= 0x7FFFFFFF;
 }
 
+// The packed operands of a batch of Q8_K rows in `scratch`
+// (tc_scratch_bytes(rows, k)): fp16 activation tiles, bsum16 tiles and token
+// scales (tc_pack_kernel); the tiles' and scales' addresses are returned.
+static ovf_status launch_tc_pack(const int8_t *aq, const float *as, const int16_t *ab, int64_t rows, int64_t k,
+                                 void *scratch, cudaStream_t st, const __half **x16_out, const float **xs_out) {
+    const int64_t mtiles = tc_mtiles(rows), nb = k / 256;
+    uint8_t *base = static_cast<uint8_t *>(scratch);
+    __half *x16 = reinterpret_cast<__half *>(base);
+    __half *bs16 = reinterpret_cast<__half *>(base + mtiles * kTcToks * k * 2);
+    float *xs = reinterpret_cast<float *>(base + mtiles * kTcToks * k * 2 + mtiles * nb * kTcBBs);
+    tc_pack_kernel<<<dim3((unsigned)(k / kTcKc), (unsigned)mtiles), 256, 0, st>>>(aq, as, ab, (int)rows, (int)k, x16,
+                                                                                  bs16, xs);
+    if (x16_out) *x16_out = x16;
+    if (xs_out) *xs_out = xs;
+    return cuda_status(cudaGetLastError(), "tc_pack");
+}
+
 // A 2-D tiled tensor map over a byte matrix [rows][inner] (row stride in
 // bytes, a multiple of 16), box `box_rows` x `box_inner` bytes (box_inner a
 // multiple of 16, at most 256), no swizzle, zero fill past the edges.
@@ -592,10 +609,8 @@ ovf_status launch_tc_project(int type, const void *w, const float *bias, const i
     __half *x16 = reinterpret_cast<__half *>(base);
     __half *bs16 = reinterpret_cast<__half *>(base + mtiles * kTcToks * k * 2);
     float *xs = reinterpret_cast<float *>(base + mtiles * kTcToks * k * 2 + mtiles * nb * kTcBBs);
-    tc_pack_kernel<<<dim3((unsigned)(k / kTcKc), (unsigned)mtiles), 256, 0, st>>>(aq, as, ab, (int)rows, (int)k, x16,
-                                                                                  bs16, xs);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "tc_pack");
+    if (ovf_status r = launch_tc_pack(aq, as, ab, rows, k, scratch, st, nullptr, nullptr)) return r;
+    cudaError_t e = cudaSuccess;
     static PerDeviceOnce attr_once;
     const int dev = current_device();
     if (attr_once.pending(dev)) {

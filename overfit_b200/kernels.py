@@ -218,7 +218,7 @@ class Q4KDotKernel(_KQuantKernel):
               "ProjectGateUpParallel")
 
 
-def _q4k_tc(input, rows, weight, bias, output, activation_quants, activation_scales, activation_bsums, scratch):
+def _kq_tc(type_, input, rows, weight, bias, output, activation_quants, activation_scales, activation_bsums, scratch):
     k, n = weight.input_size, weight.output_size
     _need(input, torch.float32, rows * k, "input")
     _need(output, torch.float32, rows * n, "output")
@@ -226,7 +226,7 @@ def _q4k_tc(input, rows, weight, bias, output, activation_quants, activation_sca
     _need(activation_scales, torch.float32, rows * k // 256, "activationScales")
     _need(activation_bsums, torch.int16, rows * k // 16, "activationBsums")
     _need(scratch, torch.uint8, tc_scratch_bytes(rows, k), "scratch")
-    check(_lib.load().ovf_kq_project_batched_tc(TYPE_Q4_K, _ptr(input), rows, _ptr(weight.blocks), n, k, _ptr(bias),
+    check(_lib.load().ovf_kq_project_batched_tc(type_, _ptr(input), rows, _ptr(weight.blocks), n, k, _ptr(bias),
                                                 _ptr(output), _ptr(activation_quants), _ptr(activation_scales),
                                                 _ptr(activation_bsums), _ptr(scratch), _stream()),
           "ProjectBatched (tensor cores)")
@@ -237,11 +237,23 @@ def tc_scratch_bytes(rows: int, k: int) -> int:
     return int(_lib.load().ovf_tc_scratch_bytes(rows, k))
 
 
+def _q4k_tc(*args):
+    _kq_tc(TYPE_Q4_K, *args)
+
+
+def _q6k_tc(*args):
+    _kq_tc(TYPE_Q6_K, *args)
+
+
 Q4KDotKernel.project_batched_tensor_cores = staticmethod(_q4k_tc)
 
 
 class Q6KDotKernel(_KQuantKernel):
     TYPE = TYPE_Q6_K
+
+
+# ProjectBatched on the tensor cores (K a multiple of 2048); bit-identical to project_batched
+Q6KDotKernel.project_batched_tensor_cores = staticmethod(_q6k_tc)
 
 
 class Q8DotKernel:

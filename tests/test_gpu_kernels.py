@@ -541,3 +541,60 @@ def test_q8_tensor_core_projection_large_and_extreme(K):
                 K.Q8DotKernel.project_batched(x, rows, w8, None, y, xq, xs)
             outs.append(host(y))
         np.testing.assert_array_equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("rows,n,k,with_bias", [(1, 96, 2048, True), (130, 300, 4096, False), (33, 1024, 4096, True),
+                                                (200, 4096, 14336, False)])
+def test_q6k_tensor_core_projection_bit_exact(K, orc, rows, n, k, with_bias):
+    """Q6KDotKernel.ProjectBatched on tcgen05 (split 8-bit scales): ragged
+    weight-row and token tiles, the 8B attn_v / ffn_down shapes."""
+    rng = np.random.default_rng(rows + 2 * n + k)
+    wf = orc.fill_normal(n * k, rows + 11, 0.0, 0.02).reshape(n, k)
+    w = orc.quantize_q6k(wf)
+    x = rng.normal(0, 1, (rows, k)).astype(np.float32)
+    x[0, :256] = 0.0
+    bias = rng.uniform(-1, 1, n).astype(np.float32) if with_bias else None
+    y = torch.empty(rows * n, device="cuda")
+    q = torch.empty(rows * k, dtype=torch.int8, device="cuda")
+    s = torch.empty(rows * k // 256, device="cuda")
+    b = torch.empty(rows * k // 16, dtype=torch.int16, device="cuda")
+    scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+    wt = K.Q6KWeight(dev(w), k, n)
+    bd = None if bias is None else dev(bias)
+    K.Q6KDotKernel.project_batched_tensor_cores(dev(x), rows, wt, bd, y, q, s, b, scratch)
+    if rows * n * k <= 1 << 30:
+        ref = orc.kq_project_batched(orc.Q6_K, x, w, n, k, bias)
+    else:  # against the dp4a kernel (itself bit-exact to the restatement)
+        y2 = torch.empty(rows * n, device="cuda")
+        K.Q6KDotKernel.project_batched(dev(x), rows, wt, bd, y2, q, s, b)
+        ref = host(y2).reshape(rows, n)
+    np.testing.assert_array_equal(host(y).reshape(rows, n), ref)
+
+
+def test_q6k_tensor_core_projection_extreme_magnitudes(K):
+    """6-bit values 0 and 63 under scales -128 and 127 against activations of
+    +-127: the largest sub-block products stay exact in both accumulators."""
+    n, k, rows = 256, 2048, 96
+    blk = np.zeros((n, k // 256, 210), np.uint8)
+    blk[: n // 2, :, :192] = 0x00            # q = 0
+    blk[n // 2:, :, :192] = 0xFF             # q = 63
+    blk[:, :, 192:208:2] = np.uint8(0x80)    # scale -128
+    blk[:, :, 193:208:2] = np.uint8(0x7F)    # scale 127
+    blk[:, :, 208:210] = np.frombuffer(np.float16(0.01).tobytes(), np.uint8)
+    w = blk.reshape(-1)
+    x = np.ones((rows, k), np.float32)
+    x[rows // 3:] = -1.0
+    outs = []
+    for tc in (True, False):
+        y = torch.empty(rows * n, device="cuda")
+        q = torch.empty(rows * k, dtype=torch.int8, device="cuda")
+        s = torch.empty(rows * k // 256, device="cuda")
+        b = torch.empty(rows * k // 16, dtype=torch.int16, device="cuda")
+        wt = K.Q6KWeight(dev(w), k, n)
+        if tc:
+            scratch = torch.empty(K.tc_scratch_bytes(rows, k), dtype=torch.uint8, device="cuda")
+            K.Q6KDotKernel.project_batched_tensor_cores(dev(x), rows, wt, None, y, q, s, b, scratch)
+        else:
+            K.Q6KDotKernel.project_batched(dev(x), rows, wt, None, y, q, s, b)
+        outs.append(host(y))
+    np.testing.assert_array_equal(outs[0], outs[1])
