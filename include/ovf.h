@@ -95,7 +95,8 @@ ovf_status ovf_kq_project_batched(int32_t type, const float *x, int64_t rows, co
  * cores (tcgen05.mma, fp32 accumulators in TMEM): the same outputs as
  * ovf_kq_project_batched, bit for bit (the integer parts of every
  * super-block dot are exact in the fp32 accumulators; the reference's fp32
- * tail runs in the epilogue).  Q4_K weights only.  Scratch: the activation
+ * tail runs in the epilogue).  Q4_K weights, or Q6_K (Q6KDotKernel.cs:403
+ * ProjectBatched) with k a multiple of 2048.  Scratch: the activation
  * quantization as for ovf_kq_project_batched plus `scratch` of
  * ovf_tc_scratch_bytes(rows, k) bytes (16-byte aligned) for the packed
  * operand tiles. */
