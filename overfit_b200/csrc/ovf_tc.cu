@@ -23,24 +23,26 @@
 // activation tiles are packed in the same K order, so the products pair up.
 //
 // Layout.  A CTA owns 128 weight rows x 64 tokens; per super-block four
-// K-chunks of 64 flow through a 4-deep ring of fp16 operand tiles in the
-// UMMA no-swizzle K-major layout (8x16-byte core matrices; K-adjacent core
+// K-chunks of 64 flow through rings of fp16 operand tiles in the UMMA
+// no-swizzle K-major layout (8x16-byte core matrices; K-adjacent core
 // matrices 128 B apart, 8-row groups 1024 B apart).  Warp roles, linked by
 // mbarriers:
-//   warp 0      producer: 1-D bulk copies of the raw Q4_K blocks (128 rows of
-//               144 B per super-block), the packed activation chunks, the
-//               bsum16 tile and the tokens' scales;
-//   warp 1      TMEM allocation and the single MMA-issuing thread: per chunk
-//               four MMAs (M=128, N=64, K=16) into the chunk's K-half
-//               accumulator, plus the minAcc MMA with chunk 0; two
-//               accumulator sets (super-block parity); tcgen05.commit
-//               releases operand stages and publishes accumulators;
-//   warps 2-5   converters: thread = weight row;
-//   warps 6-13  epilogue: warp w reads TMEM lanes 32*(w%4).., 32 tokens,
-//               keeps the running per-(row, token) sums in TMEM.
-// The operands live in this GPU's shared memory only; no cluster, no
-// multicast.  Every mbarrier wait is bounded (the device error word is set
-// and the kernel drains instead of hanging).
+//   warp 0      producer: a 2-D tensor copy of the 128 rows' 144-byte blocks
+//               per super-block, the packed activation chunks, the bsum16
+//               tile and the tokens' scales;
+//   warp 1      TMEM allocation (256 columns) and the single MMA-issuing
+//               thread: per chunk four MMAs (M=128, N=64, K=16) into the
+//               chunk's K-half accumulator, plus the minAcc MMA with chunk 0;
+//               tcgen05.commit releases operand stages and publishes the
+//               accumulator set;
+//   warps 2-5   converters: thread = weight row; they also hand d / dmin and
+//               the token scales to the epilogue through a small ring;
+//   warps 6-9   epilogue: warp w reads TMEM lanes 32*(w%4).., all 64 tokens,
+//               and keeps the running per-(row, token) sums in TMEM.
+// Two CTAs per SM overlap each other's pipeline hand-offs.  The operands live
+// in this GPU's shared memory only; no cluster, no multicast.  Every mbarrier
+// wait is bounded (the device error word is set and the kernel drains
+// instead of hanging).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -571,16 +573,17 @@ static ovf_status launch_tc_pack(const int8_t *aq, const float *as, const int16_
 // multiple of 16, at most 256), no swizzle, zero fill past the edges.
 static ovf_status encode_bytes_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows,
                                   uint64_t row_stride, uint32_t box_inner, uint32_t box_rows) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
+    // resolved once, thread-safely (function-local static initialisation)
+    static const PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
         cudaDriverEntryPointQueryResult q;
         void *fn = nullptr;
         const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
-            set_error("tensor map: cuTensorMapEncodeTiled unavailable");
-            return OVF_ECUDA;
-        }
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        return e == cudaSuccess && q == cudaDriverEntryPointSuccess ? reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn)
+                                                                    : nullptr;
+    }();
+    if (!encode) {
+        set_error("tensor map: cuTensorMapEncodeTiled unavailable");
+        return OVF_ECUDA;
     }
     const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
     const cuuint64_t gstride[1] = {(cuuint64_t)row_stride};
@@ -606,10 +609,10 @@ ovf_status launch_tc_project(int type, const void *w, const float *bias, const i
     const int64_t mtiles = tc_mtiles(rows), ntiles = (n + kTcRows - 1) / kTcRows, nb = k / 256;
     OVF_CHECK_ARG(mtiles <= 65535, "tensor-core projection: too many rows");
     uint8_t *base = static_cast<uint8_t *>(scratch);
-    __half *x16 = reinterpret_cast<__half *>(base);
-    __half *bs16 = reinterpret_cast<__half *>(base + mtiles * kTcToks * k * 2);
-    float *xs = reinterpret_cast<float *>(base + mtiles * kTcToks * k * 2 + mtiles * nb * kTcBBs);
-    if (ovf_status r = launch_tc_pack(aq, as, ab, rows, k, scratch, st, nullptr, nullptr)) return r;
+    const __half *bs16 = reinterpret_cast<const __half *>(base + mtiles * kTcToks * k * 2);
+    const __half *x16 = nullptr;
+    const float *xs = nullptr;
+    if (ovf_status r = launch_tc_pack(aq, as, ab, rows, k, scratch, st, &x16, &xs)) return r;
     cudaError_t e = cudaSuccess;
     static PerDeviceOnce attr_once;
     const int dev = current_device();
