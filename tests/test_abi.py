@@ -90,3 +90,29 @@ def test_python_mirror_raises_value_error():
         _lib.check(_lib.OVF_EINVAL, "x")
     with pytest.raises(_lib.OverfitRuntimeError):
         _lib.check(_lib.OVF_ESTATE, "x")
+
+
+def test_tensor_core_projection_host_checks():
+    """Scratch sizes and argument checks of the tensor-core projections run on
+    the host (no device work): one scratch size covers Q4_K, Q6_K and Q8_0,
+    unsupported shapes and types are rejected before any launch."""
+    from overfit_b200 import _lib
+    lib = _lib.load()
+    for rows in (1, 63, 64, 65, 2048):
+        for k in (4096, 14336):
+            mt = -(-rows // 64)
+            got = lib.ovf_tc_scratch_bytes(rows, k)
+            assert got >= mt * 64 * k * 2 + mt * (k // 256) * (2048 + 256)  # fp16 tiles, bsum16 tiles, scales
+            assert got >= mt * 64 * k + mt * (k // 32) * 64 * 4             # int8 tiles, block scales
+    assert lib.ovf_tc_scratch_bytes(16, 896) > 0       # Q8_0 widths (multiples of 64)
+    assert lib.ovf_tc_scratch_bytes(16, 100) == 0
+    assert lib.ovf_tc_scratch_bytes(0, 4096) == 0
+    p16 = C.c_void_p(16)
+    # Q8_0 as a K-quant, Q6_K with k not a multiple of 2048, rows out of range, null scratch
+    assert lib.ovf_kq_project_batched_tc(8, p16, 4, p16, 4, 4096, None, p16, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project_batched_tc(14, p16, 4, p16, 4, 1024, None, p16, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project_batched_tc(12, p16, 0, p16, 4, 4096, None, p16, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_kq_project_batched_tc(12, p16, 4, p16, 4, 4096, None, p16, p16, p16, p16, None, None) == _lib.OVF_EINVAL
+    assert lib.ovf_q8_0_project_batched_tc(p16, 4, p16, p16, 4, 96, None, p16, p16, p16, p16, None) == _lib.OVF_EINVAL
+    assert lib.ovf_q8_0_project_batched_tc(p16, 4, C.c_void_p(8), p16, 4, 128, None, p16, p16, p16, p16,
+                                           None) == _lib.OVF_EINVAL
